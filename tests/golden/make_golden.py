@@ -1,0 +1,219 @@
+"""Generate the golden vectors under tests/golden/ from the REFERENCE itself.
+
+Runs the sentinelXVI/KeSSie Python reference functions (kessie_hip_kernels.py:
+kessie_build_fog_weights, kessie_windowed_attention_ref,
+kessie_fused_fog_attention_ref, _rope_remap_ref, KeSSiePagedKVCache) on
+seeded numpy inputs and stores their outputs.  Inputs are not stored when
+they can be regenerated from the recorded seed (numpy PCG64 standard_normal
+is stable across numpy versions); the oracle tests regenerate them.
+
+Needs the reference source tree (default /root/reference, or $KESSIE_REF);
+it is run once in the build container and its outputs are committed.  Nothing
+on the GPU box runs this script.
+
+    python tests/golden/make_golden.py
+"""
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("KESSIE_REF", "/root/reference")
+sys.dont_write_bytecode = True
+sys.path.insert(0, REF)
+
+import torch  # noqa: E402
+
+import kessie_hip_kernels as R  # noqa: E402
+
+R.HAS_TRITON = False   # the Triton branches need a GPU driver; the refs are torch-only
+torch.set_num_threads(os.cpu_count() or 1)
+
+
+def rnd(seed, shape):
+    return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)
+
+
+def to_bf16_vals(x):
+    return torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+
+
+def save(name, **arrs):
+    np.savez_compressed(os.path.join(HERE, name), **arrs)
+    print("wrote", name, {k: getattr(v, "shape", v) for k, v in arrs.items()})
+
+
+def gen_fog():
+    cases = [(4096, 0.5, 512 / 4096), (4096, 0.5, 0.5), (1000, 0.7, 0.3), (17, 1.5, 0.9),
+             (512, 0.0, 0.5), (64, 0.5, 1.0), (64, 0.5, 0.0),
+             (131072, 0.5, 4096 / 131072), (1048576, 0.5, 8192 / 1048576), (262144, 0.5, 4096 / 262144)]
+    out = {}
+    for i, (n, a, fs) in enumerate(cases):
+        w = R.kessie_build_fog_weights(n, a, fs).numpy()
+        idx = np.arange(n) if n <= 4096 else np.unique(np.concatenate(
+            [np.arange(64), np.arange(n - 64, n), np.random.default_rng(i).integers(0, n, 4096)]))
+        out[f"case{i}_params"] = np.array([n, a, fs], dtype=np.float64)
+        out[f"case{i}_idx"] = idx.astype(np.int64)
+        out[f"case{i}_w"] = w[idx]
+        out[f"case{i}_clear_start"] = np.array(int(n * (1.0 - fs)))
+    out["ncases"] = np.array(len(cases))
+    save("fog_weights.npz", **out)
+
+
+def gen_rope():
+    out = {}
+    for theta in (10000.0, 500000.0):
+        for half in (32, 64):
+            f = 1.0 / (theta ** (torch.arange(half, dtype=torch.float32) / half))
+            out[f"freqs_{int(theta)}_{half}"] = f.numpy()
+    cases = [
+        # seed, T, H, D, dtype, theta, position mode
+        (11, 64, 2, 128, "float32", 10000.0, "small"),
+        (12, 64, 2, 128, "bfloat16", 500000.0, "recall"),
+        (13, 48, 3, 64, "float16", 10000.0, "small"),
+        (14, 32, 2, 128, "bfloat16", 10000.0, "neg"),
+        (15, 16, 8, 128, "float16", 500000.0, "recall"),
+    ]
+    for i, (seed, T, H, D, dt, theta, mode) in enumerate(cases):
+        rng = np.random.default_rng(seed + 1000)
+        if mode == "small":
+            orig = rng.integers(0, 4096, T); tgt = rng.integers(0, 4096, T)
+        elif mode == "recall":
+            orig = rng.integers(0, 32768, T); tgt = 131072 + np.arange(T)
+        else:
+            orig = rng.integers(100000, 131072, T); tgt = rng.integers(0, 1000, T)
+        tdt = getattr(torch, dt)
+        k = torch.from_numpy(rnd(seed, (T, H, D))).to(tdt)
+        kin = k.float().numpy().copy()
+        R._rope_remap_ref(k, torch.from_numpy(orig.astype(np.int32)),
+                          torch.from_numpy(tgt.astype(np.int32)), theta)
+        out[f"case{i}_meta"] = np.array([seed, T, H, D, theta], dtype=np.float64)
+        out[f"case{i}_dtype"] = np.array(dt)
+        out[f"case{i}_orig"] = orig.astype(np.int32)
+        out[f"case{i}_tgt"] = tgt.astype(np.int32)
+        out[f"case{i}_kin"] = kin
+        out[f"case{i}_kout"] = k.float().numpy()
+    out["ncases"] = np.array(len(cases))
+    # reference self-test KATs (kessie_hip_kernels.py:662-683): round trip and identity
+    k = torch.from_numpy(rnd(16, (64, 8, 128))).half()
+    k0 = k.clone()
+    o = torch.arange(100, 164, dtype=torch.int32); t = torch.arange(5000, 5064, dtype=torch.int32)
+    R._rope_remap_ref(k, o, t); R._rope_remap_ref(k, t, o)
+    out["kat_roundtrip_maxdiff"] = np.array((k0.float() - k.float()).abs().max().item())
+    save("rope_remap.npz", **out)
+
+
+def gen_attention():
+    out = {}
+    # the reference's own windowed-attention test configs (kessie_hip_kernels.py:623-626)
+    cfgs = [(1, 4, 128, 64, 0, True), (1, 4, 128, 64, 64, True), (1, 8, 256, 128, 128, True),
+            (2, 8, 512, 128, 256, True), (1, 2, 96, 64, 0, False), (1, 2, 80, 128, 24, False)]
+    for i, (Z, H, N, D, W, causal) in enumerate(cfgs):
+        seed = 100 + i
+        q, k, v = (torch.from_numpy(rnd(seed + j, (Z, H, N, D))) for j in range(3))
+        o = R.kessie_windowed_attention_ref(q, k, v, W, causal).numpy()
+        rows = np.unique(np.concatenate([np.arange(0, N, 7), [N - 1]]))
+        out[f"win{i}_cfg"] = np.array([Z, H, N, D, W, int(causal), seed])
+        out[f"win{i}_rows"] = rows
+        out[f"win{i}_out"] = o[:, :, rows]
+    out["nwin"] = np.array(len(cfgs))
+    # fused fog test (kessie_hip_kernels.py:647-652) plus windowed/bidirectional variants
+    fcfgs = [(1, 8, 512, 128, 0.5, 0.5, 0, True), (1, 2, 256, 64, 0.7, 0.25, 64, True),
+             (1, 2, 128, 128, 0.5, 0.5, 0, False)]
+    for i, (Z, H, N, D, a, fs, W, causal) in enumerate(fcfgs):
+        seed = 200 + i
+        q, k, v = (torch.from_numpy(rnd(seed + j, (Z, H, N, D))) for j in range(3))
+        fog = R.kessie_build_fog_weights(N, a, fs)
+        o = R.kessie_fused_fog_attention_ref(q, k, v, fog, W, causal).numpy()
+        rows = np.unique(np.concatenate([np.arange(0, N, 5), [N - 1]]))
+        out[f"fog{i}_cfg"] = np.array([Z, H, N, D, W, int(causal), seed])
+        out[f"fog{i}_fog"] = np.array([a, fs])
+        out[f"fog{i}_rows"] = rows
+        out[f"fog{i}_out"] = o[:, :, rows]
+    out["nfog"] = np.array(len(fcfgs))
+    save("attention.npz", **out)
+
+
+def gen_config1():
+    """B1 Hq8/Hkv2 D128 N4096 W512 fp32, RoPE theta 1e4 at
+    positions 0..4095, decode query = position 4095.  GQA by repeat_interleave.
+    Two fog mappings: (a) causal + clear_start = N-W; (b) reference-literal
+    window_size=W mask plus the same fog weights."""
+    B, Hq, Hkv, D, N, W = 1, 8, 2, 128, 4096, 512
+    seed = 301
+    q = torch.from_numpy(rnd(seed, (N, Hq, D)))
+    k = torch.from_numpy(rnd(seed + 1, (N, Hkv, D)))
+    v = torch.from_numpy(rnd(seed + 2, (N, Hkv, D)))
+    pos = torch.arange(N, dtype=torch.int32)
+    zero = torch.zeros(N, dtype=torch.int32)
+    # _rope_remap_ref on an fp32 tensor aliases k1 (``.float()`` returns the
+    # same storage, kessie_hip_kernels.py:603-605), so rotate float64 copies:
+    # the arithmetic is still fp32, the results are exact in float64.
+    q = R._rope_remap_ref(q.double(), zero, pos, 10000.0).float()
+    k = R._rope_remap_ref(k.double(), zero, pos, 10000.0).float()
+    qf = q.permute(1, 0, 2)[None]                                  # [1,Hq,N,D]
+    kf = k.permute(1, 0, 2)[None].repeat_interleave(Hq // Hkv, dim=1)
+    vf = v.permute(1, 0, 2)[None].repeat_interleave(Hq // Hkv, dim=1)
+    fog = R.kessie_build_fog_weights(N, 0.5, W / N)
+    oa = R.kessie_fused_fog_attention_ref(qf, kf, vf, fog, 0, True)[0, :, -1].numpy()
+    ob = R.kessie_fused_fog_attention_ref(qf, kf, vf, fog, W, True)[0, :, -1].numpy()
+    save("config1_decode.npz", cfg=np.array([B, Hq, Hkv, D, N, W, seed]),
+         q_rot_last=q[-1].numpy(), k_rot_sample=k[::257].numpy(),
+         out_causal_fog=oa, out_window_fog=ob, clear_start=np.array(int(N * (1.0 - W / N))))
+
+
+def gen_paged():
+    """KeSSiePagedKVCache bookkeeping (kessie_hip_kernels.py:484-570) driven on
+    CPU.  evict_before's no-Triton branch never clears page_valid, so the
+    device rule of kessie_kernels_v2.hip:403-406 is applied to page_valid
+    first; the reference's own Python scan then rebuilds free_pages."""
+    out = {}
+    for dt_name in ("float16", "bfloat16"):
+        dt = getattr(torch, dt_name)
+        P, ps, L, H, D = 48, 16, 2, 2, 64
+        c = R.KeSSiePagedKVCache(P, ps, L, H, D, torch.device("cpu"), dtype=dt)
+        log = []
+        steps = [("insert", 0, 40, 0), ("insert", 1, 100, 40), ("insert", 0, 16, 1000),
+                 ("evict", 48), ("insert", 1, 33, 2000), ("evict", 1001), ("insert", 0, 200, 3000),
+                 ("insert", 0, 700, 5000), ("evict", 100000), ("insert", 1, 5, 7)]
+        for si, st in enumerate(steps):
+            if st[0] == "insert":
+                _, layer, T, conv = st
+                kk = torch.from_numpy(rnd(500 + si, (T, H, D))).to(dt)
+                vv = torch.from_numpy(rnd(600 + si, (T, H, D))).to(dt)
+                ok = c.insert_probe_kv(layer, kk, vv, conv)
+                log.append(int(ok))
+            else:
+                thr = st[1]
+                hit = (c.page_valid == 1) & (c.page_positions < thr)
+                c.page_valid[hit] = 0
+                log.append(c.evict_before(thr))
+            out[f"{dt_name}_step{si}_free"] = np.array(c.free_pages, dtype=np.int32)
+            out[f"{dt_name}_step{si}_valid"] = c.page_valid.numpy().copy()
+            out[f"{dt_name}_step{si}_pos"] = c.page_positions.numpy().copy()
+            if si == 6:
+                for layer in range(L):
+                    K, V = c.get_layer_kv(layer)
+                    out[f"{dt_name}_mid_layer{layer}_K"] = K.float().numpy()
+                    out[f"{dt_name}_mid_layer{layer}_V"] = V.float().numpy()
+        for layer in range(L):
+            K, V = c.get_layer_kv(layer)
+            out[f"{dt_name}_layer{layer}_K"] = K.float().numpy()
+            out[f"{dt_name}_layer{layer}_V"] = V.float().numpy()
+        out[f"{dt_name}_results"] = np.array(log)
+        st = c.get_stats()
+        out[f"{dt_name}_stats"] = np.array([st["total_pages"], st["active_pages"], st["free_pages"],
+                                            st["active_tokens"], st["vram_gb"], st["total_evictions"],
+                                            st["total_insertions"]], dtype=np.float64)
+    out["steps"] = np.array(repr(steps))
+    save("paged_cache.npz", **out)
+
+
+if __name__ == "__main__":
+    gen_fog()
+    gen_rope()
+    gen_attention()
+    gen_config1()
+    gen_paged()
