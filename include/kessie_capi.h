@@ -1,0 +1,258 @@
+/*
+ * kessie_capi.h -- C ABI of libkessie_cuda.so (B200 / sm_100a).
+ *
+ * Drop-in replacement for the native boundary of the KeSSie fog-attention
+ * path.  The five legacy launchers keep the exact argument lists of the
+ * reference's extern "C" HIP launchers so that kessie_hip_ctypes.KeSSieKernels
+ * (kessie_hip_ctypes.py:65-114) binds them unchanged; the library is also
+ * published under the reference's file name build/libkessie_hip.so.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer owned by the caller (PyTorch tensor
+ *     storage); the library allocates no device memory.  Scratch memory is
+ *     passed in as `workspace` and sized by the matching *_workspace_size().
+ *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream),
+ *     the value of torch.cuda.Stream.cuda_stream.  All calls are asynchronous
+ *     on that stream.
+ *   - Legacy launchers return void (ctypes restype=None, as in the
+ *     reference); their failures are recorded and readable through
+ *     kessie_get_last_error().  _v2 entry points return a status:
+ *     0 = ok, >0 = argument / unsupported-shape error (nothing launched),
+ *     <0 = CUDA launch error.  No entry point calls exit() or abort().
+ *   - Device-detected faults (page id out of range, a bounded wait that ran
+ *     out) do not trap: the kernel skips the access, records a code in the
+ *     library's device status word and returns; kessie_read_device_status()
+ *     reads and clears it.
+ *   - Strides are in ELEMENTS; head_dim is always the contiguous dimension.
+ *   - Positions are int32; page tables are int32; page_valid is int8.
+ */
+#ifndef KESSIE_CAPI_H
+#define KESSIE_CAPI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of the _v2 entry points. */
+#define KESSIE_DTYPE_F16  0
+#define KESSIE_DTYPE_BF16 1
+#define KESSIE_DTYPE_F32  2
+
+/* Host-side status codes. */
+#define KESSIE_OK               0
+#define KESSIE_ERR_ARG          1   /* bad pointer / size / stride            */
+#define KESSIE_ERR_UNSUPPORTED  2   /* shape or dtype this build does not run */
+#define KESSIE_ERR_WORKSPACE    3   /* workspace missing or too small          */
+#define KESSIE_ERR_CUDA        -1   /* CUDA runtime / launch error             */
+
+/* Device status bits (kessie_read_device_status). */
+#define KESSIE_DEV_BAD_PAGE_ID  0x1 /* a page id outside [0, num_pages) was skipped */
+#define KESSIE_DEV_WAIT_TIMEOUT 0x2 /* a bounded pipeline wait gave up              */
+#define KESSIE_DEV_BAD_ARG      0x4 /* a per-sequence argument was out of range     */
+
+/* ------------------------------------------------------------------------- */
+/* Library status                                                            */
+/* ------------------------------------------------------------------------- */
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len) and returns the last status code (0 if none).
+ * No reference counterpart: the reference launchers report nothing
+ * (kessie_kernels_v2.hip:749,823 print to stderr only). */
+int kessie_get_last_error(char* buf, int len);
+
+/* Library version string, e.g. "kessie_b200 0.1 sm_100a". */
+const char* kessie_version(void);
+
+/* Synchronises `stream`, then returns the current device's status word (an
+ * OR of KESSIE_DEV_* bits) and clears it.  Returns <0 on a CUDA error. */
+int kessie_read_device_status(void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Legacy launchers -- identical argument lists to the reference             */
+/* ------------------------------------------------------------------------- */
+
+/* Replaces launch_kessie_windowed_attn (kessie_kernels_v2.hip:716-751).
+ * Q,K,V,O: fp16 [B,H,N,D] contiguous, D in {64,128}.  Causal and/or sliding
+ * window W (0 <= i-j < W) exactly as kessie_hip_kernels.py:577-588. */
+void launch_kessie_windowed_attn(const void* Q, const void* K, const void* V, void* O,
+                                 float sm_scale, int batch_size, int num_heads, int seq_len,
+                                 int head_dim, int window_size, int is_causal, void* stream);
+
+/* Replaces launch_kessie_fused_fog_attn (kessie_kernels_v2.hip:788-825).
+ * As above with fog_weights: fp32 [N]; O = softmax(mask(QK^T s)) (V * w),
+ * the semantics of kessie_fused_fog_attention_ref (kessie_hip_kernels.py:591-593). */
+void launch_kessie_fused_fog_attn(const void* Q, const void* K, const void* V, void* O,
+                                  const void* fog_weights, float sm_scale, int batch_size,
+                                  int num_heads, int seq_len, int head_dim, int window_size,
+                                  int is_causal, void* stream);
+
+/* Replaces launch_kessie_page_evict (kessie_kernels_v2.hip:753-764): for each
+ * page, valid==1 && pos < evict_before_pos -> valid=0 and *evict_count += 1.
+ * page_valid int8 [P], page_positions int32 [P], evict_count int32 [1]. */
+void launch_kessie_page_evict(void* page_valid, const void* page_positions, void* evict_count,
+                              int evict_before_pos, int num_pages, void* stream);
+
+/* Replaces launch_kessie_page_insert (kessie_kernels_v2.hip:766-782).
+ * kv_cache fp16 [max_pages, page_size, 2, H, D]; new_keys/new_values fp16
+ * [T, H, D]; token t -> page target_page_ids[t/page_size], slot t%page_size;
+ * first token of each page sets page_valid=1, page_positions=conv_pos+t.
+ * Page ids outside [0,max_pages) are skipped (as kessie_kernels_v2.hip:441). */
+void launch_kessie_page_insert(void* kv_cache, const void* new_keys, const void* new_values,
+                               const void* target_page_ids, void* page_valid, void* page_positions,
+                               int conv_pos, int num_tokens, int num_heads, int head_dim,
+                               int page_size, int max_pages, void* stream);
+
+/* Replaces launch_kessie_rope_remap (kessie_kernels_v2.hip:827-842).
+ * In-place rotate-half re-rotation of fp16 K [T, H, 2*half_dim] from
+ * orig_positions to target_positions (int32 [T]). */
+void launch_kessie_rope_remap(void* k_data, const void* orig_positions,
+                              const void* target_positions, float rope_theta,
+                              int num_tokens, int num_heads, int half_dim, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* _v2 entry points (dtype-generic, strided, paged, status-returning)        */
+/* ------------------------------------------------------------------------- */
+
+/* RoPE remap, any dtype, strided K (token_stride, head_stride in elements,
+ * head_dim contiguous).  Same math as kessie_hip_kernels.py:596-606 /
+ * kessie_kernels_v2.hip:670-707; the frequency table 1/theta^(d/half) is
+ * computed once on the host in float64 and rounded to fp32 (bit-identical to
+ * the reference's torch table at theta 1e4 and 5e5). */
+int kessie_rope_remap_v2(void* k_data, int dtype, int num_tokens, int num_heads, int head_dim,
+                         int64_t token_stride, int64_t head_stride,
+                         const int32_t* orig_positions, const int32_t* target_positions,
+                         float rope_theta, void* stream);
+
+/* Device eviction with ORDERED compaction of the freed page ids.
+ * Replaces KeSSiePagedKVCache.evict_before (kessie_hip_kernels.py:526-540)
+ * whose Python loop does one device sync per page.
+ *   - valid==1 && pos < evict_before_pos -> valid = 0 (kessie_kernels_v2.hip:403-406)
+ *   - freed set = pages with page_allocated[p]==1 && valid[p]==0 after the
+ *     update (the reference's "page_valid==0 and not in free_pages");
+ *     their page_allocated is cleared.  With page_allocated == NULL the
+ *     freed set is the pages evicted by this call.
+ *   - freed_ids[0..*freed_count) = freed page ids in ascending order (the
+ *     append order of the reference's scan).  freed_ids may be NULL.
+ * workspace: kessie_page_evict_workspace_size(num_pages) bytes. */
+size_t kessie_page_evict_workspace_size(int num_pages);
+int kessie_page_evict_v2(int8_t* page_valid, const int32_t* page_positions, int8_t* page_allocated,
+                         int num_pages, int evict_before_pos, int32_t* freed_count,
+                         int32_t* freed_ids, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Ordered list of pages with page_valid != 0 (the torch.nonzero of
+ * KeSSiePagedKVCache.get_layer_kv, kessie_hip_kernels.py:559).
+ * Uses the same workspace size as kessie_page_evict_v2. */
+int kessie_page_list_valid_v2(const int8_t* page_valid, int num_pages, int32_t* count,
+                              int32_t* ids, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused page insert + RoPE remap.  Replaces launch_kessie_page_insert
+ * (kessie_kernels_v2.hip:766-782) + launch_kessie_rope_remap for the recall
+ * path and KeSSiePagedKVCache.insert_probe_kv's per-page copies
+ * (kessie_hip_kernels.py:548-554).
+ * kv_cache: [.., page_size, .., H, D] addressed by page/token/kv/head strides
+ * (covers [P][ps][2][H][D] and vLLM's [2][P][ps][H][D]).  new_keys /
+ * new_values: [T, H, D] with src_token_stride / src_head_stride.
+ * When orig_positions != NULL, K is re-rotated from orig_positions[t] to
+ * target_positions[t] (or conv_pos + t when target_positions == NULL).
+ * page_valid / page_positions may be NULL (no metadata update). */
+int kessie_page_insert_v2(void* kv_cache, int dtype, int64_t page_stride, int64_t token_stride,
+                          int64_t kv_stride, int64_t head_stride, int max_pages, int page_size,
+                          const void* new_keys, const void* new_values, int64_t src_token_stride,
+                          int64_t src_head_stride, int num_tokens, int num_heads, int head_dim,
+                          const int32_t* target_page_ids, int8_t* page_valid,
+                          int32_t* page_positions, int conv_pos, const int32_t* orig_positions,
+                          const int32_t* target_positions, float rope_theta, void* stream);
+
+/* Page gather: out_keys / out_values [n*page_size, H, D] contiguous from the
+ * pages page_ids[0..n) in that order -- KeSSiePagedKVCache.get_layer_kv
+ * (kessie_hip_kernels.py:558-564) and the connector's block copies
+ * (kessie_kv_connector.py:419-428, 467-479).  Ids outside [0,max_pages)
+ * produce zero rows and set KESSIE_DEV_BAD_PAGE_ID.  Either output may be
+ * NULL (gather only K or only V). */
+int kessie_page_gather_v2(const void* kv_cache, int dtype, int64_t page_stride,
+                          int64_t token_stride, int64_t kv_stride, int64_t head_stride,
+                          int max_pages, int page_size, const int32_t* page_ids, int num_gather,
+                          int num_heads, int head_dim, void* out_keys, void* out_values,
+                          void* stream);
+
+/* Paged fog decode (one query token per sequence), split-KV over the page
+ * table, GQA.  New entry point: the reference has no paged / GQA / decode
+ * kernel; its semantics are kessie_fused_fog_attention_ref
+ * (kessie_hip_kernels.py:577-593) evaluated at the query row.
+ *   q [B, Hq, D] (q_stride_b, q_stride_h); K and V pages at k_cache /
+ *   v_cache with shared page/token/head strides; block_table [B, *]
+ *   (block_table_stride); seq_lens [B] local keys; kv_pos_offset [B]
+ *   (nullable: 0) global position of local key 0; q_positions [B]
+ *   (nullable: offset + len - 1) query position.
+ *   Mask: key j (global) visible iff j <= q_pos and, when window_size > 0,
+ *   q_pos - j < window_size.
+ *   Fog on V: w(j) = (j / max(cs-1,1))^fog_alpha for j < cs = clear_start[b]
+ *   (global), else 1 (kessie_hip_kernels.py:408-412); clear_start NULL or
+ *   fog_alpha <= 0 means no fog; fog_weights (nullable, fp32 indexed by
+ *   global position) overrides the formula.
+ *   out [B, Hq, D] (dtype) and/or out_partial fp32 [B, Hq, D+2] holding
+ *   (O/l, m, l) with m in natural-log units of the scaled scores -- the
+ *   triple merged across context-parallel shards by kessie_lse_combine_v2.
+ *   D in {64, 128}; dtype f16 or bf16; Hq % Hkv == 0; Hq/Hkv <= 16.
+ * workspace: kessie_paged_fog_decode_workspace_size(...) bytes. */
+size_t kessie_paged_fog_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
+                                              int head_dim, int max_seq_len, int page_size);
+int kessie_paged_fog_decode_v2(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                               const void* k_cache, const void* v_cache, int64_t page_stride,
+                               int64_t token_stride, int64_t head_stride, int num_pages,
+                               int page_size, const int32_t* block_table,
+                               int64_t block_table_stride, const int32_t* seq_lens,
+                               const int32_t* kv_pos_offset, const int32_t* q_positions,
+                               const int32_t* clear_start, float fog_alpha,
+                               const float* fog_weights, int window_size, float sm_scale,
+                               int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                               int max_seq_len, int dtype, void* out, float* out_partial,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dense fog attention, any GQA ratio: q/out [B, Hq, N, D], k/v [B, Hkv, N, D]
+ * contiguous (f16 or bf16), optional fog_weights fp32 [N].  The _v2 form of
+ * launch_kessie_fused_fog_attn / launch_kessie_windowed_attn
+ * (kessie_hip_kernels.py:367-440, semantics :577-593). */
+int kessie_fog_attention_v2(const void* q, const void* k, const void* v, void* out, int dtype,
+                            const float* fog_weights, float sm_scale, int batch, int num_q_heads,
+                            int num_kv_heads, int seq_len, int head_dim, int window_size,
+                            int is_causal, void* stream);
+
+/* Chunked prefill over a paged KV cache.  New entry point (the reference has
+ * no paged prefill); semantics kessie_hip_kernels.py:577-593 with a query
+ * offset: query i of sequence b sits at absolute position q_start[b] + i
+ * (q_start NULL: kv_lens[b] - num_q_tokens, i.e. the chunk is the last
+ * num_q_tokens keys of the cache) and attends to keys j < kv_lens[b] with
+ * j <= pos (is_causal) and pos - j < window_size (window_size > 0).
+ * Fog: clear_start[b] / fog_alpha as in the decode, or fog_weights
+ * [B, fog_weights_stride_b] fp32 by key position.
+ * q [B, T, Hq, D] and out [B, T, Hq, D] with explicit strides. */
+int kessie_paged_fog_prefill_v2(const void* q, int64_t q_stride_b, int64_t q_stride_t,
+                                int64_t q_stride_h, const void* k_cache, const void* v_cache,
+                                int64_t page_stride, int64_t token_stride, int64_t head_stride,
+                                int num_pages, int page_size, const int32_t* block_table,
+                                int64_t block_table_stride, const int32_t* kv_lens,
+                                const int32_t* q_start, const int32_t* clear_start,
+                                float fog_alpha, const float* fog_weights,
+                                int64_t fog_weights_stride_b, int window_size, int is_causal,
+                                float sm_scale, int batch, int num_q_tokens, int num_q_heads,
+                                int num_kv_heads, int head_dim, int dtype, void* out,
+                                int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h,
+                                void* stream);
+
+/* Log-sum-exp merge of S partial triples [S][rows][D+2] (split_stride
+ * elements apart) -> out [rows, D] (out_dtype) and/or out_partial
+ * [rows, D+2].  Used for the context-parallel combine after the NCCL
+ * all-gather.  New entry point (the reference has no split-KV path). */
+int kessie_lse_combine_v2(const float* partials, int num_splits, int64_t split_stride, int rows,
+                          int head_dim, void* out, int out_dtype, float* out_partial,
+                          void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KESSIE_CAPI_H */

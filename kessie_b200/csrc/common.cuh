@@ -1,0 +1,67 @@
+// common.cuh -- shared host/device helpers for libkessie_cuda.so (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/kessie_capi.h"
+
+namespace kessie {
+
+// ---------------------------------------------------------------- host errors
+// Record a status + message for kessie_get_last_error(); returns `code`.
+int set_error(int code, const char* fmt, ...);
+// Clear the calling thread's error (successful call).
+void clear_error();
+// Map a CUDA error after a launch to a status; returns 0 when none.
+int check_launch(const char* what);
+
+// Device address of this library's status word on the current device.
+int* device_status_ptr();
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ---------------------------------------------------------------- dtypes
+template <int DT> struct Elem;
+template <> struct Elem<KESSIE_DTYPE_F16>  { using T = __half;        static constexpr int bytes = 2; };
+template <> struct Elem<KESSIE_DTYPE_BF16> { using T = __nv_bfloat16; static constexpr int bytes = 2; };
+template <> struct Elem<KESSIE_DTYPE_F32>  { using T = float;         static constexpr int bytes = 4; };
+
+inline int dtype_bytes(int dt) { return dt == KESSIE_DTYPE_F32 ? 4 : 2; }
+inline bool dtype_ok(int dt) { return dt == KESSIE_DTYPE_F16 || dt == KESSIE_DTYPE_BF16 || dt == KESSIE_DTYPE_F32; }
+
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(float x) { return x; }
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+
+// 16-byte vector of elements: 8 halves / 8 bf16 / 4 floats.
+template <typename T> struct Vec16 { static constexpr int N = 16 / sizeof(T); };
+
+__device__ __forceinline__ void record_status(int* status, int bits) {
+    if (status) atomicOr(status, bits);
+}
+
+// Streaming 16-byte global load that does not allocate in L1.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ void stg_stream(void* p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};"
+                 :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
+}  // namespace kessie

@@ -1,0 +1,689 @@
+// page_ops.cu -- RoPE remap, page evict/compaction, page insert(+remap), page gather.
+//
+// All four are HBM-bound byte movers.  Layout rules:
+//   * head_dim is contiguous; every row moves as 16-byte vectors
+//     (8 x fp16/bf16 or 4 x fp32), one vector per thread per token.
+//   * a CTA owns one page (insert / gather) or a group of tokens (remap) and
+//     loops over its tokens with the loads issued back to back, so each
+//     thread keeps page_size 16-byte loads in flight with no index math in the
+//     loop body.
+//   * the RoPE angle depends on (token, d) only, so cos/sin are computed once
+//     per token into shared memory and reused by every head.
+// Semantics follow kessie_kernels_v2.hip:393-456,670-707 and
+// kessie_hip_kernels.py:520-564,596-606 (see each kernel).
+#include "common.cuh"
+
+#include <math.h>
+#include <stdio.h>
+
+namespace kessie {
+namespace {
+
+constexpr int kMaxHalf = 128;   // head_dim <= 256
+
+struct FreqTable { float f[kMaxHalf]; };
+
+// 1/theta^(d/half): theta^e in float64 rounded to fp32, then the fp32
+// reciprocal -- the two roundings of the reference's torch expression
+// (kessie_hip_kernels.py:600) with a correctly rounded pow.
+FreqTable make_freqs(float theta, int half) {
+    FreqTable t;
+    for (int d = 0; d < kMaxHalf; ++d) {
+        if (d < half) {
+            float e = (float)d / (float)half;
+            float p = (float)pow((double)theta, (double)e);
+            t.f[d] = 1.0f / p;
+        } else {
+            t.f[d] = 0.f;
+        }
+    }
+    return t;
+}
+
+// ------------------------------------------------------------------ vectors
+template <typename T> struct VecOps;
+template <> struct VecOps<__half> {
+    static constexpr int N = 8;
+    __device__ static void unpack(uint4 v, float* f) {
+        const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { float2 x = __half22float2(h[i]); f[2 * i] = x.x; f[2 * i + 1] = x.y; }
+    }
+    __device__ static uint4 pack(const float* f) {
+        uint4 v; __half2* h = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        return v;
+    }
+};
+template <> struct VecOps<__nv_bfloat16> {
+    static constexpr int N = 8;
+    __device__ static void unpack(uint4 v, float* f) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { float2 x = __bfloat1622float2(h[i]); f[2 * i] = x.x; f[2 * i + 1] = x.y; }
+    }
+    __device__ static uint4 pack(const float* f) {
+        uint4 v; __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+        return v;
+    }
+};
+template <> struct VecOps<float> {
+    static constexpr int N = 4;
+    __device__ static void unpack(uint4 v, float* f) { f[0] = __uint_as_float(v.x); f[1] = __uint_as_float(v.y); f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w); }
+    __device__ static uint4 pack(const float* f) { return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3])); }
+};
+
+// Rotate one (lo, hi) pair of 16-byte vectors: lo' = lo c - hi s, hi' = lo s + hi c
+// (kessie_kernels_v2.hip:697-706; fp32 math, round once to storage).
+template <typename T>
+__device__ __forceinline__ void rotate_pair(uint4& lo, uint4& hi, const float* c, const float* s) {
+    constexpr int N = VecOps<T>::N;
+    float a[N], b[N], ra[N], rb[N];
+    VecOps<T>::unpack(lo, a);
+    VecOps<T>::unpack(hi, b);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        ra[i] = a[i] * c[i] - b[i] * s[i];
+        rb[i] = a[i] * s[i] + b[i] * c[i];
+    }
+    lo = VecOps<T>::pack(ra);
+    hi = VecOps<T>::pack(rb);
+}
+
+// ------------------------------------------------------------------ RoPE remap
+// CTA = `tpb` tokens.  Stage 1: cos/sin of (tgt-orig)*f_d for the CTA's tokens
+// into smem.  Stage 2: every (token, head, 16B chunk of the low half) item
+// loads its low/high vectors, rotates, stores.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_remap_kernel(
+    T* __restrict__ k, int num_tokens, int num_heads, int half, int64_t tstride, int64_t hstride,
+    const int32_t* __restrict__ orig, const int32_t* __restrict__ tgt, FreqTable ft, int tpb) {
+    extern __shared__ float sm[];
+    float* cs = sm;                       // [tpb][half]
+    float* sn = sm + tpb * half;          // [tpb][half]
+    const int t0 = blockIdx.x * tpb;
+    const int nt = min(tpb, num_tokens - t0);
+    for (int i = threadIdx.x; i < nt * half; i += blockDim.x) {
+        int tl = i / half, d = i - tl * half;
+        int t = t0 + tl;
+        float delta = (float)(tgt[t] - orig[t]) * ft.f[d];
+        float s, c;
+        sincosf(delta, &s, &c);
+        cs[i] = c; sn[i] = s;
+    }
+    __syncthreads();
+    constexpr int N = VecOps<T>::N;
+    const int chunks = half / N;
+    const int items = nt * num_heads * chunks;
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+        int c = i % chunks;
+        int r = i / chunks;
+        int h = r % num_heads;
+        int tl = r / num_heads;
+        T* row = k + (int64_t)(t0 + tl) * tstride + (int64_t)h * hstride;
+        uint4* plo = reinterpret_cast<uint4*>(row + c * N);
+        uint4* phi = reinterpret_cast<uint4*>(row + half + c * N);
+        uint4 lo = *plo, hi = *phi;
+        rotate_pair<T>(lo, hi, cs + tl * half + c * N, sn + tl * half + c * N);
+        *plo = lo; *phi = hi;
+    }
+}
+
+// Scalar fallback for rows whose halves are not 16-byte aligned.
+template <typename T>
+__global__ void rope_remap_scalar_kernel(T* __restrict__ k, int num_tokens, int num_heads, int half,
+                                         int64_t tstride, int64_t hstride, const int32_t* __restrict__ orig,
+                                         const int32_t* __restrict__ tgt, FreqTable ft) {
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t total = (int64_t)num_tokens * num_heads * half;
+    if (gid >= total) return;
+    int d = (int)(gid % half);
+    int64_t r = gid / half;
+    int h = (int)(r % num_heads);
+    int t = (int)(r / num_heads);
+    float delta = (float)(tgt[t] - orig[t]) * ft.f[d];
+    float s, c;
+    sincosf(delta, &s, &c);
+    T* row = k + (int64_t)t * tstride + (int64_t)h * hstride;
+    float a = to_f32(row[d]), b = to_f32(row[d + half]);
+    row[d] = from_f32<T>(a * c - b * s);
+    row[d + half] = from_f32<T>(a * s + b * c);
+}
+
+template <typename T>
+int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int32_t* orig,
+                const int32_t* tgt, float theta, cudaStream_t st) {
+    const int half = D / 2;
+    FreqTable ft = make_freqs(theta, half);
+    constexpr int N = VecOps<T>::N;
+    bool vec = (half % N == 0) && ((reinterpret_cast<uintptr_t>(k) & 15) == 0) &&
+               ((ts * (int64_t)sizeof(T)) % 16 == 0) && ((hs * (int64_t)sizeof(T)) % 16 == 0);
+    if (vec) {
+        int per_token = H * (half / N);
+        int tpb = per_token >= 256 ? 1 : (256 / per_token);
+        if (tpb > 64) tpb = 64;
+        int grid = (T_ + tpb - 1) / tpb;
+        size_t smem = (size_t)2 * tpb * half * sizeof(float);
+        rope_remap_kernel<T><<<grid, 256, smem, st>>>((T*)k, T_, H, half, ts, hs, orig, tgt, ft, tpb);
+    } else {
+        int64_t total = (int64_t)T_ * H * half;
+        int grid = (int)((total + 255) / 256);
+        rope_remap_scalar_kernel<T><<<grid, 256, 0, st>>>((T*)k, T_, H, half, ts, hs, orig, tgt, ft);
+    }
+    return check_launch("rope_remap");
+}
+
+// ------------------------------------------------------------------ evict
+// kessie_kernels_v2.hip:393-407 -- identical rule, used by the legacy launcher.
+__global__ void page_evict_legacy_kernel(int8_t* __restrict__ valid, const int32_t* __restrict__ pos,
+                                         int32_t* __restrict__ count, int thr, int P) {
+    int p = blockIdx.x * blockDim.x + threadIdx.x;
+    bool hit = false;
+    if (p < P && valid[p] == 1 && pos[p] < thr) { valid[p] = 0; hit = true; }
+    unsigned m = __ballot_sync(0xffffffffu, hit);
+    if ((threadIdx.x & 31) == 0 && m) atomicAdd(count, __popc(m));
+}
+
+constexpr int kTile = 4096;          // pages per compaction tile
+constexpr int kTileThreads = 1024;   // 4 pages per thread
+
+size_t evict_ws(int P) {
+    int tiles = (P + kTile - 1) / kTile;
+    return align_up((size_t)P, 256) + align_up((size_t)tiles * 4, 256);
+}
+
+// Pass 1 of the ordered compaction: per page decide the flag, update state,
+// write the flag byte and the tile's count.
+// mode 0: eviction (valid/allocated update); mode 1: list pages with valid != 0.
+__global__ void __launch_bounds__(kTileThreads) compact_flags_kernel(
+    int8_t* __restrict__ valid, const int32_t* __restrict__ pos, int8_t* __restrict__ alloc, int P,
+    int thr, int mode, uint8_t* __restrict__ flags, int32_t* __restrict__ tile_counts) {
+    __shared__ int warp_sums[kTileThreads / 32];
+    const int base = blockIdx.x * kTile + threadIdx.x * 4;
+    int cnt = 0;
+    uint32_t fl = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int p = base + i;
+        if (p >= P) break;
+        int v = valid[p];
+        bool f;
+        if (mode == 1) {
+            f = v != 0;
+        } else {
+            bool hit = (v == 1) && (pos[p] < thr);
+            if (hit) { valid[p] = 0; v = 0; }
+            if (alloc) {
+                f = (alloc[p] == 1) && (v == 0);
+                if (f) alloc[p] = 0;
+            } else {
+                f = hit;
+            }
+        }
+        fl |= (uint32_t)f << (8 * i);
+        cnt += f;
+    }
+    if (base + 3 < P) {
+        *reinterpret_cast<uint32_t*>(flags + base) = fl;
+    } else {
+        for (int i = 0; i < 4 && base + i < P; ++i) flags[base + i] = (fl >> (8 * i)) & 1;
+    }
+    int w = __reduce_add_sync(0xffffffffu, cnt);
+    if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = w;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int s = __reduce_add_sync(0xffffffffu, warp_sums[threadIdx.x]);
+        if (threadIdx.x == 0) tile_counts[blockIdx.x] = s;
+    }
+}
+
+// Pass 2: exclusive prefix over earlier tiles + in-tile scan, write ids in
+// ascending page order.  Block 0 also writes the total.
+__global__ void __launch_bounds__(kTileThreads) compact_scatter_kernel(
+    const uint8_t* __restrict__ flags, const int32_t* __restrict__ tile_counts, int P, int tiles,
+    int32_t* __restrict__ out_count, int32_t* __restrict__ out_ids) {
+    __shared__ int warp_sums[kTileThreads / 32];
+    __shared__ int s_prefix, s_total;
+    // prefix of earlier tiles (and total) -- tiles is small (P/4096)
+    int pre = 0, tot = 0;
+    for (int i = threadIdx.x; i < tiles; i += blockDim.x) {
+        int c = tile_counts[i];
+        tot += c;
+        if (i < (int)blockIdx.x) pre += c;
+    }
+    pre = __reduce_add_sync(0xffffffffu, pre);
+    tot = __reduce_add_sync(0xffffffffu, tot);
+    if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = pre;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int s = __reduce_add_sync(0xffffffffu, warp_sums[threadIdx.x]);
+        if (threadIdx.x == 0) s_prefix = s;
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = tot;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int s = __reduce_add_sync(0xffffffffu, warp_sums[threadIdx.x]);
+        if (threadIdx.x == 0) s_total = s;
+    }
+    __syncthreads();
+    if (blockIdx.x == 0 && threadIdx.x == 0 && out_count) *out_count = s_total;
+    if (!out_ids) return;
+
+    const int base = blockIdx.x * kTile + threadIdx.x * 4;
+    uint32_t fl = 0;
+    for (int i = 0; i < 4; ++i)
+        if (base + i < P) fl |= (uint32_t)(flags[base + i] & 1) << (8 * i);
+    int cnt = __popc(fl);
+    // warp inclusive scan
+    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    __syncthreads();
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int v = warp_sums[lane];
+        int s = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        warp_sums[lane] = s - v;   // exclusive
+    }
+    __syncthreads();
+    int off = s_prefix + warp_sums[warp] + incl - cnt;
+    for (int i = 0; i < 4; ++i)
+        if ((fl >> (8 * i)) & 1) out_ids[off++] = base + i;
+}
+
+int run_compaction(int8_t* valid, const int32_t* pos, int8_t* alloc, int P, int thr, int mode,
+                   int32_t* count, int32_t* ids, void* ws, size_t wsb, cudaStream_t st) {
+    if (P < 0) return set_error(KESSIE_ERR_ARG, "num_pages < 0");
+    if (P == 0) {
+        if (count) cudaMemsetAsync(count, 0, 4, st);
+        return check_launch("page compaction (empty)");
+    }
+    if (!valid || (mode == 0 && !pos)) return set_error(KESSIE_ERR_ARG, "null page_valid/page_positions");
+    size_t need = evict_ws(P);
+    if (!ws || wsb < need)
+        return set_error(KESSIE_ERR_WORKSPACE, "workspace %zu bytes < required %zu", wsb, need);
+    int tiles = (P + kTile - 1) / kTile;
+    uint8_t* flags = static_cast<uint8_t*>(ws);
+    int32_t* tc = reinterpret_cast<int32_t*>(static_cast<char*>(ws) + align_up((size_t)P, 256));
+    compact_flags_kernel<<<tiles, kTileThreads, 0, st>>>(valid, pos, alloc, P, thr, mode, flags, tc);
+    compact_scatter_kernel<<<tiles, kTileThreads, 0, st>>>(flags, tc, P, tiles, count, ids);
+    return check_launch("page compaction");
+}
+
+// ------------------------------------------------------------------ insert / gather
+struct PageGeom {
+    int64_t page_stride, token_stride, kv_stride, head_stride;   // elements
+    int max_pages, page_size, num_heads, head_dim;
+};
+
+// One CTA per destination page: items = (kv, head, 16B chunk); each item
+// copies its vector for the page's tokens.  K vectors are rotated when
+// orig != nullptr (cos/sin per token from smem).
+template <typename T, bool REMAP>
+__global__ void __launch_bounds__(256) page_insert_kernel(
+    T* __restrict__ cache, PageGeom g, const T* __restrict__ nk, const T* __restrict__ nv,
+    int64_t src_ts, int64_t src_hs, int num_tokens, const int32_t* __restrict__ page_ids,
+    int8_t* __restrict__ valid, int32_t* __restrict__ positions, int conv_pos,
+    const int32_t* __restrict__ orig, const int32_t* __restrict__ tgt, FreqTable ft, int* status) {
+    extern __shared__ float sm[];
+    const int pg = blockIdx.x;
+    const int ps = g.page_size;
+    const int t0 = pg * ps;
+    const int nt = min(ps, num_tokens - t0);
+    const int phys = page_ids[pg];
+    if (phys < 0 || phys >= g.max_pages) {       // kessie_kernels_v2.hip:441 skips silently
+        if (threadIdx.x == 0) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
+        return;
+    }
+    constexpr int N = VecOps<T>::N;
+    const int D = g.head_dim, half = D / 2;
+    if (REMAP) {
+        float* cs = sm;
+        float* sn = sm + ps * half;
+        for (int i = threadIdx.x; i < nt * half; i += blockDim.x) {
+            int tl = i / half, d = i - tl * half;
+            int t = t0 + tl;
+            int target = tgt ? tgt[t] : conv_pos + t;
+            float s, c;
+            sincosf((float)(target - orig[t]) * ft.f[d], &s, &c);
+            cs[i] = c; sn[i] = s;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0 && valid) valid[phys] = 1;
+    if (threadIdx.x == 0 && positions) positions[phys] = conv_pos + t0;
+    T* page = cache + (int64_t)phys * g.page_stride;
+    const int chunks = D / N;
+    if (REMAP) {
+        // K: items (head, low-half chunk) rotate pairs; V: items (head, chunk) copy.
+        const int kitems = g.num_heads * (chunks / 2);
+        const int vitems = g.num_heads * chunks;
+        for (int i = threadIdx.x; i < kitems + vitems; i += blockDim.x) {
+            if (i < kitems) {
+                int h = i / (chunks / 2), c = i - h * (chunks / 2);
+                const T* src = nk + (int64_t)t0 * src_ts + (int64_t)h * src_hs + c * N;
+                T* dst = page + (int64_t)h * g.head_stride + c * N;
+                for (int tl = 0; tl < nt; ++tl) {
+                    uint4 lo = *reinterpret_cast<const uint4*>(src + (int64_t)tl * src_ts);
+                    uint4 hi = *reinterpret_cast<const uint4*>(src + (int64_t)tl * src_ts + half);
+                    rotate_pair<T>(lo, hi, sm + tl * half + c * N, sm + ps * half + tl * half + c * N);
+                    *reinterpret_cast<uint4*>(dst + (int64_t)tl * g.token_stride) = lo;
+                    *reinterpret_cast<uint4*>(dst + (int64_t)tl * g.token_stride + half) = hi;
+                }
+            } else {
+                int j = i - kitems;
+                int h = j / chunks, c = j - h * chunks;
+                const T* src = nv + (int64_t)t0 * src_ts + (int64_t)h * src_hs + c * N;
+                T* dst = page + g.kv_stride + (int64_t)h * g.head_stride + c * N;
+#pragma unroll 4
+                for (int tl = 0; tl < nt; ++tl)
+                    *reinterpret_cast<uint4*>(dst + (int64_t)tl * g.token_stride) =
+                        ldg_stream(src + (int64_t)tl * src_ts);
+            }
+        }
+    } else {
+        const int items = 2 * g.num_heads * chunks;
+        for (int i = threadIdx.x; i < items; i += blockDim.x) {
+            int kv = i / (g.num_heads * chunks);
+            int r = i - kv * g.num_heads * chunks;
+            int h = r / chunks, c = r - h * chunks;
+            const T* src = (kv ? nv : nk) + (int64_t)t0 * src_ts + (int64_t)h * src_hs + c * N;
+            T* dst = page + kv * g.kv_stride + (int64_t)h * g.head_stride + c * N;
+#pragma unroll 4
+            for (int tl = 0; tl < nt; ++tl)
+                *reinterpret_cast<uint4*>(dst + (int64_t)tl * g.token_stride) =
+                    ldg_stream(src + (int64_t)tl * src_ts);
+        }
+    }
+}
+
+// Legacy element-wise insert (kessie_kernels_v2.hip:414-456) for shapes the
+// vector path cannot take (head_dim not a multiple of 8, unaligned rows).
+template <typename T>
+__global__ void page_insert_scalar_kernel(T* __restrict__ cache, PageGeom g, const T* __restrict__ nk,
+                                          const T* __restrict__ nv, int64_t src_ts, int64_t src_hs,
+                                          int num_tokens, const int32_t* __restrict__ page_ids,
+                                          int8_t* __restrict__ valid, int32_t* __restrict__ positions,
+                                          int conv_pos, int* status) {
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t total = (int64_t)num_tokens * g.num_heads * g.head_dim;
+    if (gid >= total) return;
+    int d = (int)(gid % g.head_dim);
+    int64_t r = gid / g.head_dim;
+    int h = (int)(r % g.num_heads);
+    int t = (int)(r / g.num_heads);
+    int pg = t / g.page_size, in_pg = t % g.page_size;
+    int phys = page_ids[pg];
+    if (phys < 0 || phys >= g.max_pages) {
+        if (in_pg == 0 && h == 0 && d == 0) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
+        return;
+    }
+    int64_t base = (int64_t)phys * g.page_stride + (int64_t)in_pg * g.token_stride + (int64_t)h * g.head_stride + d;
+    int64_t src = (int64_t)t * src_ts + (int64_t)h * src_hs + d;
+    cache[base] = nk[src];
+    cache[base + g.kv_stride] = nv[src];
+    if (in_pg == 0 && h == 0 && d == 0) {
+        if (valid) valid[phys] = 1;
+        if (positions) positions[phys] = conv_pos + t;
+    }
+}
+
+// One CTA per gathered page: items (kv, head, chunk) copy their vector for
+// all page_size tokens into the dense [n*ps, H, D] outputs.
+template <typename T>
+__global__ void __launch_bounds__(256) page_gather_kernel(const T* __restrict__ cache, PageGeom g,
+                                                           const int32_t* __restrict__ ids,
+                                                           T* __restrict__ ok, T* __restrict__ ov,
+                                                           int* status) {
+    const int i = blockIdx.x;
+    const int phys = ids[i];
+    const bool bad = phys < 0 || phys >= g.max_pages;
+    if (bad && threadIdx.x == 0) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
+    constexpr int N = VecOps<T>::N;
+    const int chunks = g.head_dim / N;
+    const int H = g.num_heads, ps = g.page_size;
+    const int64_t orow = (int64_t)H * g.head_dim;            // dense token stride
+    const int items = 2 * H * chunks;
+    const T* page = cache + (bad ? 0 : (int64_t)phys * g.page_stride);
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+        int kv = it / (H * chunks);
+        int r = it - kv * H * chunks;
+        int h = r / chunks, c = r - h * chunks;
+        T* out = kv ? ov : ok;
+        if (!out) continue;
+        const T* src = page + kv * g.kv_stride + (int64_t)h * g.head_stride + c * N;
+        T* dst = out + (int64_t)i * ps * orow + (int64_t)h * g.head_dim + c * N;
+        if (bad) {
+            for (int t = 0; t < ps; ++t) *reinterpret_cast<uint4*>(dst + t * orow) = make_uint4(0, 0, 0, 0);
+            continue;
+        }
+        if (ps == 16) {
+            uint4 v[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = ldg_stream(src + (int64_t)t * g.token_stride);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) stg_stream(dst + t * orow, v[t]);
+        } else {
+#pragma unroll 4
+            for (int t = 0; t < ps; ++t) stg_stream(dst + t * orow, ldg_stream(src + (int64_t)t * g.token_stride));
+        }
+    }
+}
+
+template <typename T>
+__global__ void page_gather_scalar_kernel(const T* __restrict__ cache, PageGeom g, const int32_t* __restrict__ ids,
+                                          int n, T* __restrict__ ok, T* __restrict__ ov, int* status) {
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t total = (int64_t)n * g.page_size * g.num_heads * g.head_dim;
+    if (gid >= total) return;
+    int d = (int)(gid % g.head_dim);
+    int64_t r = gid / g.head_dim;
+    int h = (int)(r % g.num_heads);
+    int64_t tok = r / g.num_heads;
+    int i = (int)(tok / g.page_size), s = (int)(tok % g.page_size);
+    int phys = ids[i];
+    bool bad = phys < 0 || phys >= g.max_pages;
+    if (bad && s == 0 && h == 0 && d == 0) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
+    int64_t src = (int64_t)phys * g.page_stride + (int64_t)s * g.token_stride + (int64_t)h * g.head_stride + d;
+    if (ok) ok[gid] = bad ? from_f32<T>(0.f) : cache[src];
+    if (ov) ov[gid] = bad ? from_f32<T>(0.f) : cache[src + g.kv_stride];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <typename T>
+int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv, int64_t sts, int64_t shs,
+                  int T_, const int32_t* ids, int8_t* valid, int32_t* positions, int conv_pos,
+                  const int32_t* orig, const int32_t* tgt, float theta, cudaStream_t st) {
+    constexpr int N = VecOps<T>::N;
+    const int es = sizeof(T);
+    bool vec = g.head_dim % (2 * N) == 0 && aligned16(cache) && aligned16(nk) && aligned16(nv) &&
+               (g.page_stride * es) % 16 == 0 && (g.token_stride * es) % 16 == 0 &&
+               (g.kv_stride * es) % 16 == 0 && (g.head_stride * es) % 16 == 0 &&
+               (sts * es) % 16 == 0 && (shs * es) % 16 == 0;
+    int* status = device_status_ptr();
+    int pages = (T_ + g.page_size - 1) / g.page_size;
+    if (pages == 0) return check_launch("page_insert (empty)");
+    if (orig) {
+        if (!vec) return set_error(KESSIE_ERR_UNSUPPORTED, "fused insert+remap needs 16-byte aligned rows and head_dim %% %d == 0", 2 * N);
+        if (g.head_dim / 2 > kMaxHalf) return set_error(KESSIE_ERR_UNSUPPORTED, "head_dim > %d", 2 * kMaxHalf);
+        FreqTable ft = make_freqs(theta, g.head_dim / 2);
+        size_t smem = (size_t)2 * g.page_size * (g.head_dim / 2) * sizeof(float);
+        if (smem > 200 * 1024) return set_error(KESSIE_ERR_UNSUPPORTED, "page_size too large for fused remap");
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(page_insert_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        page_insert_kernel<T, true><<<pages, 256, smem, st>>>((T*)cache, g, (const T*)nk, (const T*)nv, sts, shs, T_,
+                                                               ids, valid, positions, conv_pos, orig, tgt, ft, status);
+    } else if (vec) {
+        FreqTable ft{};
+        page_insert_kernel<T, false><<<pages, 256, 0, st>>>((T*)cache, g, (const T*)nk, (const T*)nv, sts, shs, T_,
+                                                             ids, valid, positions, conv_pos, nullptr, nullptr, ft, status);
+    } else {
+        int64_t total = (int64_t)T_ * g.num_heads * g.head_dim;
+        page_insert_scalar_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+            (T*)cache, g, (const T*)nk, (const T*)nv, sts, shs, T_, ids, valid, positions, conv_pos, status);
+    }
+    return check_launch("page_insert");
+}
+
+template <typename T>
+int launch_gather(const void* cache, const PageGeom& g, const int32_t* ids, int n, void* ok, void* ov, cudaStream_t st) {
+    constexpr int N = VecOps<T>::N;
+    const int es = sizeof(T);
+    int* status = device_status_ptr();
+    if (n == 0) return check_launch("page_gather (empty)");
+    bool vec = g.head_dim % N == 0 && aligned16(cache) && (!ok || aligned16(ok)) && (!ov || aligned16(ov)) &&
+               (g.page_stride * es) % 16 == 0 && (g.token_stride * es) % 16 == 0 &&
+               (g.kv_stride * es) % 16 == 0 && (g.head_stride * es) % 16 == 0;
+    if (vec) {
+        page_gather_kernel<T><<<n, 256, 0, st>>>((const T*)cache, g, ids, (T*)ok, (T*)ov, status);
+    } else {
+        int64_t total = (int64_t)n * g.page_size * g.num_heads * g.head_dim;
+        page_gather_scalar_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>((const T*)cache, g, ids, n, (T*)ok, (T*)ov, status);
+    }
+    return check_launch("page_gather");
+}
+
+}  // namespace
+}  // namespace kessie
+
+using namespace kessie;
+
+// ============================================================== C ABI
+extern "C" {
+
+void launch_kessie_rope_remap(void* k_data, const void* orig_positions, const void* target_positions,
+                              float rope_theta, int num_tokens, int num_heads, int half_dim, void* stream) {
+    if (!k_data || !orig_positions || !target_positions || num_tokens < 0 || num_heads <= 0 ||
+        half_dim <= 0 || half_dim > kMaxHalf) {
+        set_error(KESSIE_ERR_ARG, "launch_kessie_rope_remap: bad arguments (half_dim=%d)", half_dim);
+        return;
+    }
+    if (num_tokens == 0) { clear_error(); return; }
+    int64_t D = 2 * (int64_t)half_dim;
+    launch_rope<__half>(k_data, num_tokens, num_heads, (int)D, (int64_t)num_heads * D, D,
+                        (const int32_t*)orig_positions, (const int32_t*)target_positions, rope_theta,
+                        as_stream(stream));
+}
+
+int kessie_rope_remap_v2(void* k_data, int dtype, int num_tokens, int num_heads, int head_dim,
+                         int64_t token_stride, int64_t head_stride, const int32_t* orig_positions,
+                         const int32_t* target_positions, float rope_theta, void* stream) {
+    if (!dtype_ok(dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "rope_remap_v2: dtype %d", dtype);
+    if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0 || (head_dim & 1) || head_dim / 2 > kMaxHalf)
+        return set_error(KESSIE_ERR_ARG, "rope_remap_v2: bad shape T=%d H=%d D=%d", num_tokens, num_heads, head_dim);
+    if (num_tokens == 0) { clear_error(); return 0; }
+    if (!k_data || !orig_positions || !target_positions) return set_error(KESSIE_ERR_ARG, "rope_remap_v2: null pointer");
+    if (token_stride < head_dim || head_stride < head_dim)
+        return set_error(KESSIE_ERR_ARG, "rope_remap_v2: strides smaller than head_dim");
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case KESSIE_DTYPE_F16: return launch_rope<__half>(k_data, num_tokens, num_heads, head_dim, token_stride, head_stride, orig_positions, target_positions, rope_theta, st);
+        case KESSIE_DTYPE_BF16: return launch_rope<__nv_bfloat16>(k_data, num_tokens, num_heads, head_dim, token_stride, head_stride, orig_positions, target_positions, rope_theta, st);
+        default: return launch_rope<float>(k_data, num_tokens, num_heads, head_dim, token_stride, head_stride, orig_positions, target_positions, rope_theta, st);
+    }
+}
+
+void launch_kessie_page_evict(void* page_valid, const void* page_positions, void* evict_count,
+                              int evict_before_pos, int num_pages, void* stream) {
+    if (num_pages <= 0) { clear_error(); return; }
+    if (!page_valid || !page_positions || !evict_count) {
+        set_error(KESSIE_ERR_ARG, "launch_kessie_page_evict: null pointer");
+        return;
+    }
+    page_evict_legacy_kernel<<<(num_pages + 255) / 256, 256, 0, as_stream(stream)>>>(
+        (int8_t*)page_valid, (const int32_t*)page_positions, (int32_t*)evict_count, evict_before_pos, num_pages);
+    check_launch("page_evict");
+}
+
+size_t kessie_page_evict_workspace_size(int num_pages) { return num_pages > 0 ? evict_ws(num_pages) : 0; }
+
+int kessie_page_evict_v2(int8_t* page_valid, const int32_t* page_positions, int8_t* page_allocated,
+                         int num_pages, int evict_before_pos, int32_t* freed_count, int32_t* freed_ids,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+    return run_compaction(page_valid, page_positions, page_allocated, num_pages, evict_before_pos, 0,
+                          freed_count, freed_ids, workspace, workspace_bytes, as_stream(stream));
+}
+
+int kessie_page_list_valid_v2(const int8_t* page_valid, int num_pages, int32_t* count, int32_t* ids,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+    return run_compaction(const_cast<int8_t*>(page_valid), nullptr, nullptr, num_pages, 0, 1, count, ids,
+                          workspace, workspace_bytes, as_stream(stream));
+}
+
+void launch_kessie_page_insert(void* kv_cache, const void* new_keys, const void* new_values,
+                               const void* target_page_ids, void* page_valid, void* page_positions,
+                               int conv_pos, int num_tokens, int num_heads, int head_dim, int page_size,
+                               int max_pages, void* stream) {
+    if (num_tokens <= 0) { clear_error(); return; }
+    if (!kv_cache || !new_keys || !new_values || !target_page_ids || num_heads <= 0 || head_dim <= 0 ||
+        page_size <= 0 || max_pages <= 0) {
+        set_error(KESSIE_ERR_ARG, "launch_kessie_page_insert: bad arguments");
+        return;
+    }
+    PageGeom g;
+    g.head_stride = head_dim;
+    g.kv_stride = (int64_t)num_heads * head_dim;
+    g.token_stride = 2 * g.kv_stride;
+    g.page_stride = (int64_t)page_size * g.token_stride;
+    g.max_pages = max_pages; g.page_size = page_size; g.num_heads = num_heads; g.head_dim = head_dim;
+    launch_insert<__half>(kv_cache, g, new_keys, new_values, (int64_t)num_heads * head_dim, head_dim, num_tokens,
+                          (const int32_t*)target_page_ids, (int8_t*)page_valid, (int32_t*)page_positions,
+                          conv_pos, nullptr, nullptr, 0.f, as_stream(stream));
+}
+
+int kessie_page_insert_v2(void* kv_cache, int dtype, int64_t page_stride, int64_t token_stride, int64_t kv_stride,
+                          int64_t head_stride, int max_pages, int page_size, const void* new_keys,
+                          const void* new_values, int64_t src_token_stride, int64_t src_head_stride, int num_tokens,
+                          int num_heads, int head_dim, const int32_t* target_page_ids, int8_t* page_valid,
+                          int32_t* page_positions, int conv_pos, const int32_t* orig_positions,
+                          const int32_t* target_positions, float rope_theta, void* stream) {
+    if (!dtype_ok(dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "page_insert_v2: dtype %d", dtype);
+    if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0 || page_size <= 0 || max_pages <= 0)
+        return set_error(KESSIE_ERR_ARG, "page_insert_v2: bad shape");
+    if (num_tokens == 0) { clear_error(); return 0; }
+    if (!kv_cache || !new_keys || !new_values || !target_page_ids)
+        return set_error(KESSIE_ERR_ARG, "page_insert_v2: null pointer");
+    if (orig_positions && (head_dim & 1)) return set_error(KESSIE_ERR_ARG, "page_insert_v2: odd head_dim with remap");
+    PageGeom g{page_stride, token_stride, kv_stride, head_stride, max_pages, page_size, num_heads, head_dim};
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case KESSIE_DTYPE_F16: return launch_insert<__half>(kv_cache, g, new_keys, new_values, src_token_stride, src_head_stride, num_tokens, target_page_ids, page_valid, page_positions, conv_pos, orig_positions, target_positions, rope_theta, st);
+        case KESSIE_DTYPE_BF16: return launch_insert<__nv_bfloat16>(kv_cache, g, new_keys, new_values, src_token_stride, src_head_stride, num_tokens, target_page_ids, page_valid, page_positions, conv_pos, orig_positions, target_positions, rope_theta, st);
+        default: return launch_insert<float>(kv_cache, g, new_keys, new_values, src_token_stride, src_head_stride, num_tokens, target_page_ids, page_valid, page_positions, conv_pos, orig_positions, target_positions, rope_theta, st);
+    }
+}
+
+int kessie_page_gather_v2(const void* kv_cache, int dtype, int64_t page_stride, int64_t token_stride,
+                          int64_t kv_stride, int64_t head_stride, int max_pages, int page_size,
+                          const int32_t* page_ids, int num_gather, int num_heads, int head_dim, void* out_keys,
+                          void* out_values, void* stream) {
+    if (!dtype_ok(dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "page_gather_v2: dtype %d", dtype);
+    if (num_gather < 0 || num_heads <= 0 || head_dim <= 0 || page_size <= 0 || max_pages <= 0)
+        return set_error(KESSIE_ERR_ARG, "page_gather_v2: bad shape");
+    if (num_gather == 0) { clear_error(); return 0; }
+    if (!kv_cache || !page_ids || (!out_keys && !out_values)) return set_error(KESSIE_ERR_ARG, "page_gather_v2: null pointer");
+    PageGeom g{page_stride, token_stride, kv_stride, head_stride, max_pages, page_size, num_heads, head_dim};
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case KESSIE_DTYPE_F16: return launch_gather<__half>(kv_cache, g, page_ids, num_gather, out_keys, out_values, st);
+        case KESSIE_DTYPE_BF16: return launch_gather<__nv_bfloat16>(kv_cache, g, page_ids, num_gather, out_keys, out_values, st);
+        default: return launch_gather<float>(kv_cache, g, page_ids, num_gather, out_keys, out_values, st);
+    }
+}
+
+}  // extern "C"

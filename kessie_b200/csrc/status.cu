@@ -1,0 +1,103 @@
+// status.cu -- last-error bookkeeping, device status word, device queries.
+#include "common.cuh"
+
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+namespace {
+
+thread_local char g_msg[512] = {0};
+thread_local int g_status = 0;
+
+// One status word per device context; OR of KESSIE_DEV_* bits.
+__device__ int g_device_status;
+
+constexpr int kMaxDevices = 64;
+int* g_status_ptr[kMaxDevices] = {nullptr};
+int g_sm_count[kMaxDevices] = {0};
+std::mutex g_mu;
+
+}  // namespace
+
+namespace kessie {
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    g_status = code;
+    return code;
+}
+
+void clear_error() {
+    g_status = 0;
+    g_msg[0] = 0;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(KESSIE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    clear_error();
+    return KESSIE_OK;
+}
+
+int* device_status_ptr() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_status_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        g_status_ptr[dev] = static_cast<int*>(p);
+    }
+    return g_status_ptr[dev];
+}
+
+int sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_sm_count[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = 148;
+        }
+        g_sm_count[dev] = n;
+    }
+    return g_sm_count[dev];
+}
+
+}  // namespace kessie
+
+extern "C" int kessie_get_last_error(char* buf, int len) {
+    if (buf && len > 0) {
+        strncpy(buf, g_msg, (size_t)len - 1);
+        buf[len - 1] = 0;
+    }
+    return g_status;
+}
+
+extern "C" const char* kessie_version(void) { return "kessie_b200 0.1 sm_100a"; }
+
+extern "C" int kessie_read_device_status(void* stream) {
+    int* p = kessie::device_status_ptr();
+    if (!p) return kessie::set_error(KESSIE_ERR_CUDA, "device status word unavailable");
+    cudaStream_t s = kessie::as_stream(stream);
+    int host = 0;
+    if (cudaMemcpyAsync(&host, p, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemsetAsync(p, 0, sizeof(int), s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaError_t e = cudaGetLastError();
+        return kessie::set_error(KESSIE_ERR_CUDA, "read_device_status: %s", cudaGetErrorString(e));
+    }
+    kessie::clear_error();
+    return host;
+}

@@ -1,0 +1,49 @@
+// tma_host.cuh -- host-side TMA descriptor encoding through the driver entry point
+// (no link-time dependency on libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+namespace kessie {
+
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// Tensor map over the paged K (or V) cache of one layer, viewed as the 5-D
+// tensor [d_lo 64][token ps][d_hi D/64][head H][page P] (innermost first).
+// One box = one 16-token slice of one head of one page:
+// {64, 16, D/64, 1, 1} elements, 128-byte swizzled rows in shared memory
+// (row r = d_hi*16 + token, so ldmatrix row groups never share a bank set).
+// Returns CUDA_SUCCESS or the driver's error.
+inline CUresult encode_kv_tile_map(CUtensorMap* map, const void* base, bool bf16, int head_dim, int page_size,
+                                   int num_heads, int num_pages, int64_t token_stride, int64_t head_stride,
+                                   int64_t page_stride) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return CUDA_ERROR_NOT_SUPPORTED;
+    const int dhi = head_dim / 64;
+    cuuint64_t dims[5] = {64, (cuuint64_t)page_size, (cuuint64_t)dhi, (cuuint64_t)num_heads, (cuuint64_t)num_pages};
+    cuuint64_t strides[4] = {(cuuint64_t)token_stride * 2, 128, (cuuint64_t)head_stride * 2, (cuuint64_t)page_stride * 2};
+    cuuint32_t box[5] = {64, 16, (cuuint32_t)dhi, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+               const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace kessie

@@ -1,0 +1,262 @@
+"""Tensor-level wrappers over the C ABI (PyTorch tensors are buffers only).
+
+Every function here launches CUDA kernels of libkessie_cuda.so on the given
+stream (default: torch's current stream) and never computes on the CPU.
+Shapes follow the reference: K rows are [tokens, heads, head_dim] with
+head_dim contiguous; KV caches are addressed by (page, token, kv, head)
+strides so both the KeSSie layout [P, ps, 2, H, D]
+(kessie_hip_kernels.py:496-498) and vLLM's [2, P, ps, H, D]
+(kessie_kv_connector.py:309,465) work without copies.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
+
+_ws_lock = threading.Lock()
+_ws_cache: dict = {}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError(f"tensor must be on a CUDA device, got {t.device}")
+
+
+def _i32(t: Optional[torch.Tensor], device) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    if not torch.is_tensor(t):
+        t = torch.as_tensor(t, dtype=torch.int32, device=device)
+    if t.dtype != torch.int32:
+        t = t.to(torch.int32)
+    return t.contiguous()
+
+
+def workspace(nbytes: int, device, tag: str = "default") -> torch.Tensor:
+    """A cached uint8 scratch buffer of at least nbytes on device (reused by
+    later calls with the same tag, so steady-state calls allocate nothing).
+    Calls that share a tag must be ordered on one stream."""
+    dev = torch.device(device)
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), tag)
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+            _ws_cache[key] = buf
+        return buf
+
+
+def read_device_status(stream=None) -> int:
+    """Synchronise the stream and return/clear the device status bits."""
+    r = _lib.load().kessie_read_device_status(_stream(stream))
+    if r < 0:
+        _lib.check(r, "read_device_status")
+    return r
+
+
+# --------------------------------------------------------------------- RoPE
+def rope_remap(k: torch.Tensor, orig_positions, target_positions, rope_theta: float = 10000.0, stream=None):
+    """In-place re-rotation of K [T, H, D] (kessie_hip_kernels.py:596-606)."""
+    _need_cuda(k)
+    if k.dim() != 3 or k.stride(2) != 1:
+        raise ValueError("k must be [tokens, heads, head_dim] with head_dim contiguous")
+    T, H, D = k.shape
+    o = _i32(orig_positions, k.device)
+    t = _i32(target_positions, k.device)
+    if o.numel() != T or t.numel() != T:
+        raise ValueError("positions must have one entry per token")
+    lib = _lib.load()
+    _lib.check(lib.kessie_rope_remap_v2(k.data_ptr(), dtype_code(k), T, H, D, k.stride(0), k.stride(1),
+                                        o.data_ptr(), t.data_ptr(), float(rope_theta), _stream(stream)),
+               "rope_remap")
+    return k
+
+
+# --------------------------------------------------------------------- pages
+def kv_layout_strides(kv: torch.Tensor, layout: str = "kessie") -> Tuple[int, int, int, int, int, int, int, int]:
+    """(page, token, kv, head strides, num_pages, page_size, heads, head_dim)."""
+    if layout == "kessie":          # [P, ps, 2, H, D]
+        P, ps, two, H, D = kv.shape
+        s = kv.stride()
+        return s[0], s[1], s[2], s[3], P, ps, H, D
+    if layout == "vllm":            # [2, P, ps, H, D]
+        two, P, ps, H, D = kv.shape
+        s = kv.stride()
+        return s[1], s[2], s[0], s[3], P, ps, H, D
+    raise ValueError(f"unknown layout {layout}")
+
+
+def page_evict(page_valid: torch.Tensor, page_positions: torch.Tensor, evict_before_pos: int,
+               page_allocated: Optional[torch.Tensor] = None, stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Device eviction + ordered compaction.  Returns (count int32[1],
+    ids int32[P]); ids[:count] are the freed page ids in ascending order."""
+    _need_cuda(page_valid, page_positions, page_allocated)
+    P = page_valid.numel()
+    dev = page_valid.device
+    count = torch.zeros(1, dtype=torch.int32, device=dev)
+    ids = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    ws_n = lib.kessie_page_evict_workspace_size(P)
+    ws = workspace(ws_n, dev, "compaction")
+    _lib.check(lib.kessie_page_evict_v2(page_valid.data_ptr(), page_positions.data_ptr(), _p(page_allocated), P,
+                                        int(evict_before_pos), count.data_ptr(), ids.data_ptr(), ws.data_ptr(),
+                                        ws.numel(), _stream(stream)), "page_evict")
+    return count, ids
+
+
+def list_valid_pages(page_valid: torch.Tensor, stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Ascending ids of pages with page_valid != 0: (count int32[1], ids int32[P])."""
+    _need_cuda(page_valid)
+    P = page_valid.numel()
+    dev = page_valid.device
+    count = torch.zeros(1, dtype=torch.int32, device=dev)
+    ids = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    ws = workspace(lib.kessie_page_evict_workspace_size(P), dev, "compaction")
+    _lib.check(lib.kessie_page_list_valid_v2(page_valid.data_ptr(), P, count.data_ptr(), ids.data_ptr(),
+                                             ws.data_ptr(), ws.numel(), _stream(stream)), "list_valid_pages")
+    return count, ids
+
+
+def page_insert(kv: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, page_ids, page_valid=None,
+                page_positions=None, conv_pos: int = 0, orig_positions=None, target_positions=None,
+                rope_theta: float = 10000.0, layout: str = "kessie", stream=None):
+    """Copy keys/values [T, H, D] into pages page_ids (token t -> page
+    page_ids[t // ps], slot t % ps), optionally re-rotating K from
+    orig_positions to target_positions (default conv_pos + t)."""
+    _need_cuda(kv, keys, values)
+    if keys.dtype != kv.dtype or values.dtype != kv.dtype:
+        raise TypeError("keys/values dtype must match the cache")
+    if keys.stride(2) != 1 or values.stride(2) != 1 or keys.stride() != values.stride():
+        raise ValueError("keys/values must share strides with head_dim contiguous")
+    ps_, ts_, kvs_, hs_, P, ps, H, D = kv_layout_strides(kv, layout)
+    T = keys.shape[0]
+    ids = _i32(page_ids, kv.device)
+    o = _i32(orig_positions, kv.device)
+    tg = _i32(target_positions, kv.device)
+    lib = _lib.load()
+    _lib.check(lib.kessie_page_insert_v2(kv.data_ptr(), dtype_code(kv), ps_, ts_, kvs_, hs_, P, ps, keys.data_ptr(),
+                                         values.data_ptr(), keys.stride(0), keys.stride(1), T, H, D, ids.data_ptr(),
+                                         _p(page_valid), _p(page_positions), int(conv_pos), _p(o), _p(tg),
+                                         float(rope_theta), _stream(stream)), "page_insert")
+
+
+def page_gather(kv: torch.Tensor, page_ids, layout: str = "kessie", out_keys=None, out_values=None,
+                want_keys: bool = True, want_values: bool = True, stream=None):
+    """Gather pages -> dense K, V [n*ps, H, D] in the order of page_ids."""
+    _need_cuda(kv)
+    ps_, ts_, kvs_, hs_, P, ps, H, D = kv_layout_strides(kv, layout)
+    ids = _i32(page_ids, kv.device)
+    n = ids.numel()
+    if want_keys and out_keys is None:
+        out_keys = torch.empty(n * ps, H, D, dtype=kv.dtype, device=kv.device)
+    if want_values and out_values is None:
+        out_values = torch.empty(n * ps, H, D, dtype=kv.dtype, device=kv.device)
+    lib = _lib.load()
+    _lib.check(lib.kessie_page_gather_v2(kv.data_ptr(), dtype_code(kv), ps_, ts_, kvs_, hs_, P, ps, ids.data_ptr(), n,
+                                         H, D, _p(out_keys if want_keys else None),
+                                         _p(out_values if want_values else None), _stream(stream)), "page_gather")
+    return out_keys, out_values
+
+
+# --------------------------------------------------------------------- decode
+def decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, max_seq_len, page_size=16) -> int:
+    return int(_lib.load().kessie_paged_fog_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim,
+                                                                  max_seq_len, page_size))
+
+
+def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                     seq_lens: torch.Tensor, clear_start=None, fog_alpha: float = 0.5, fog_weights=None,
+                     window_size: int = 0, sm_scale: Optional[float] = None, kv_pos_offset=None,
+                     q_positions=None, max_seq_len: Optional[int] = None, out: Optional[torch.Tensor] = None,
+                     out_partial: Optional[torch.Tensor] = None, want_out: bool = True, stream=None,
+                     ws: Optional[torch.Tensor] = None):
+    """Paged fog decode: q [B, Hq, D]; k_cache / v_cache [P, ps, Hkv, D]
+    views (any page/token/head strides, D contiguous); block_table [B, maxP]
+    int32; seq_lens [B] int32.  Returns out [B, Hq, D] (q.dtype) and, if
+    requested, out_partial fp32 [B, Hq, D+2] = (O/l, m, l) for the
+    context-parallel combine."""
+    _need_cuda(q, k_cache, v_cache, block_table, seq_lens)
+    B, Hq, D = q.shape
+    P, ps, Hkv, Dk = k_cache.shape
+    if Dk != D or v_cache.shape != k_cache.shape or v_cache.stride() != k_cache.stride():
+        raise ValueError("k_cache/v_cache must be matching [P, ps, Hkv, D] views")
+    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise TypeError("q and the cache must share a dtype")
+    if q.stride(2) != 1 or k_cache.stride(3) != 1:
+        raise ValueError("head_dim must be contiguous")
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    if bt.stride(1) != 1:
+        bt = bt.contiguous()
+    sl = _i32(seq_lens, q.device)
+    if max_seq_len is None:
+        max_seq_len = bt.shape[1] * ps
+    if max_seq_len > bt.shape[1] * ps:
+        raise ValueError(f"max_seq_len {max_seq_len} exceeds the block table capacity {bt.shape[1] * ps}")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    cs = _i32(clear_start, q.device)
+    off = _i32(kv_pos_offset, q.device)
+    qp = _i32(q_positions, q.device)
+    fw = None
+    if fog_weights is not None:
+        fw = fog_weights if fog_weights.dtype == torch.float32 else fog_weights.float()
+        fw = fw.contiguous()
+    if want_out and out is None:
+        out = torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
+    lib = _lib.load()
+    need = lib.kessie_paged_fog_decode_workspace_size(B, Hq, Hkv, D, int(max_seq_len), ps)
+    if ws is None:
+        ws = workspace(need, q.device, "decode")
+    _lib.check(lib.kessie_paged_fog_decode_v2(
+        q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
+        k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), sl.data_ptr(), _p(off), _p(qp),
+        _p(cs), float(fog_alpha), _p(fw), int(window_size), float(sm_scale), B, Hq, Hkv, D, int(max_seq_len),
+        dtype_code(q), _p(out if want_out else None), _p(out_partial), ws.data_ptr(), ws.numel(), _stream(stream)),
+        "paged_fog_decode")
+    return out
+
+
+def lse_combine(partials: torch.Tensor, out: Optional[torch.Tensor] = None, out_dtype=torch.bfloat16,
+                out_partial: Optional[torch.Tensor] = None, stream=None):
+    """Merge partial triples [S, rows..., D+2] (fp32) into out [rows..., D]."""
+    _need_cuda(partials)
+    if partials.dtype != torch.float32 or not partials.is_contiguous():
+        raise ValueError("partials must be contiguous fp32 [S, ..., D+2]")
+    S = partials.shape[0]
+    D = partials.shape[-1] - 2
+    rows = partials[0].numel() // (D + 2)
+    if out is None:
+        out = torch.empty(*partials.shape[1:-1], D, dtype=out_dtype, device=partials.device)
+    lib = _lib.load()
+    _lib.check(lib.kessie_lse_combine_v2(partials.data_ptr(), S, partials.stride(0), rows, D, _p(out),
+                                         dtype_code(out), _p(out_partial), _stream(stream)), "lse_combine")
+    return out
