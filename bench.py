@@ -1,0 +1,478 @@
+#!/usr/bin/env python
+"""Benchmark of the KeSSie fog-attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kessie|reference] [--workload NAME]
+
+Default workload (every N): BASELINE config 5, the 1M-token context-parallel
+fog decode at the 70B attention shape -- batch 4, 64 query / 8 KV heads,
+head_dim 128, bf16 paged KV (page 16) of 1,048,576 tokens per sequence,
+window 8192 (clear_start = N - 8192, fog alpha 0.5).  The KV sequence is
+sharded by position across the N ranks (strong scaling: total work fixed);
+each rank decodes its shard, the fp32 (O/l, m, l) triples are all-gathered
+over NCCL and merged by log-sum-exp.  At N = 1 the step moves the same
+17.18 GB of KV as the "@128k" decode headline (config 3 at fixed 128k).
+
+One step = one decode of every sequence.  `value` = algorithmic KV bytes of
+the whole job / step time (max over ranks), GB/s.  The KV (17.2 GB) is far
+larger than L2 (126 MB), so no L2 flush is needed between steps.
+
+Other workloads (parity configs, measured on request): decode_cfg3
+(config 3, lengths U[64k,128k]), decode_128k (config 3 at fixed 128k),
+page_ops (config 2), prefill (config 4).
+
+`--impl reference` times the reference path's CPU implementation (the numpy
+oracle port of kessie_hip_kernels.py:577-593; the reference's Python module
+cannot travel to the GPU box) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_NOTE = "KV working set far above the 126 MB L2; no flush between steps"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["kessie", "reference"], default="kessie")
+    ap.add_argument("--workload", default="cp_decode_1m",
+                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "page_ops", "prefill"])
+    ap.add_argument("--seed", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def load_traffic(kernel_key):
+    """dram bytes per unit of work from a committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get(kernel_key)
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampler for the timed region (our own child process)."""
+
+    FIELDS = ["clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, local_rank):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idx = local_rank
+        if vis:
+            parts = [x.strip() for x in vis.split(",") if x.strip()]
+            if local_rank < len(parts) and parts[local_rank].isdigit():
+                idx = int(parts[local_rank])
+        self.idx = idx
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + ",".join(self.FIELDS),
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0])); mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------- workloads
+CFG5 = dict(batch=4, q_heads=64, kv_heads=8, head_dim=128, ctx=1048576, window=8192, page=16, alpha=0.5)
+CFG3 = dict(batch=32, q_heads=32, kv_heads=8, head_dim=128, window=4096, page=16, alpha=0.5, lo=65536, hi=131072)
+
+
+def cpu_decode_sample(seconds=10.0, tokens=131072, max_seconds=30.0, seed=0):
+    """Time the oracle port (fp32 numpy, all host threads via BLAS) on a
+    bounded sample: one KV head group (8 query heads, GQA) over `tokens`
+    keys with fog.  Returns (GB/s of bf16-equivalent KV, sample text)."""
+    import numpy as np
+    from oracle import fog_oracle as O
+    rng = np.random.default_rng(seed)
+    G, D = 8, 128
+    q = rng.standard_normal((G, 1, D), dtype=np.float32)
+    k = rng.standard_normal((1, tokens, D), dtype=np.float32)
+    v = rng.standard_normal((1, tokens, D), dtype=np.float32)
+    w = O.fog_weights_from_clear_start(tokens, tokens - 8192, 0.5)
+    q, k, v = q[:, 0], k[0], v[0]
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        O.fog_decode_group_fp32(q, k, v, w)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or el >= max_seconds:
+            break
+    per = el / reps
+    gbs = tokens * D * 2 * 2 / per / 1e9
+    return gbs, per, (f"1 KV-head group (8 q heads, GQA) x {tokens} keys, fp32 numpy GEMM port "
+                      f"(oracle.fog_decode_group_fp32), {reps} reps in {el:.1f} s; GB/s of bf16-equivalent KV")
+
+
+def reference_arm(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    import numpy as np
+    from oracle import fog_oracle as O
+    threads = os.cpu_count() or 1
+    tokens = 65536
+    rng = np.random.default_rng(args.seed)
+    G, D = 8, 128
+    q = rng.standard_normal((G, 1, D), dtype=np.float32)
+    k = rng.standard_normal((1, tokens, D), dtype=np.float32)
+    v = rng.standard_normal((1, tokens, D), dtype=np.float32)
+    w = O.fog_weights_from_clear_start(tokens, tokens - 8192, 0.5)
+    q, k, v = q[:, 0], k[0], v[0]
+    step = lambda: O.fog_decode_group_fp32(q, k, v, w)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    per = el / args.steps
+    gbs = tokens * D * 2 * 2 / per / 1e9
+    c = CFG5
+    total_bytes = c["batch"] * c["ctx"] * c["kv_heads"] * c["head_dim"] * 4
+    ms_full = total_bytes / (gbs * 1e9) * 1e3
+    sample = (f"each step: 1 KV-head group (8 q heads) x {tokens} keys of the config-5 decode, fp32 numpy GEMM "
+              f"port of kessie_hip_kernels.py:577-593 (oracle.fog_decode_group_fp32); full-step time extrapolated "
+              f"by bytes")
+    line = {"impl": "reference", "metric": "fog-attn decode HBM GB/s (1M ctx, 70B shape)", "value": round(gbs, 3),
+            "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_full, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cp_decode_1m (BASELINE config 5)", **c, "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    if args.workload != "cp_decode_1m":
+        return run_aux_workload(args)
+    return run_cp_decode(args)
+
+
+def _setup_dist(args):
+    import torch
+    import torch.distributed as dist
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def run_cp_decode(args):
+    import torch
+    import torch.distributed as dist
+    from kessie_b200 import _lib
+    from kessie_b200.context_parallel import ContextParallelFogDecode, shard_range
+
+    rank, world, local = _setup_dist(args)
+    dev = torch.device("cuda", local)
+    c = CFG5
+    B, Hq, Hkv, D, N, W, ps = c["batch"], c["q_heads"], c["kv_heads"], c["head_dim"], c["ctx"], c["window"], c["page"]
+    start, end = shard_range(N, rank, world, ps)
+    n_loc = end - start
+    pages_loc = (n_loc + ps - 1) // ps
+    P = B * pages_loc
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed * 1000 + rank)
+    kv = torch.empty(P, ps, 2, Hkv, D, dtype=torch.bfloat16, device=dev)
+    chunk = max(1, (1 << 28) // (ps * 2 * Hkv * D))
+    for i in range(0, P, chunk):
+        kv[i:i + chunk].normal_(generator=g)
+    bt = torch.randperm(P, device=dev, generator=g).to(torch.int32).view(B, pages_loc).contiguous()
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(args.seed)
+    q = torch.randn(B, Hq, D, generator=gq, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    lens = torch.full((B,), n_loc, dtype=torch.int32, device=dev)
+    off = torch.full((B,), start, dtype=torch.int32, device=dev)
+    qpos = torch.full((B,), N - 1, dtype=torch.int32, device=dev)
+    cs = torch.full((B,), N - W, dtype=torch.int32, device=dev)
+    dec = ContextParallelFogDecode(B, Hq, D, torch.bfloat16, dev)
+    kc, vc = kv[:, :, 0], kv[:, :, 1]
+
+    def step(phase_events=None, i=0):
+        if phase_events is not None:
+            phase_events[0][i].record()
+        dec.local(q, kc, vc, bt, lens, off, qpos, cs, c["alpha"], 0, None, n_loc, phases=1)
+        if phase_events is not None:
+            phase_events[1][i].record()
+        dec.local(q, kc, vc, bt, lens, off, qpos, cs, c["alpha"], 0, None, n_loc, phases=2)
+        return dec.merge()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    K = args.steps
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.15)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start.record()
+    for i in range(K):
+        step((ev_a, ev_b), i)
+    t_end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks.stop()
+    el_ms = t_start.elapsed_time(t_end)
+    kern_ms = sum(ev_a[i].elapsed_time(ev_b[i]) for i in range(K)) / K
+    t = torch.tensor([el_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = t.item() / K
+
+    # parity spot check of the merged output against a local recompute is in the tests; here a sanity check only
+    out = dec.state.out
+    finite = bool(torch.isfinite(out.float()).all().item())
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        q_host = torch.empty(B, Hq, D, dtype=torch.bfloat16, pin_memory=True)
+        q_host.copy_(q.cpu())
+        out_host = torch.empty(B, Hq, D, dtype=torch.bfloat16, pin_memory=True)
+        q_dev = torch.empty_like(q)
+        K2 = max(10, K // 2)
+
+        def e2e_step():
+            q_dev.copy_(q_host, non_blocking=True)
+            o = dec(q_dev, kc, vc, bt, lens, off, qpos, cs, c["alpha"], 0, None, n_loc)
+            out_host.copy_(o, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        for _ in range(3):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K2):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1) / K2], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = te.item()
+        total_bytes = B * N * Hkv * D * 4
+        e2e = {"value": round(total_bytes / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+               "ms_per_step": round(e2e_ms, 4),
+               "h2d_bytes_per_step": int(q_host.numel() * 2 * world),
+               "d2h_bytes_per_step": int(out_host.numel() * 2 * world),
+               "api": "kessie_b200.context_parallel.ContextParallelFogDecode.__call__ (pinned host q in, out back)"}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        hbm, tf, tfs, peak_src = load_peaks()
+        total_bytes = B * N * Hkv * D * 4
+        local_bytes = B * n_loc * Hkv * D * 4
+        achieved = local_bytes / (kern_ms / 1e3) / 1e9
+        tr = load_traffic("fog_decode_kernel_bytes_per_kv_byte")
+        roof = {"bound": "hbm", "kernel": "fog_decode_kernel (split-KV paged decode)",
+                "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "peak_source": f"{peak_src} hbm_gbs (copy, burst)",
+                "algorithmic_bytes_per_launch": local_bytes, "kernel_ms": round(kern_ms, 4),
+                "traffic": (int(tr * local_bytes) if tr else None)}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            gbs, per, sample = cpu_decode_sample()
+            cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": sample}
+        line = {"metric": "fog-attn decode HBM GB/s (1M ctx, 70B shape; per-step us in ms_per_step)",
+                "value": round(total_bytes / (ms_step / 1e3) / 1e9, 3), "unit": "GB/s", "n_gpus": world,
+                "steps": K, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4),
+                "us_per_step": round(ms_step * 1e3, 1), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v)",
+                "config": {"workload": "cp_decode_1m (BASELINE config 5)", **c,
+                           "kv_bytes_per_step": total_bytes, "l2": L2_NOTE, "parallelism": f"cp{world}",
+                           "shard_tokens_per_seq": n_loc},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": K * (2 if world == 1 else 3),
+                "gpu_launches_note": "per step: split-KV decode + chunk merge (+ LSE merge of ranks when N>1); NCCL all-gather not counted",
+                "clocks": clocks.summary(), "output_finite": finite, "library": _lib.loaded_path()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_aux_workload(args):
+    """Single-GPU measurements of the other configs (not bench lines)."""
+    import numpy as np
+    import torch
+    from kessie_b200 import ops
+    _setup_dist(args)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    hbm, tf, tfs, peak_src = load_peaks()
+    res = {"workload": args.workload}
+
+    def timeit(fn, K):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+        for a, b in evs:
+            a.record(); fn(); b.record()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / K
+
+    if args.workload in ("decode_cfg3", "decode_128k"):
+        c = CFG3
+        B, Hq, Hkv, D, ps = c["batch"], c["q_heads"], c["kv_heads"], c["head_dim"], c["page"]
+        rng = np.random.default_rng(3)
+        lens = (np.full(B, 131072) if args.workload == "decode_128k" else rng.integers(c["lo"], c["hi"] + 1, B))
+        need = [(int(n) + ps - 1) // ps for n in lens]
+        P = sum(need)
+        kv = torch.empty(P, ps, 2, Hkv, D, dtype=torch.bfloat16, device=dev)
+        kv.normal_().mul_(1 / math.sqrt(128))
+        perm = torch.randperm(P, device=dev).to(torch.int32)
+        maxp = max(need)
+        bt = torch.zeros(B, maxp, dtype=torch.int32, device=dev)
+        o = 0
+        for b, k in enumerate(need):
+            bt[b, :k] = perm[o:o + k]; o += k
+        sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+        cs = sl - c["window"]
+        q = (torch.randn(B, Hq, D, device=dev) / math.sqrt(128)).to(torch.bfloat16)
+        out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
+        ms = timeit(lambda: ops.paged_fog_decode(q, kv[:, :, 0], kv[:, :, 1], bt, sl, clear_start=cs, fog_alpha=0.5,
+                                                 max_seq_len=maxp * ps, out=out), args.steps)
+        byts = int(sum(lens)) * Hkv * D * 4
+        res.update(ms_per_step=ms, us_per_step=ms * 1e3, kv_bytes=byts, GBs=byts / ms / 1e6,
+                   frac_of_hbm=byts / ms / 1e6 / hbm, total_tokens=int(sum(lens)))
+    elif args.workload == "page_ops":
+        P, ps, H, D = 8192, 16, 8, 128
+        kv = torch.randn(P, ps, 2, H, D, device=dev, dtype=torch.bfloat16)
+        perm = np.random.default_rng(2).permutation(P)
+        pos = torch.from_numpy((16 * perm).astype(np.int32)).to(dev)
+        valid = torch.ones(P, dtype=torch.int8, device=dev)
+        cnt, ids = ops.page_evict(valid, pos, 32768)
+        n = cnt.item()
+        ev = ids[:n].clone()
+        Kst, Vst = ops.page_gather(kv, ev)
+        ms_g = timeit(lambda: ops.page_gather(kv, ev, out_keys=Kst, out_values=Vst), args.steps)
+        oldpos = (pos[ev.long()].view(-1, 1) + torch.arange(16, device=dev, dtype=torch.int32)).reshape(-1)
+        newpos = torch.arange(131072, 131072 + n * 16, device=dev, dtype=torch.int32)
+        ms_r = timeit(lambda: ops.rope_remap(Kst, oldpos, newpos, 500000.0), args.steps)
+        free = torch.from_numpy(np.random.default_rng(22).permutation(ev.cpu().numpy())).to(dev)
+        ms_i = timeit(lambda: ops.page_insert(kv, Kst, Vst, free, conv_pos=131072, orig_positions=oldpos,
+                                              rope_theta=500000.0), args.steps)
+
+        def ev_step():
+            valid.fill_(1)
+            ops.page_evict(valid, pos, 32768)
+        ms_e = timeit(ev_step, args.steps)
+        res.update(evicted=n, gather_ms=ms_g, gather_GBs=268435456 / ms_g / 1e6, remap_ms=ms_r,
+                   remap_GBs=134217728 / ms_r / 1e6, insert_remap_ms=ms_i, insert_remap_GBs=268435456 / ms_i / 1e6,
+                   evict_plus_refill_us=ms_e * 1e3, hbm_peak=hbm)
+    elif args.workload == "prefill":
+        Hq, Hkv, D, ps, T, Nk = 32, 8, 128, 16, 8192, 262144
+        P = Nk // ps
+        kv = torch.randn(P, ps, 2, Hkv, D, device=dev, dtype=torch.bfloat16)
+        bt = torch.randperm(P, device=dev).to(torch.int32)[None]
+        q = torch.randn(1, T, Hq, D, device=dev, dtype=torch.bfloat16)
+        kl = torch.tensor([Nk], dtype=torch.int32, device=dev)
+        cs = torch.tensor([Nk - 4096], dtype=torch.int32, device=dev)
+        out = torch.empty_like(q)
+        ms = timeit(lambda: ops.paged_fog_prefill(q, kv[:, :, 0], kv[:, :, 1], bt, kl, clear_start=cs, fog_alpha=0.5,
+                                                  out=out), max(3, args.steps // 20))
+        flops = 4 * D * Hq * (T * (Nk - T) + T * (T + 1) // 2)
+        res.update(ms=ms, tflops=flops / ms / 1e9, frac_of_bf16_peak=flops / ms / 1e9 / tf, flops=flops)
+    print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

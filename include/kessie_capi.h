@@ -178,6 +178,13 @@ int kessie_page_gather_v2(const void* kv_cache, int dtype, int64_t page_stride,
                           int num_heads, int head_dim, void* out_keys, void* out_values,
                           void* stream);
 
+/* Fog weight vector fp32 [seq_len]: 1, then (j/max(cs-1,1))^fog_alpha for
+ * j < clear_start when fog_alpha > 0 and clear_start > 0.  Replaces
+ * kessie_build_fog_weights (kessie_hip_kernels.py:403-413); the caller
+ * passes clear_start = int(seq_len * (1.0 - fog_start)) computed on the host. */
+int kessie_build_fog_weights_v2(float* out, int seq_len, int clear_start, float fog_alpha,
+                                void* stream);
+
 /* Paged fog decode (one query token per sequence), split-KV over the page
  * table, GQA.  New entry point: the reference has no paged / GQA / decode
  * kernel; its semantics are kessie_fused_fog_attention_ref
@@ -242,6 +249,23 @@ int kessie_paged_fog_prefill_v2(const void* q, int64_t q_stride_b, int64_t q_str
                                 int num_kv_heads, int head_dim, int dtype, void* out,
                                 int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h,
                                 void* stream);
+
+/* kessie_paged_fog_decode_v2 split into its two phases: phases bit 0 runs
+ * the split-KV kernel (partials left in `workspace`), bit 1 the per-row
+ * merge into out / out_partial; 3 = both.  Both phases must see identical
+ * arguments.  For callers that time or overlap the phases separately. */
+int kessie_paged_fog_decode_ex_v2(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                  const void* k_cache, const void* v_cache, int64_t page_stride,
+                                  int64_t token_stride, int64_t head_stride, int num_pages,
+                                  int page_size, const int32_t* block_table,
+                                  int64_t block_table_stride, const int32_t* seq_lens,
+                                  const int32_t* kv_pos_offset, const int32_t* q_positions,
+                                  const int32_t* clear_start, float fog_alpha,
+                                  const float* fog_weights, int window_size, float sm_scale,
+                                  int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                  int max_seq_len, int dtype, void* out, float* out_partial,
+                                  void* workspace, size_t workspace_bytes, int phases,
+                                  void* stream);
 
 /* Log-sum-exp merge of S partial triples [S][rows][D+2] (split_stride
  * elements apart) -> out [rows, D] (out_dtype) and/or out_partial

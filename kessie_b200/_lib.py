@@ -55,6 +55,7 @@ SIGNATURES = {
                                       c_int64, c_int, c_int, c_int, I32P, P, I32P, c_int, I32P, I32P, c_float, P]),
     "kessie_page_gather_v2": (c_int, [P, c_int, c_int64, c_int64, c_int64, c_int64, c_int, c_int, I32P, c_int,
                                       c_int, c_int, P, P, P]),
+    "kessie_build_fog_weights_v2": (c_int, [P, c_int, c_int, c_float, P]),
     "kessie_paged_fog_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "kessie_paged_fog_decode_v2": (c_int, [P, c_int64, c_int64, P, P, c_int64, c_int64, c_int64, c_int, c_int,
                                            I32P, c_int64, I32P, I32P, I32P, I32P, c_float, P, c_int, c_float,
@@ -65,6 +66,9 @@ SIGNATURES = {
                                             c_int, I32P, c_int64, I32P, I32P, I32P, c_float, P, c_int64, c_int,
                                             c_int, c_float, c_int, c_int, c_int, c_int, c_int, c_int, P, c_int64,
                                             c_int64, c_int64, P]),
+    "kessie_paged_fog_decode_ex_v2": (c_int, [P, c_int64, c_int64, P, P, c_int64, c_int64, c_int64, c_int, c_int,
+                                              I32P, c_int64, I32P, I32P, I32P, I32P, c_float, P, c_int, c_float,
+                                              c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_size_t, c_int, P]),
     "kessie_lse_combine_v2": (c_int, [P, c_int, c_int64, c_int, c_int, P, c_int, P, P]),
 }
 

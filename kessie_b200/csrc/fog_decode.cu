@@ -439,12 +439,8 @@ template <int D, bool BF16, int NT>
 int launch_decode_t(const CUtensorMap& mk, const CUtensorMap& mv, const DecodeParams& p, cudaStream_t st) {
     auto kern = fog_decode_kernel<D, BF16, NT>;
     const int smem = Smem<D>::kAlloc;
-    static bool attr_set = false;   // per process; the attribute is per function, idempotent
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-            return check_launch("decode: set smem attribute");
-        attr_set = true;
-    }
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return check_launch("decode: set smem attribute");
     dim3 grid(p.max_chunks, p.Hkv, p.B);
     kern<<<grid, kThreads, smem, st>>>(mk, mv, p);
     return check_launch("paged_fog_decode");
@@ -462,13 +458,13 @@ extern "C" size_t kessie_paged_fog_decode_workspace_size(int batch, int num_q_he
     return make_plan(batch, num_q_heads, num_kv_heads, head_dim, max_seq_len).ws;
 }
 
-extern "C" int kessie_paged_fog_decode_v2(
+extern "C" int kessie_paged_fog_decode_ex_v2(
     const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache, const void* v_cache,
     int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
     const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens, const int32_t* kv_pos_offset,
     const int32_t* q_positions, const int32_t* clear_start, float fog_alpha, const float* fog_weights,
     int window_size, float sm_scale, int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_seq_len,
-    int dtype, void* out, float* out_partial, void* workspace, size_t workspace_bytes, void* stream) {
+    int dtype, void* out, float* out_partial, void* workspace, size_t workspace_bytes, int phases, void* stream) {
     if (dtype != KESSIE_DTYPE_BF16 && dtype != KESSIE_DTYPE_F16)
         return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_v2: dtype %d (f16/bf16 only)", dtype);
     if (head_dim != 64 && head_dim != 128)
@@ -479,8 +475,9 @@ extern "C" int kessie_paged_fog_decode_v2(
     if (G > 16) return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_v2: Hq/Hkv=%d > 16", G);
     if (page_size <= 0 || page_size % 16 || page_size > 256)
         return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_v2: page_size %d (multiple of 16, <= 256)", page_size);
-    if (!q || !k_cache || !v_cache || !block_table || !seq_lens || (!out && !out_partial) || num_pages <= 0 ||
-        max_seq_len < 0)
+    if (phases < 1 || phases > 3) return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: phases %d", phases);
+    if (!q || !k_cache || !v_cache || !block_table || !seq_lens || ((phases & 2) && !out && !out_partial) ||
+        num_pages <= 0 || max_seq_len < 0)
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: null pointer or bad size");
     if ((q_stride_h & 1) || (q_stride_b & 1) || (reinterpret_cast<uintptr_t>(q) & 3))
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: q rows must be 4-byte aligned");
@@ -493,14 +490,6 @@ extern "C" int kessie_paged_fog_decode_v2(
     if (pl.max_chunks > 65535 * 16) return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_v2: too many chunks");
 
     const bool bf16 = dtype == KESSIE_DTYPE_BF16;
-    CUtensorMap mk, mv;
-    CUresult r1 = encode_kv_tile_map(&mk, k_cache, bf16, head_dim, page_size, num_kv_heads, num_pages, token_stride,
-                                     head_stride, page_stride);
-    CUresult r2 = encode_kv_tile_map(&mv, v_cache, bf16, head_dim, page_size, num_kv_heads, num_pages, token_stride,
-                                     head_stride, page_stride);
-    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
-        return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: TMA descriptor rejected (%d/%d)", (int)r1, (int)r2);
-
     DecodeParams p;
     p.q = q; p.q_sb = q_stride_b; p.q_sh = q_stride_h;
     p.block_table = block_table; p.bt_stride = block_table_stride;
@@ -513,22 +502,49 @@ extern "C" int kessie_paged_fog_decode_v2(
     p.max_units = pl.max_units; p.cu = pl.cu; p.max_chunks = pl.max_chunks;
     p.part = static_cast<float*>(workspace);
     p.status = device_status_ptr();
-
     cudaStream_t st = as_stream(stream);
-    int rc;
-    const bool nt2 = G > 8;
-    if (head_dim == 128) {
-        if (bf16) rc = nt2 ? launch_decode_t<128, true, 2>(mk, mv, p, st) : launch_decode_t<128, true, 1>(mk, mv, p, st);
-        else rc = nt2 ? launch_decode_t<128, false, 2>(mk, mv, p, st) : launch_decode_t<128, false, 1>(mk, mv, p, st);
-    } else {
-        if (bf16) rc = nt2 ? launch_decode_t<64, true, 2>(mk, mv, p, st) : launch_decode_t<64, true, 1>(mk, mv, p, st);
-        else rc = nt2 ? launch_decode_t<64, false, 2>(mk, mv, p, st) : launch_decode_t<64, false, 1>(mk, mv, p, st);
+
+    if (phases & 1) {
+        CUtensorMap mk, mv;
+        CUresult r1 = encode_kv_tile_map(&mk, k_cache, bf16, head_dim, page_size, num_kv_heads, num_pages,
+                                         token_stride, head_stride, page_stride);
+        CUresult r2 = encode_kv_tile_map(&mv, v_cache, bf16, head_dim, page_size, num_kv_heads, num_pages,
+                                         token_stride, head_stride, page_stride);
+        if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
+            return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: TMA descriptor rejected (%d/%d)", (int)r1, (int)r2);
+        int rc;
+        const bool nt2 = G > 8;
+        if (head_dim == 128) {
+            if (bf16) rc = nt2 ? launch_decode_t<128, true, 2>(mk, mv, p, st) : launch_decode_t<128, true, 1>(mk, mv, p, st);
+            else rc = nt2 ? launch_decode_t<128, false, 2>(mk, mv, p, st) : launch_decode_t<128, false, 1>(mk, mv, p, st);
+        } else {
+            if (bf16) rc = nt2 ? launch_decode_t<64, true, 2>(mk, mv, p, st) : launch_decode_t<64, true, 1>(mk, mv, p, st);
+            else rc = nt2 ? launch_decode_t<64, false, 2>(mk, mv, p, st) : launch_decode_t<64, false, 1>(mk, mv, p, st);
+        }
+        if (rc) return rc;
     }
-    if (rc) return rc;
-    const int rows = batch * num_q_heads;
-    if (bf16) decode_combine_kernel<__nv_bfloat16><<<rows, head_dim, 0, st>>>(p, head_dim, (__nv_bfloat16*)out, out_partial);
-    else decode_combine_kernel<__half><<<rows, head_dim, 0, st>>>(p, head_dim, (__half*)out, out_partial);
-    return check_launch("paged_fog_decode combine");
+    if (phases & 2) {
+        const int rows = batch * num_q_heads;
+        if (bf16) decode_combine_kernel<__nv_bfloat16><<<rows, head_dim, 0, st>>>(p, head_dim, (__nv_bfloat16*)out, out_partial);
+        else decode_combine_kernel<__half><<<rows, head_dim, 0, st>>>(p, head_dim, (__half*)out, out_partial);
+        return check_launch("paged_fog_decode combine");
+    }
+    clear_error();
+    return 0;
+}
+
+extern "C" int kessie_paged_fog_decode_v2(
+    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+    int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
+    const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens, const int32_t* kv_pos_offset,
+    const int32_t* q_positions, const int32_t* clear_start, float fog_alpha, const float* fog_weights,
+    int window_size, float sm_scale, int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_seq_len,
+    int dtype, void* out, float* out_partial, void* workspace, size_t workspace_bytes, void* stream) {
+    return kessie_paged_fog_decode_ex_v2(q, q_stride_b, q_stride_h, k_cache, v_cache, page_stride, token_stride,
+                                         head_stride, num_pages, page_size, block_table, block_table_stride, seq_lens,
+                                         kv_pos_offset, q_positions, clear_start, fog_alpha, fog_weights, window_size,
+                                         sm_scale, batch, num_q_heads, num_kv_heads, head_dim, max_seq_len, dtype, out,
+                                         out_partial, workspace, workspace_bytes, 3, stream);
 }
 
 extern "C" int kessie_lse_combine_v2(const float* partials, int num_splits, int64_t split_stride, int rows,

@@ -503,6 +503,15 @@ __global__ void page_gather_scalar_kernel(const T* __restrict__ cache, PageGeom 
     if (ov) ov[gid] = bad ? from_f32<T>(0.f) : cache[src + g.kv_stride];
 }
 
+// kessie_hip_kernels.py:408-412: w = 1, then (j / max(cs-1,1))^alpha for j < cs.
+__global__ void fog_weights_kernel(float* __restrict__ w, int n, int cs, float alpha) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    float v = 1.f;
+    if (alpha > 0.f && cs > 0 && j < cs) v = powf(__fdiv_rn((float)j, (float)max(cs - 1, 1)), alpha);
+    w[j] = v;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <typename T>
@@ -684,6 +693,13 @@ int kessie_page_gather_v2(const void* kv_cache, int dtype, int64_t page_stride, 
         case KESSIE_DTYPE_BF16: return launch_gather<__nv_bfloat16>(kv_cache, g, page_ids, num_gather, out_keys, out_values, st);
         default: return launch_gather<float>(kv_cache, g, page_ids, num_gather, out_keys, out_values, st);
     }
+}
+
+int kessie_build_fog_weights_v2(float* out, int seq_len, int clear_start, float fog_alpha, void* stream) {
+    if (seq_len < 0 || (seq_len > 0 && !out)) return set_error(KESSIE_ERR_ARG, "build_fog_weights_v2: bad arguments");
+    if (seq_len == 0) { clear_error(); return 0; }
+    fog_weights_kernel<<<(seq_len + 255) / 256, 256, 0, as_stream(stream)>>>(out, seq_len, clear_start, fog_alpha);
+    return check_launch("build_fog_weights");
 }
 
 }  // extern "C"

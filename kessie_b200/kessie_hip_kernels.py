@@ -1,0 +1,251 @@
+"""Drop-in replacement for the reference module ``kessie_hip_kernels``.
+
+Same public names, signatures and defaults as kessie_hip_kernels.py:367-606;
+every accelerated entry point runs on libkessie_cuda.so (sm_100a) and there is
+no Triton or CPU path behind them -- if the library is missing, the call
+raises ``KessieLibraryError``.
+
+    kessie_fused_fog_attention   kessie_hip_kernels.py:367-400
+    kessie_windowed_attention    kessie_hip_kernels.py:416-440
+    kessie_build_fog_weights     kessie_hip_kernels.py:403-413
+    kessie_rope_remap            kessie_hip_kernels.py:443-477
+    KeSSiePagedKVCache           kessie_hip_kernels.py:484-570
+    *_ref                        kessie_hip_kernels.py:577-606 (reference math, torch)
+
+Differences from the reference, all deliberate:
+  * inputs may be fp16 or bf16, with Hq a multiple of Hkv (GQA);
+  * ``kessie_rope_remap`` works in place on strided K without copying and
+    rotates every element (the reference's Triton grid rotates only the
+    first ceil(T*H*half/256) pairs, kessie_hip_kernels.py:313-316,466-467);
+  * ``KeSSiePagedKVCache.evict_before`` runs the eviction rule of the HIP
+    kernel (kessie_kernels_v2.hip:403-406) with an ordered device compaction,
+    reproducing the reference's free-list order with one device->host copy
+    instead of one sync per page (kessie_hip_kernels.py:535-538).
+"""
+
+from __future__ import annotations
+
+import logging
+import math
+from typing import List, Optional, Tuple
+
+import torch
+
+from . import ops
+from ._lib import KessieLibraryError  # noqa: F401  (re-exported for callers)
+
+logger = logging.getLogger("KeSSie.B200")
+
+HAS_KESSIE_CUDA = True
+
+
+def _device_of(t: torch.Tensor) -> torch.device:
+    if not t.is_cuda:
+        raise ValueError(f"KeSSie B200 kernels need CUDA tensors, got {t.device}")
+    return t.device
+
+
+# =============================================================================
+# Attention
+# =============================================================================
+
+def kessie_fused_fog_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, fog_weights: torch.Tensor,
+                               window_size: int = 0, causal: bool = True,
+                               sm_scale: Optional[float] = None) -> torch.Tensor:
+    """Flash attention with fused fog decay on V (kessie_hip_kernels.py:367-400).
+
+    q: [Z, Hq, N, D]; k, v: [Z, Hkv, N, D] (fp16 or bf16); fog_weights: [N]
+    float32, 1.0 = clear, < 1.0 = fogged."""
+    Z, H, N, D = q.shape
+    assert fog_weights.shape == (N,)
+    _device_of(q)
+    return ops.fog_attention(q.contiguous(), k.contiguous(), v.contiguous(), fog_weights.to(q.device),
+                             window_size, causal, sm_scale)
+
+
+def kessie_windowed_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window_size: int = 0,
+                              causal: bool = True, sm_scale: Optional[float] = None) -> torch.Tensor:
+    """Windowed flash attention without fog (kessie_hip_kernels.py:416-440)."""
+    _device_of(q)
+    return ops.fog_attention(q.contiguous(), k.contiguous(), v.contiguous(), None, window_size, causal, sm_scale)
+
+
+def kessie_build_fog_weights(seq_len: int, fog_alpha: float = 0.5, fog_start: float = 0.5,
+                             device: torch.device = None) -> torch.Tensor:
+    """Fog decay weights, 1.0 = clear, < 1.0 = fogged (kessie_hip_kernels.py:403-413).
+
+    clear_start = int(seq_len * (1.0 - fog_start)) is evaluated here in Python
+    float64, exactly as the reference; the vector is built on the GPU and
+    returned on ``device`` (the current CUDA device when None is given, as
+    there is no CPU path)."""
+    clear_start = int(seq_len * (1.0 - fog_start))
+    dev = torch.device(device) if device is not None else None
+    build_dev = dev if (dev is not None and dev.type == "cuda") else None
+    w = ops.build_fog_weights(seq_len, clear_start, fog_alpha, build_dev)
+    if dev is not None and dev.type != "cuda":
+        w = w.to(dev)
+    return w
+
+
+def kessie_rope_remap(k_tensor: torch.Tensor, orig_positions: torch.Tensor, target_positions: torch.Tensor,
+                      rope_theta: float = 10000.0) -> torch.Tensor:
+    """Re-rotate K from original to target RoPE positions, in place
+    (kessie_hip_kernels.py:443-477).  k_tensor: [T, H, D] with D contiguous."""
+    _device_of(k_tensor)
+    return ops.rope_remap(k_tensor, orig_positions.to(k_tensor.device), target_positions.to(k_tensor.device),
+                          rope_theta)
+
+
+# =============================================================================
+# KeSSiePagedKVCache
+# =============================================================================
+
+class KeSSiePagedKVCache:
+    """Paged KV cache with KeSSie fog-of-war semantics (kessie_hip_kernels.py:484-570).
+
+    Same state and methods as the reference: ``kv_data`` [L, P, ps, 2, H, D],
+    ``page_positions`` int32 [P], ``page_valid`` int8 [P], the host free list
+    ``free_pages`` (source of truth for allocation order: pops from the end),
+    ``total_evictions`` / ``total_insertions`` and ``get_stats()``.
+    Additionally keeps ``page_allocated`` int8 [P] on the device, the mirror of
+    "not in free_pages" that the device eviction needs to reproduce the
+    reference's free-list rebuild."""
+
+    def __init__(self, num_pages, page_size, num_layers, num_heads, head_dim, device, dtype=torch.float16):
+        self.num_pages = num_pages
+        self.page_size = page_size
+        self.num_layers = num_layers
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("KeSSiePagedKVCache on B200 lives on a CUDA device")
+        self.dtype = dtype
+        self.kv_data = torch.zeros(num_layers, num_pages, page_size, 2, num_heads, head_dim, device=self.device,
+                                   dtype=dtype)
+        self.page_positions = torch.zeros(num_pages, dtype=torch.int32, device=self.device)
+        self.page_valid = torch.zeros(num_pages, dtype=torch.int8, device=self.device)
+        self.page_allocated = torch.zeros(num_pages, dtype=torch.int8, device=self.device)
+        self.free_pages: List[int] = list(range(num_pages))
+        self.total_evictions = 0
+        self.total_insertions = 0
+        self._host_buf = torch.empty(num_pages + 1, dtype=torch.int32, pin_memory=True)
+        logger.info(f"KeSSiePagedKVCache: {num_pages}p x {page_size}t, {num_layers}L x {num_heads}H x {head_dim}D, "
+                    f"VRAM={self.vram_bytes / 1e9:.2f} GB")
+
+    @property
+    def vram_bytes(self):
+        return self.kv_data.nelement() * self.kv_data.element_size()
+
+    @property
+    def active_pages(self):
+        return self.num_pages - len(self.free_pages)
+
+    @property
+    def active_tokens(self):
+        return self.active_pages * self.page_size
+
+    def allocate_pages(self, n):
+        """Pop n page ids from the END of free_pages (kessie_hip_kernels.py:520-524)."""
+        if len(self.free_pages) < n:
+            return None
+        ids = [self.free_pages.pop() for _ in range(n)]
+        t = torch.tensor(ids, dtype=torch.int32, device=self.device)
+        if n:
+            self.page_allocated[t.long()] = 1
+        return t
+
+    def evict_before(self, position):
+        """Evict valid pages whose position < `position`; freed pages are
+        appended to free_pages in ascending page order
+        (kessie_hip_kernels.py:526-540, rule kessie_kernels_v2.hip:403-406)."""
+        cnt, ids = ops.page_evict(self.page_valid, self.page_positions, int(position), self.page_allocated)
+        # one device->host copy of [count, ids...]
+        self._host_buf[0:1].copy_(cnt, non_blocking=True)
+        self._host_buf[1:1 + self.num_pages].copy_(ids[:self.num_pages], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        n = int(self._host_buf[0])
+        if n:
+            self.free_pages.extend(self._host_buf[1:1 + n].tolist())
+        self.total_evictions += n
+        return n
+
+    def insert_probe_kv(self, layer_idx, keys, values, conv_position, orig_positions=None,
+                        rope_theta: float = 10000.0):
+        """Insert probe KV [T, H, D] into freshly allocated pages
+        (kessie_hip_kernels.py:542-556) with one device copy kernel.
+        With ``orig_positions`` (int32 [T]) the keys are also re-rotated from
+        their original positions to conv_position + t (the recall path,
+        fused insert + RoPE remap)."""
+        num_tokens = keys.shape[0]
+        pages_needed = (num_tokens + self.page_size - 1) // self.page_size
+        page_ids = self.allocate_pages(pages_needed)
+        if page_ids is None:
+            return False
+        k = keys.to(device=self.device, dtype=self.dtype)
+        v = values.to(device=self.device, dtype=self.dtype)
+        if k.stride(-1) != 1 or k.stride() != v.stride():
+            k, v = k.contiguous(), v.contiguous()
+        ops.page_insert(self.kv_data[layer_idx], k, v, page_ids, self.page_valid, self.page_positions,
+                        int(conv_position), orig_positions=orig_positions, rope_theta=rope_theta)
+        self.total_insertions += num_tokens
+        return True
+
+    def get_layer_kv(self, layer_idx):
+        """K, V [n_valid * ps, H, D] of the valid pages in physical-page order
+        (kessie_hip_kernels.py:558-564)."""
+        cnt, ids = ops.list_valid_pages(self.page_valid)
+        n = int(cnt.item())
+        if n == 0:
+            empty = torch.empty(0, self.num_heads, self.head_dim, device=self.device, dtype=self.dtype)
+            return empty, empty.clone()
+        return ops.page_gather(self.kv_data[layer_idx], ids[:n])
+
+    def get_stats(self):
+        return {"total_pages": self.num_pages, "active_pages": self.active_pages,
+                "free_pages": len(self.free_pages), "active_tokens": self.active_tokens,
+                "vram_gb": self.vram_bytes / 1e9,
+                "total_evictions": self.total_evictions, "total_insertions": self.total_insertions}
+
+
+# =============================================================================
+# Reference implementations (kessie_hip_kernels.py:577-606), torch math.
+# Kept for API compatibility with the reference module (its tests compare
+# against them); no accelerated entry point above calls them.
+# =============================================================================
+
+def kessie_windowed_attention_ref(q, k, v, window_size=0, causal=True, sm_scale=None):
+    Z, H, N, D = q.shape
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    scores = torch.matmul(q, k.transpose(-2, -1)) * sm_scale
+    pos = torch.arange(N, device=q.device)
+    dist = pos[:, None] - pos[None, :]
+    keep = torch.ones(N, N, dtype=torch.bool, device=q.device)
+    if causal:
+        keep &= dist >= 0
+    if window_size > 0:
+        keep &= (dist >= 0) & (dist < window_size)
+    scores = scores.masked_fill(~keep, float("-inf"))
+    return torch.matmul(torch.softmax(scores, dim=-1), v)
+
+
+def kessie_fused_fog_attention_ref(q, k, v, fog_weights, window_size=0, causal=True, sm_scale=None):
+    return kessie_windowed_attention_ref(q, k, v * fog_weights[None, None, :, None], window_size, causal, sm_scale)
+
+
+def _rope_remap_ref(k_tensor, orig_positions, target_positions, rope_theta=10000.0):
+    """Rotate-half re-rotation in fp32 from the loaded pair (the HIP kernel's
+    arithmetic, kessie_kernels_v2.hip:697-706).  The reference's torch version
+    reads the first half back after overwriting it when K is fp32
+    (``.float()`` is a view there); this one always rotates from copies."""
+    num_tokens, num_heads, head_dim = k_tensor.shape
+    half_dim = head_dim // 2
+    freqs = 1.0 / (rope_theta ** (torch.arange(half_dim, dtype=torch.float32, device=k_tensor.device) / half_dim))
+    delta = torch.outer((target_positions - orig_positions).float(), freqs)
+    cos_d, sin_d = delta.cos()[:, None, :], delta.sin()[:, None, :]
+    k1 = k_tensor[:, :, :half_dim].float().clone()
+    k2 = k_tensor[:, :, half_dim:].float().clone()
+    k_tensor[:, :, :half_dim] = (k1 * cos_d - k2 * sin_d).to(k_tensor.dtype)
+    k_tensor[:, :, half_dim:] = (k1 * sin_d + k2 * cos_d).to(k_tensor.dtype)
+    return k_tensor

@@ -100,6 +100,18 @@ def rope_remap(k: torch.Tensor, orig_positions, target_positions, rope_theta: fl
     return k
 
 
+# --------------------------------------------------------------------- fog weights
+def build_fog_weights(seq_len: int, clear_start: int, fog_alpha: float, device=None, stream=None) -> torch.Tensor:
+    """fp32 [seq_len] fog weights on a CUDA device (kessie_hip_kernels.py:403-413)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if dev.type != "cuda":
+        raise ValueError("fog weights are built on a CUDA device")
+    w = torch.empty(int(seq_len), dtype=torch.float32, device=dev)
+    _lib.check(_lib.load().kessie_build_fog_weights_v2(_p(w) if seq_len else None, int(seq_len), int(clear_start),
+                                                       float(fog_alpha), _stream(stream)), "build_fog_weights")
+    return w
+
+
 # --------------------------------------------------------------------- pages
 def kv_layout_strides(kv: torch.Tensor, layout: str = "kessie") -> Tuple[int, int, int, int, int, int, int, int]:
     """(page, token, kv, head strides, num_pages, page_size, heads, head_dim)."""
@@ -198,7 +210,7 @@ def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                      window_size: int = 0, sm_scale: Optional[float] = None, kv_pos_offset=None,
                      q_positions=None, max_seq_len: Optional[int] = None, out: Optional[torch.Tensor] = None,
                      out_partial: Optional[torch.Tensor] = None, want_out: bool = True, stream=None,
-                     ws: Optional[torch.Tensor] = None):
+                     ws: Optional[torch.Tensor] = None, phases: int = 3):
     """Paged fog decode: q [B, Hq, D]; k_cache / v_cache [P, ps, Hkv, D]
     views (any page/token/head strides, D contiguous); block_table [B, maxP]
     int32; seq_lens [B] int32.  Returns out [B, Hq, D] (q.dtype) and, if
@@ -236,12 +248,12 @@ def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     need = lib.kessie_paged_fog_decode_workspace_size(B, Hq, Hkv, D, int(max_seq_len), ps)
     if ws is None:
         ws = workspace(need, q.device, "decode")
-    _lib.check(lib.kessie_paged_fog_decode_v2(
+    _lib.check(lib.kessie_paged_fog_decode_ex_v2(
         q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
         k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), sl.data_ptr(), _p(off), _p(qp),
         _p(cs), float(fog_alpha), _p(fw), int(window_size), float(sm_scale), B, Hq, Hkv, D, int(max_seq_len),
-        dtype_code(q), _p(out if want_out else None), _p(out_partial), ws.data_ptr(), ws.numel(), _stream(stream)),
-        "paged_fog_decode")
+        dtype_code(q), _p(out if want_out else None), _p(out_partial), ws.data_ptr(), ws.numel(), int(phases),
+        _stream(stream)), "paged_fog_decode")
     return out
 
 
@@ -259,4 +271,72 @@ def lse_combine(partials: torch.Tensor, out: Optional[torch.Tensor] = None, out_
     lib = _lib.load()
     _lib.check(lib.kessie_lse_combine_v2(partials.data_ptr(), S, partials.stride(0), rows, D, _p(out),
                                          dtype_code(out), _p(out_partial), _stream(stream)), "lse_combine")
+    return out
+
+
+# --------------------------------------------------------------------- prefill / dense
+def fog_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, fog_weights: Optional[torch.Tensor] = None,
+                  window_size: int = 0, causal: bool = True, sm_scale: Optional[float] = None,
+                  out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Dense fog attention: q [B, Hq, N, D], k/v [B, Hkv, N, D] (f16/bf16,
+    contiguous), fog_weights fp32 [N] or None (kessie_hip_kernels.py:367-440)."""
+    _need_cuda(q, k, v, fog_weights)
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("q, k, v must be contiguous [B, H, N, D]")
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    if k.shape != (B, Hkv, N, D) or v.shape != k.shape:
+        raise ValueError("k/v must be [B, Hkv, N, D] matching q")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    fw = None
+    if fog_weights is not None:
+        if fog_weights.numel() != N:
+            raise ValueError("fog_weights must have N entries")
+        fw = fog_weights.float().contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    lib = _lib.load()
+    _lib.check(lib.kessie_fog_attention_v2(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dtype_code(q),
+                                           _p(fw), float(sm_scale), B, Hq, Hkv, N, D, int(window_size),
+                                           1 if causal else 0, _stream(stream)), "fog_attention")
+    return out
+
+
+def paged_fog_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                      kv_lens, q_start=None, clear_start=None, fog_alpha: float = 0.5, fog_weights=None,
+                      window_size: int = 0, causal: bool = True, sm_scale: Optional[float] = None,
+                      out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Chunked prefill: q [B, T, Hq, D] (query t of sequence b at position
+    q_start[b] + t, default kv_lens[b] - T) over k_cache / v_cache
+    [P, ps, Hkv, D] views through block_table [B, maxP]."""
+    _need_cuda(q, k_cache, v_cache, block_table)
+    B, T, Hq, D = q.shape
+    P, ps, Hkv, Dk = k_cache.shape
+    if Dk != D or v_cache.shape != k_cache.shape or v_cache.stride() != k_cache.stride():
+        raise ValueError("k_cache/v_cache must be matching [P, ps, Hkv, D] views")
+    if q.stride(3) != 1 or k_cache.stride(3) != 1:
+        raise ValueError("head_dim must be contiguous")
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    if bt.stride(1) != 1:
+        bt = bt.contiguous()
+    kl = _i32(kv_lens, q.device)
+    qs = _i32(q_start, q.device)
+    cs = _i32(clear_start, q.device)
+    fw = None
+    fw_sb = 0
+    if fog_weights is not None:
+        fw = fog_weights.float().contiguous()
+        fw_sb = fw.shape[-1] if fw.dim() == 2 else 0
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    lib = _lib.load()
+    _lib.check(lib.kessie_paged_fog_prefill_v2(
+        q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k_cache.data_ptr(), v_cache.data_ptr(),
+        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), kl.data_ptr(),
+        _p(qs), _p(cs), float(fog_alpha), _p(fw), fw_sb, int(window_size), 1 if causal else 0, float(sm_scale),
+        B, T, Hq, Hkv, D, dtype_code(q), out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+        _stream(stream)), "paged_fog_prefill")
     return out

@@ -23,7 +23,7 @@ __all__ = [
     "windowed_attention", "fused_fog_attention", "fog_attention_rows",
     "rope_freqs", "rope_remap", "rope_remap_fp32_inplace_reference", "page_evict", "PagedKVCacheOracle",
     "page_gather", "paged_fog_decode", "paged_fog_prefill", "lse_combine",
-    "partials_from_rows",
+    "partials_from_rows", "fog_decode_group_fp32",
 ]
 
 
@@ -134,7 +134,7 @@ def fused_fog_attention(q, k, v, fog_weights, window_size: int = 0, causal: bool
 
 def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal: bool = True,
                        sm_scale: Optional[float] = None, k_pos=None,
-                       return_partials: bool = False):
+                       return_partials: bool = False, dtype=np.float64):
     """Query-offset, GQA restatement of kessie_hip_kernels.py:577-593.
 
     q: [Hq, Nq, D] at absolute positions q_pos[Nq]; k, v: [Hkv, N, D] at
@@ -142,10 +142,11 @@ def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal:
     h reads KV head h // (Hq // Hkv).  Same mask, softmax and ``@ (v*fog)``
     as the square reference; validated against its last rows.
     With return_partials, also returns (m, l, O_unnormalised) in natural-log
-    units for the LSE combine."""
-    q = np.asarray(q, dtype=np.float64)
-    k = np.asarray(k, dtype=np.float64)
-    v = np.asarray(v, dtype=np.float64)
+    units for the LSE combine.  dtype=np.float32 evaluates in fp32 like the
+    reference's torch path (used for the timed CPU baseline)."""
+    q = np.asarray(q, dtype=dtype)
+    k = np.asarray(k, dtype=dtype)
+    v = np.asarray(v, dtype=dtype)
     Hq, Nq, D = q.shape
     Hkv, N, _ = k.shape
     g = Hq // Hkv
@@ -154,13 +155,13 @@ def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal:
     if k_pos is None:
         k_pos = np.arange(N)
     ok = _mask(np.asarray(q_pos), np.asarray(k_pos), window_size, causal)
-    w = np.ones(N) if fog_w is None else np.asarray(fog_w, dtype=np.float64)
-    out = np.empty((Hq, Nq, D))
-    ms = np.empty((Hq, Nq)); ls = np.empty((Hq, Nq)); os_ = np.empty((Hq, Nq, D))
+    w = np.ones(N, dtype=dtype) if fog_w is None else np.asarray(fog_w, dtype=dtype)
+    out = np.empty((Hq, Nq, D), dtype=dtype)
+    ms = np.empty((Hq, Nq), dtype=dtype); ls = np.empty((Hq, Nq), dtype=dtype); os_ = np.empty((Hq, Nq, D), dtype=dtype)
     for h in range(Hq):
         kh = h // g
-        s = (q[h] @ k[kh].T) * sm_scale
-        s = np.where(ok, s, -np.inf)
+        s = (q[h] @ k[kh].T) * dtype(sm_scale)
+        s = np.where(ok, s, dtype(-np.inf))
         m = s.max(axis=-1, keepdims=True)
         mf = np.where(np.isfinite(m), m, 0.0)
         p = np.exp(s - mf)
@@ -172,6 +173,24 @@ def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal:
     if return_partials:
         return out, (ms, ls, os_)
     return out
+
+
+def fog_decode_group_fp32(q: np.ndarray, k: np.ndarray, v: np.ndarray, w: np.ndarray,
+                          sm_scale: Optional[float] = None) -> np.ndarray:
+    """Last-row (decode) evaluation of kessie_hip_kernels.py:577-593 for the
+    G query heads of one KV head, in fp32 like the reference's torch path:
+    q [G, D]; k, v [N, D] (all N keys visible); w [N] fog weights.  Batched
+    as two GEMMs (scores [G, N], then P @ (V * w)); used as the timed CPU
+    baseline."""
+    q = np.asarray(q, np.float32); k = np.asarray(k, np.float32); v = np.asarray(v, np.float32)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    s = (q @ k.T) * np.float32(sm_scale)
+    s -= s.max(axis=1, keepdims=True)
+    np.exp(s, out=s)
+    l = s.sum(axis=1, keepdims=True)
+    vw = v * np.asarray(w, np.float32)[:, None]
+    return (s @ vw) / l
 
 
 def lse_combine(ms: np.ndarray, ls: np.ndarray, os_: np.ndarray) -> np.ndarray:

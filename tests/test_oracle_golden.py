@@ -170,3 +170,13 @@ def test_hip_evict_kats():
     assert O.page_evict(valid, pos, 8192)[1] == 64
     valid2 = np.zeros(64, np.int8); valid2[:] = 1; pos2 = np.arange(64, dtype=np.int32) * 128
     assert O.page_evict(valid2, pos2, 4096)[1] == 32
+
+
+def test_group_decode_fp32_equals_rows():
+    rng = np.random.default_rng(9)
+    q = rng.standard_normal((8, 128)).astype(np.float32)
+    k = rng.standard_normal((3000, 128)).astype(np.float32); v = rng.standard_normal((3000, 128)).astype(np.float32)
+    w = O.fog_weights_from_clear_start(3000, 2000, 0.5)
+    a = O.fog_decode_group_fp32(q, k, v, w)
+    b = O.fog_attention_rows(q[:, None], k[None], v[None], np.array([2999]), w)[:, 0]
+    np.testing.assert_allclose(a, b, atol=1e-5)
