@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["kessie", "reference"], default="kessie")
     ap.add_argument("--workload", default="cp_decode_1m",
-                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "page_ops", "prefill"])
+                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "page_ops", "prefill"])
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -408,11 +408,14 @@ def run_aux_workload(args):
         torch.cuda.synchronize()
         return sum(a.elapsed_time(b) for a, b in evs) / K
 
-    if args.workload in ("decode_cfg3", "decode_128k"):
+    if args.workload in ("decode_cfg3", "decode_128k", "decode_small"):
         c = CFG3
         B, Hq, Hkv, D, ps = c["batch"], c["q_heads"], c["kv_heads"], c["head_dim"], c["page"]
         rng = np.random.default_rng(3)
-        lens = (np.full(B, 131072) if args.workload == "decode_128k" else rng.integers(c["lo"], c["hi"] + 1, B))
+        if args.workload == "decode_small":        # profiling size: 2.1 GB of KV (> L2)
+            B = 4
+        lens = (np.full(B, 131072) if args.workload in ("decode_128k", "decode_small")
+                else rng.integers(c["lo"], c["hi"] + 1, B))
         need = [(int(n) + ps - 1) // ps for n in lens]
         P = sum(need)
         kv = torch.empty(P, ps, 2, Hkv, D, dtype=torch.bfloat16, device=dev)
