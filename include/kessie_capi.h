@@ -267,6 +267,35 @@ int kessie_paged_fog_decode_ex_v2(const void* q, int64_t q_stride_b, int64_t q_s
                                   void* workspace, size_t workspace_bytes, int phases,
                                   void* stream);
 
+/* Size of the scratch array built into the library for
+ * kessie_paged_fog_decode_noalloc_v2 (16 MiB per GPU that loads the library). */
+#define KESSIE_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+
+/* Paged fog decode for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Same arguments and results as
+ * kessie_paged_fog_decode_v2 except that there is no workspace argument: the
+ * split-KV scratch is a fixed KESSIE_NOALLOC_SCRATCH_BYTES array inside the
+ * library, so code whose device allocator is fixed or owned by another
+ * runtime can still decode.  Allocates nothing (no cudaMalloc / cudaFree).
+ *   - Shapes whose scratch (kessie_paged_fog_decode_workspace_size) exceeds
+ *     the array are rejected with KESSIE_ERR_WORKSPACE and a message.
+ *   - The first call on each device looks the array's address up
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call uses the same array: calls that can overlap on the GPU race
+ *     and must be ordered by the caller.  Leftover contents from a previous
+ *     call are never read. */
+int kessie_paged_fog_decode_noalloc_v2(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                       const void* k_cache, const void* v_cache,
+                                       int64_t page_stride, int64_t token_stride,
+                                       int64_t head_stride, int num_pages, int page_size,
+                                       const int32_t* block_table, int64_t block_table_stride,
+                                       const int32_t* seq_lens, const int32_t* kv_pos_offset,
+                                       const int32_t* q_positions, const int32_t* clear_start,
+                                       float fog_alpha, const float* fog_weights, int window_size,
+                                       float sm_scale, int batch, int num_q_heads,
+                                       int num_kv_heads, int head_dim, int max_seq_len, int dtype,
+                                       void* out, float* out_partial, void* stream);
+
 /* Log-sum-exp merge of S partial triples [S][rows][D+2] (split_stride
  * elements apart) -> out [rows, D] (out_dtype) and/or out_partial
  * [rows, D+2].  Used for the context-parallel combine after the NCCL

@@ -32,6 +32,8 @@
 
 #include <math.h>
 
+#include <mutex>
+
 namespace kessie {
 namespace {
 
@@ -559,4 +561,79 @@ extern "C" int kessie_lse_combine_v2(const float* partials, int num_splits, int6
         default: lse_combine_kernel<float><<<rows, head_dim, 0, st>>>(partials, num_splits, split_stride, head_dim, (float*)out, out_partial); break;
     }
     return check_launch("lse_combine");
+}
+
+// ============================================================================
+// Allocation-free decode entry point.
+//
+// Some callers cannot allocate device memory at the point where they decode:
+// code running under an allocator that is frozen or owned by someone else
+// (a serving engine that pre-reserved all of HBM for its KV pool, a plugin
+// invoked from inside another runtime's step, a process that must not grow
+// its footprint after start-up).  They cannot provide the split-KV scratch
+// that kessie_paged_fog_decode_v2 takes as `workspace`.  This variant keeps
+// that scratch in a fixed array inside the library instead.
+//
+// The array below is file-scope device memory of KESSIE_NOALLOC_SCRATCH_BYTES
+// (16 MiB); every GPU that loads this library holds it until the process
+// exits.  Its name is only a host-side handle: host code must never pass it
+// to a kernel.  Its device address is looked up with cudaGetSymbolAddress
+// once per device, on the first call made with that device current, and
+// cached; make that first call before any stream capture.  All calls share
+// the one array, so two calls whose work overlaps on the GPU (different
+// streams, or different threads using one device) race on it; callers must
+// order them.  The array keeps whatever the previous call left: the decode
+// writes every partial it later reads, so nothing needs clearing.
+// ============================================================================
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KESSIE_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoAllocMaxDevices = 64;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_scratch on the current device (set-up on first use).
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return set_error(KESSIE_ERR_CUDA, "noalloc decode: cudaGetDevice failed");
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return set_error(KESSIE_ERR_UNSUPPORTED, "noalloc decode: device %d", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(KESSIE_ERR_CUDA, "noalloc decode: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return KESSIE_OK;
+}
+
+}  // namespace
+
+extern "C" int kessie_paged_fog_decode_noalloc_v2(
+    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+    int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
+    const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens, const int32_t* kv_pos_offset,
+    const int32_t* q_positions, const int32_t* clear_start, float fog_alpha, const float* fog_weights,
+    int window_size, float sm_scale, int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_seq_len,
+    int dtype, void* out, float* out_partial, void* stream) {
+    if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_seq_len < 0)
+        return set_error(KESSIE_ERR_ARG, "noalloc decode: bad sizes");
+    const size_t need = kessie_paged_fog_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim,
+                                                               max_seq_len, page_size);
+    if (need > (size_t)KESSIE_NOALLOC_SCRATCH_BYTES)
+        return set_error(KESSIE_ERR_WORKSPACE,
+                         "noalloc decode: this shape needs %zu bytes of scratch, above the built-in %d-byte array; "
+                         "use kessie_paged_fog_decode_v2 with a caller-provided workspace",
+                         need, (int)KESSIE_NOALLOC_SCRATCH_BYTES);
+    void* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    return kessie_paged_fog_decode_ex_v2(q, q_stride_b, q_stride_h, k_cache, v_cache, page_stride, token_stride,
+                                         head_stride, num_pages, page_size, block_table, block_table_stride, seq_lens,
+                                         kv_pos_offset, q_positions, clear_start, fog_alpha, fog_weights, window_size,
+                                         sm_scale, batch, num_q_heads, num_kv_heads, head_dim, max_seq_len, dtype, out,
+                                         out_partial, scratch, (size_t)KESSIE_NOALLOC_SCRATCH_BYTES, 3, stream);
 }
