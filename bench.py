@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["kessie", "reference"], default="kessie")
     ap.add_argument("--workload", default="cp_decode_1m",
-                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "page_ops", "prefill"])
+                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "page_ops", "prefill", "prefill_small"])
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -460,8 +460,10 @@ def run_aux_workload(args):
         res.update(evicted=n, gather_ms=ms_g, gather_GBs=268435456 / ms_g / 1e6, remap_ms=ms_r,
                    remap_GBs=134217728 / ms_r / 1e6, insert_remap_ms=ms_i, insert_remap_GBs=268435456 / ms_i / 1e6,
                    evict_plus_refill_us=ms_e * 1e3, hbm_peak=hbm)
-    elif args.workload == "prefill":
+    elif args.workload in ("prefill", "prefill_small"):
         Hq, Hkv, D, ps, T, Nk = 32, 8, 128, 16, 8192, 262144
+        if args.workload == "prefill_small":        # profiling size: 256 MB of KV
+            T, Nk = 1024, 65536
         P = Nk // ps
         kv = torch.randn(P, ps, 2, Hkv, D, device=dev, dtype=torch.bfloat16)
         bt = torch.randperm(P, device=dev).to(torch.int32)[None]
@@ -469,6 +471,7 @@ def run_aux_workload(args):
         kl = torch.tensor([Nk], dtype=torch.int32, device=dev)
         cs = torch.tensor([Nk - 4096], dtype=torch.int32, device=dev)
         out = torch.empty_like(q)
+        res["impl"] = os.environ.get("KESSIE_PREFILL_IMPL", "tcgen05")
         ms = timeit(lambda: ops.paged_fog_prefill(q, kv[:, :, 0], kv[:, :, 1], bt, kl, clear_start=cs, fog_alpha=0.5,
                                                   out=out), max(3, args.steps // 20))
         flops = 4 * D * Hq * (T * (Nk - T) + T * (T + 1) // 2)

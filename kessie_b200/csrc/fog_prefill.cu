@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "ptx.cuh"
 #include "tma_host.cuh"
+#include "prefill_common.cuh"
 
 #include <math.h>
 
@@ -34,19 +35,7 @@ constexpr int kPST = 3;           // stages
 constexpr int kPThreads = (kPW + 1) * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 
-struct PrefillParams {
-    const void* q; int64_t q_sb, q_st, q_sh;
-    void* o; int64_t o_sb, o_st, o_sh;
-    const int32_t* block_table; int64_t bt_stride;   // null: dense (page coordinate = batch)
-    const int32_t* kv_lens; int kv_len_const;
-    const int32_t* q_start; int q_start_const;
-    int Nq, causal, window;
-    const int32_t* clear_start; int clear_start_const; float fog_alpha;
-    const float* fog_w; int64_t fog_w_sb;
-    float scale_log2;
-    int B, Hq, Hkv, G, upp, num_pages;
-    int* status;
-};
+
 
 template <int D>
 struct PSmem {
@@ -334,6 +323,10 @@ int launch_prefill_t(const CUtensorMap& mk, const CUtensorMap& mv, const Prefill
 
 int run_prefill(const PrefillParams& p, const void* kc, const void* vc, int64_t page_stride, int64_t token_stride,
                 int64_t head_stride, int map_pages, int map_tokens, int D, bool bf16, cudaStream_t st) {
+    // tcgen05/TMEM kernel for the shapes it covers (head_dim 128, Hq/Hkv | 128)
+    const int rc = run_prefill_tc(p, p.q, kc, vc, page_stride, token_stride, head_stride, map_pages, map_tokens, D,
+                                  bf16, st);
+    if (rc != kTcNotCovered) return rc;
     CUtensorMap mk, mv;
     CUresult r1 = encode_kv_tile_map(&mk, kc, bf16, D, map_tokens, p.Hkv, map_pages, token_stride, head_stride, page_stride);
     CUresult r2 = encode_kv_tile_map(&mv, vc, bf16, D, map_tokens, p.Hkv, map_pages, token_stride, head_stride, page_stride);

@@ -1,0 +1,472 @@
+// fog_prefill_tc.cu -- chunked-prefill fog attention on the 5th-generation
+// tensor cores (tcgen05 + TMEM), head_dim 128, bf16 / fp16.
+//
+// Semantics are those of fog_prefill.cu (kessie_hip_kernels.py:577-593 with a
+// query offset, GQA, paged or dense KV): O_i = sum_j p_ij w_j v_j / sum_j p_ij.
+//
+// CTA = 128 query rows of one KV head (rows are (token, head-in-group) pairs,
+// so the Hq/Hkv heads sharing a KV head share every K/V tile), 6 warps:
+//   warp 0     TMA producer: Q once; per 128-key tile the K and V boxes
+//              (16..128 tokens each, one per d-half) into 3- / 2-stage rings.
+//   warp 1     TMEM owner and MMA issuer (one thread):
+//                S_j  = Q K_j^T           tcgen05.mma  SS, M128 N128 K16 x 8  -> TMEM S[j%2]
+//                O   += P_{j-1} V_{j-1}   tcgen05.mma  TS (P in TMEM), V MN-major -> TMEM O
+//              S_j is issued before PV_{j-1}, so the tensor core computes the
+//              next scores while the softmax warps work on the current ones.
+//   warps 2-5  softmax, one row per thread (TMEM lane = row): tcgen05.ld S,
+//              mask (boundary tiles only), online max, p = 2^(s*scale - m),
+//              row sum of p (unweighted), P' = p * w_j (fog), tcgen05.st P'.
+//              The running max is only moved (and O rescaled in TMEM) when it
+//              grows by more than 2^8, so p <= 256 and the rescale is rare;
+//              the final O / l is exact either way.
+// TMEM: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512) columns.
+// Every mbarrier wait is bounded; on a timeout all warps still reach the final
+// barrier and the TMEM is freed.
+#include "common.cuh"
+#include "ptx.cuh"
+#include "tma_host.cuh"
+#include "prefill_common.cuh"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+namespace kessie {
+namespace {
+
+constexpr int kNK = 3;                 // K stages
+constexpr int kNV = 2;                 // V stages
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
+constexpr float kRescaleThreshold = 8.0f;    // log2 units
+
+struct L {
+    static constexpr int kHalf = 128 * 128;         // [128 rows][64 el] x 2 B
+    static constexpr int kTile = 2 * kHalf;         // both d-halves: 32 KB
+    static constexpr int kQ = 0;
+    static constexpr int kK = kQ + kTile;
+    static constexpr int kV = kK + kNK * kTile;
+    static constexpr int kW = kV + kNV * kTile;     // 4 softmax warps x 128 fp32 weights
+    static constexpr int kBar = kW + 4 * 128 * 4;
+    // q_full, k_full[3], k_empty[3], v_full[2], v_empty[2], s_full[2], p_full[2], o_bar[2]
+    static constexpr int kNumBar = 1 + 2 * kNK + 2 * kNV + 6;
+    static constexpr int kSlot = kBar + kNumBar * 8;
+    static constexpr int kBytes = kSlot + 16;
+    static constexpr int kAlloc = kBytes + 1024;
+};
+
+struct TcArgs {
+    PrefillParams p;
+    int q_mode;        // 0: Q map {64, g, t(batch-folded), dh, hk}; 1: {64, t, dh, h, b} (G == 1)
+    int box_tokens;    // tokens per K/V box
+    int dense;         // K/V map page coordinate = batch
+    int page_size;
+};
+
+__device__ __forceinline__ float fog_w(const PrefillParams& p, int b, int cs, int key) {
+    if (p.fog_w) return __ldg(p.fog_w + b * p.fog_w_sb + key);
+    if (key >= cs) return 1.f;
+    return powf(__fdiv_rn((float)key, (float)max(cs - 1, 1)), p.fog_alpha);
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                                      const __grid_constant__ CUtensorMap tmK,
+                                                                      const __grid_constant__ CUtensorMap tmV,
+                                                                      const TcArgs a) {
+    const PrefillParams& p = a.p;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + kNK;
+    uint64_t* v_full = k_empty + kNK;
+    uint64_t* v_empty = v_full + kNV;
+    uint64_t* s_full = v_empty + kNV;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* o_bar = p_full + 2;
+    uint32_t* slot = reinterpret_cast<uint32_t*>(smem + L::kSlot);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile_m = gridDim.x - 1 - blockIdx.x;          // heavy (late, causal) row tiles first
+    const int hk = blockIdx.y, b = blockIdx.z;
+    const int G = p.G;
+    const int rows_total = p.Nq * G;
+    const int row0 = tile_m * 128;
+    const int kv_len = p.kv_lens ? p.kv_lens[b] : p.kv_len_const;
+    const int q0 = p.q_start ? p.q_start[b] : (p.q_start_const >= 0 ? p.q_start_const : kv_len - p.Nq);
+    const int t_first = row0 / G;
+    const int t_last = (min(row0 + 128, rows_total) - 1) / G;
+    const int pos_lo = q0 + t_first, pos_hi = q0 + t_last;
+    int j_lo = p.window > 0 ? max(0, pos_lo - p.window + 1) : 0;
+    int j_hi = (p.causal || p.window > 0) ? min(kv_len, pos_hi + 1) : kv_len;
+    if (j_hi < j_lo) j_hi = j_lo;
+    const int tile_lo = j_lo / 128, tile_hi = (j_hi + 127) / 128;
+    const int n_tiles = tile_hi - tile_lo;
+
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(q_full, 1);
+        for (int i = 0; i < kNK; ++i) { ptx::mbar_init(&k_full[i], 1); ptx::mbar_init(&k_empty[i], 1); }
+        for (int i = 0; i < kNV; ++i) { ptx::mbar_init(&v_full[i], 1); ptx::mbar_init(&v_empty[i], 1); }
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(&s_full[i], 1);
+            ptx::mbar_init(&p_full[i], 4);
+            ptx::mbar_init(&o_bar[i], 1);
+        }
+        ptx::fence_mbar_init();
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(slot, kTmemCols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *slot;
+
+    if (warp == 0) {
+        // ================================================================ producer
+        const int32_t* bt = a.dense ? nullptr : p.block_table + (int64_t)b * p.bt_stride;
+        const int ps = a.page_size, bxt = a.box_tokens, nbox = 128 / bxt;
+        const int kv_pages = a.dense ? 0 : (kv_len + ps - 1) / ps;
+        const uint64_t pol = ptx::policy_evict_first();
+        if (lane == 0 && n_tiles > 0) {
+            ptx::prefetch_tensormap(&tmQ);
+            ptx::prefetch_tensormap(&tmK);
+            ptx::prefetch_tensormap(&tmV);
+            ptx::mbar_arrive_expect_tx(q_full, (uint32_t)L::kTile);
+            for (int dh = 0; dh < 2; ++dh) {
+                if (a.q_mode == 0)
+                    ptx::tma_load_5d(smem + L::kQ + dh * L::kHalf, &tmQ, q_full, 0, 0, b * p.Nq + row0 / G, dh, hk);
+                else
+                    ptx::tma_load_5d(smem + L::kQ + dh * L::kHalf, &tmQ, q_full, 0, row0, dh, hk, b);
+            }
+        }
+        int ids_reg = -1, ids_base = -(1 << 30);
+        int k_issued = 0, v_issued = 0;
+        bool ok = true;
+        for (int it = 0; it < n_tiles && ok; ++it) {
+            const int key0 = (tile_lo + it) * 128;
+            // page ids of this tile (at most 8 pages); one warp-wide load covers 32 pages
+            if (!a.dense) {
+                const int pg_first = key0 / ps, pg_last = (key0 + 127) / ps;
+                if (pg_first < ids_base || pg_last >= ids_base + 32) {
+                    ids_base = pg_first;
+                    const int pi = ids_base + lane;
+                    int id = -1;
+                    if (pi < kv_pages) {
+                        id = __ldg(bt + pi);
+                        if (id < 0 || id >= p.num_pages) { record_status(p.status, KESSIE_DEV_BAD_PAGE_ID); id = -1; }
+                    }
+                    ids_reg = id;
+                }
+            }
+            int pages[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int key = key0 + u * bxt;
+                const int pi = a.dense ? 0 : key / ps;
+                int id = __shfl_sync(0xffffffffu, ids_reg, (pi - ids_base) & 31);
+                pages[u] = (u < nbox) ? id : -1;
+            }
+            if (lane == 0) {
+                const int ks = it % kNK, vs = it % kNV;
+                if (it >= kNK && !ptx::mbar_wait(&k_empty[ks], ((uint32_t)(it / kNK) & 1u) ^ 1u)) ok = false;
+                if (ok) {
+                    ptx::mbar_arrive_expect_tx(&k_full[ks], (uint32_t)L::kTile);
+                    uint8_t* kt = smem + L::kK + ks * L::kTile;
+                    for (int u = 0; u < nbox; ++u) {
+                        const int key = key0 + u * bxt;
+                        const int c1 = a.dense ? key : key % ps;
+                        const int c4 = a.dense ? b : (pages[u] < 0 ? p.num_pages : pages[u]);
+                        for (int dh = 0; dh < 2; ++dh)
+                            ptx::tma_load_5d_hint(kt + dh * L::kHalf + u * bxt * 128, &tmK, &k_full[ks], 0, c1, dh, hk, c4, pol);
+                    }
+                    k_issued = it + 1;
+                }
+                if (ok && it >= kNV && !ptx::mbar_wait(&v_empty[vs], ((uint32_t)(it / kNV) & 1u) ^ 1u)) ok = false;
+                if (ok) {
+                    ptx::mbar_arrive_expect_tx(&v_full[vs], (uint32_t)L::kTile);
+                    uint8_t* vt = smem + L::kV + vs * L::kTile;
+                    for (int u = 0; u < nbox; ++u) {
+                        const int key = key0 + u * bxt;
+                        const int c1 = a.dense ? key : key % ps;
+                        const int c4 = a.dense ? b : (pages[u] < 0 ? p.num_pages : pages[u]);
+                        for (int dh = 0; dh < 2; ++dh)
+                            ptx::tma_load_5d_hint(vt + dh * L::kHalf + u * bxt * 128, &tmV, &v_full[vs], 0, c1, dh, hk, c4, pol);
+                    }
+                    v_issued = it + 1;
+                } else {
+                    record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+                }
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        }
+        if (lane == 0) {
+            // drain: every issued load has landed before the CTA can exit
+            for (int it = max(0, k_issued - kNK); it < k_issued; ++it)
+                if (!ptx::mbar_wait(&k_full[it % kNK], (uint32_t)(it / kNK) & 1u)) break;
+            for (int it = max(0, v_issued - kNV); it < v_issued; ++it)
+                if (!ptx::mbar_wait(&v_full[it % kNV], (uint32_t)(it / kNV) & 1u)) break;
+        }
+    } else if (warp == 1) {
+        // ================================================================ MMA issuer
+        const uint32_t idS = ptx::umma_idesc_f16(BF16, false, 128);
+        const uint32_t idPV = ptx::umma_idesc_f16(BF16, true, 128);
+        const uint32_t qa = ptx::smem_u32(smem + L::kQ);
+        bool ok = n_tiles > 0 && ptx::mbar_wait(q_full, 0);
+        if (n_tiles > 0 && !ok) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+        ptx::tc_fence_after();
+        for (int it = 0; ok && it <= n_tiles; ++it) {
+            if (it < n_tiles) {
+                const int ks = it % kNK;
+                if (!ptx::mbar_wait(&k_full[ks], (uint32_t)(it / kNK) & 1u)) { ok = false; break; }
+                ptx::tc_fence_after();
+                const uint32_t kb = ptx::smem_u32(smem + L::kK + ks * L::kTile);
+                const uint32_t dS = tmem + kColS + (uint32_t)(it & 1) * 128;
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (uint32_t)((kk >> 2) * L::kHalf + (kk & 3) * 32);
+                        ptx::umma_ss(dS, ptx::smem_desc_sw128(qa + off, 16, 1024),
+                                     ptx::smem_desc_sw128(kb + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+                    }
+                    ptx::umma_commit(&s_full[it & 1]);
+                    ptx::umma_commit(&k_empty[ks]);
+                }
+                __syncwarp();
+            }
+            if (it >= 1) {
+                const int j = it - 1, vs = j % kNV;
+                if (!ptx::mbar_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u)) { ok = false; break; }
+                if (!ptx::mbar_wait(&v_full[vs], (uint32_t)(j / kNV) & 1u)) { ok = false; break; }
+                ptx::tc_fence_after();
+                uint8_t* vt = smem + L::kV + vs * L::kTile;
+                const int key0 = (tile_lo + j) * 128;
+                if (!a.dense && key0 + 128 > kv_len) {
+                    // stale slots past kv_len in the last page: zero their V rows so
+                    // 0 * (stale NaN) cannot reach O
+                    const int first = max(0, kv_len - key0);
+                    for (int e = lane; e < (128 - first) * 2 * 8; e += 32) {
+                        const int row = first + e / 16, dh = (e >> 3) & 1, ch = e & 7;
+                        *reinterpret_cast<uint4*>(vt + dh * L::kHalf + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+                    }
+                    ptx::fence_proxy_async_smem();
+                    __syncwarp();
+                }
+                const uint32_t vb = ptx::smem_u32(vt);
+                const uint32_t aP = tmem + kColP + (uint32_t)(j & 1) * 64;
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        ptx::umma_ts(tmem + kColO, aP + kk * 8, ptx::smem_desc_sw128(vb + kk * 2048, L::kHalf, 1024),
+                                     idPV, (j > 0 || kk > 0) ? 1u : 0u);
+                    ptx::umma_commit(&v_empty[vs]);
+                    ptx::umma_commit(&o_bar[j & 1]);
+                }
+                __syncwarp();
+            }
+        }
+        if (!ok && n_tiles > 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+    } else {
+        // ================================================================ softmax warps
+        const int q4 = warp & 3;
+        const int r = q4 * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        const int rr = row0 + r;
+        const bool valid_row = rr < rows_total;
+        const int tok = rr / G, gh = rr - tok * G;
+        const int pos = q0 + tok;
+        float* wbuf = reinterpret_cast<float*>(smem + L::kW) + (warp - 2) * 128;
+        const int cs = (p.clear_start || p.clear_start_const > 0) && p.fog_alpha > 0.f
+                           ? (p.clear_start ? p.clear_start[b] : p.clear_start_const) : INT_MIN;
+        const bool has_fog = p.fog_w != nullptr || cs > 0;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int key0 = (tile_lo + j) * 128;
+            if (has_fog) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int key = key0 + lane * 4 + e;
+                    wbuf[lane * 4 + e] = key < kv_len ? fog_w(p, b, cs, key) : 0.f;
+                }
+            }
+            __syncwarp();
+            if (!ptx::mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u)) { ok = false; break; }
+            ptx::tc_fence_after();
+            uint32_t sv[4][32];
+            const uint32_t sbase = tmem + lane_off + kColS + (uint32_t)(j & 1) * 128;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ptx::tmem_ld32(sbase + c * 32, sv[c]);
+            ptx::tmem_ld_wait();
+            // tile-uniform visibility: no per-element mask for interior tiles
+            const bool interior = key0 + 128 <= kv_len && (!(p.causal || p.window > 0) || key0 + 127 <= pos_lo) &&
+                                  (p.window <= 0 || key0 >= pos_hi - p.window + 1);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float s = __uint_as_float(sv[c][i]);
+                    if (!interior || !valid_row) {
+                        const int key = key0 + c * 32 + i;
+                        bool vis = valid_row && key < kv_len;
+                        if (p.causal || p.window > 0) vis = vis && key <= pos;
+                        if (p.window > 0) vis = vis && pos - key < p.window;
+                        s = vis ? s : -INFINITY;
+                        sv[c][i] = __float_as_uint(s);
+                    }
+                    mx = fmaxf(mx, s);
+                }
+            const float m_tile = mx == -INFINITY ? -INFINITY : mx * p.scale_log2;
+            const float m_new = fmaxf(m_used, m_tile);
+            const bool need = m_new != -INFINITY && (m_used == -INFINITY || m_new > m_used + kRescaleThreshold);
+            float factor = 1.f;
+            if (need) {
+                factor = m_used == -INFINITY ? 0.f : exp2f(m_used - m_new);
+                l *= factor;
+                m_used = m_new;
+            }
+            // O rescale in TMEM (warp-collective; only when some row moved its max
+            // after O already holds a partial sum)
+            if (__any_sync(0xffffffffu, need && factor != 0.f && j > 0) ) {
+                if (!ptx::mbar_wait(&o_bar[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u)) { ok = false; break; }
+                ptx::tc_fence_after();
+                const float f = (need && factor != 0.f) ? factor : 1.f;
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t ov[32];
+                    ptx::tmem_ld32(tmem + lane_off + kColO + c * 32, ov);
+                    ptx::tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * f);
+                    ptx::tmem_st32(tmem + lane_off + kColO + c * 32, ov);
+                }
+                ptx::tmem_st_wait();
+            }
+            const float base = m_used == -INFINITY ? 0.f : m_used;
+            float lt = 0.f;
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                uint32_t pk[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int c0 = h2 * 64 + 2 * i;          // key column
+                    const float s0 = __uint_as_float(sv[c0 >> 5][c0 & 31]);
+                    const float s1 = __uint_as_float(sv[(c0 + 1) >> 5][(c0 + 1) & 31]);
+                    const float p0 = exp2f(fmaf(s0, p.scale_log2, -base));
+                    const float p1 = exp2f(fmaf(s1, p.scale_log2, -base));
+                    lt += p0 + p1;
+                    const float w0 = has_fog ? wbuf[c0] : 1.f, w1 = has_fog ? wbuf[c0 + 1] : 1.f;
+                    pk[i] = ptx::pack2<BF16>(p0 * w0, p1 * w1);
+                }
+                ptx::tmem_st32(tmem + lane_off + kColP + (uint32_t)(j & 1) * 64 + h2 * 32, pk);
+            }
+            ptx::tmem_st_wait();
+            l += lt;
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&p_full[j & 1]);
+        }
+        // ---- epilogue: O / l -> global
+        bool have = n_tiles > 0 && ok;
+        if (have) {
+            const int jl = n_tiles - 1;
+            have = ptx::mbar_wait(&o_bar[jl & 1], (uint32_t)(jl >> 1) & 1u);
+            ptx::tc_fence_after();
+        }
+        if (!ok || (n_tiles > 0 && !have)) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint16_t* orow = reinterpret_cast<uint16_t*>(p.o) + (int64_t)b * p.o_sb + (int64_t)tok * p.o_st +
+                         (int64_t)(hk * G + gh) * p.o_sh;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+            uint32_t ov[32];
+            if (have) {
+                ptx::tmem_ld32(tmem + lane_off + kColO + c * 32, ov);
+                ptx::tmem_ld_wait();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) ov[i] = 0u;
+            }
+            if (valid_row) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    pk[i] = ptx::pack2<BF16>(__uint_as_float(ov[2 * i]) * inv, __uint_as_float(ov[2 * i + 1]) * inv);
+                uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            }
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+int run_prefill_tc(const PrefillParams& p, const void* q_base, const void* k_cache, const void* v_cache,
+                   int64_t page_stride, int64_t token_stride, int64_t head_stride, int map_pages, int map_tokens,
+                   int head_dim, bool bf16, cudaStream_t st) {
+    const char* env = getenv("KESSIE_PREFILL_IMPL");
+    if (env && strcmp(env, "mma") == 0) return kTcNotCovered;
+    if (head_dim != 128 || p.G <= 0 || 128 % p.G) return kTcNotCovered;
+    // alignment: Q/O rows and K/V rows 16-byte aligned
+    if (((p.q_st | p.q_sh | p.o_st | p.o_sh) & 7) || ((token_stride | head_stride | page_stride) & 7))
+        return kTcNotCovered;
+    const bool dense = p.block_table == nullptr;
+    int q_mode;
+    if (p.B == 1 || p.q_sb == (int64_t)p.Nq * p.q_st) q_mode = 0;
+    else if (p.G == 1) q_mode = 1;
+    else return kTcNotCovered;
+    const int ps = map_tokens;
+    int box = dense ? 128 : (ps >= 128 ? 128 : ps);
+    if (!dense && (ps % 16 || 128 % box)) return kTcNotCovered;
+
+    CUtensorMap mq, mk, mv;
+    CUresult r;
+    if (q_mode == 0) {
+        const cuuint64_t dims[5] = {64, (cuuint64_t)p.G, (cuuint64_t)p.B * p.Nq, 2, (cuuint64_t)p.Hkv};
+        const cuuint64_t str[4] = {(cuuint64_t)p.q_sh * 2, (cuuint64_t)p.q_st * 2, 128, (cuuint64_t)p.G * p.q_sh * 2};
+        const cuuint32_t bx[5] = {64, (cuuint32_t)p.G, (cuuint32_t)(128 / p.G), 1, 1};
+        r = encode_tiled_5d_sw128(&mq, q_base, bf16, dims, str, bx);
+    } else {
+        const cuuint64_t dims[5] = {64, (cuuint64_t)p.Nq, 2, (cuuint64_t)p.Hq, (cuuint64_t)p.B};
+        const cuuint64_t str[4] = {(cuuint64_t)p.q_st * 2, 128, (cuuint64_t)p.q_sh * 2, (cuuint64_t)p.q_sb * 2};
+        const cuuint32_t bx[5] = {64, 128, 1, 1, 1};
+        r = encode_tiled_5d_sw128(&mq, q_base, bf16, dims, str, bx);
+    }
+    if (r != CUDA_SUCCESS) return kTcNotCovered;
+    {
+        const cuuint64_t dims[5] = {64, (cuuint64_t)map_tokens, 2, (cuuint64_t)p.Hkv, (cuuint64_t)map_pages};
+        const cuuint64_t str[4] = {(cuuint64_t)token_stride * 2, 128, (cuuint64_t)head_stride * 2,
+                                   (cuuint64_t)page_stride * 2};
+        const cuuint32_t bx[5] = {64, (cuuint32_t)box, 1, 1, 1};
+        if (encode_tiled_5d_sw128(&mk, k_cache, bf16, dims, str, bx) != CUDA_SUCCESS ||
+            encode_tiled_5d_sw128(&mv, v_cache, bf16, dims, str, bx) != CUDA_SUCCESS)
+            return kTcNotCovered;
+    }
+    TcArgs a;
+    a.p = p;
+    a.q_mode = q_mode;
+    a.box_tokens = box;
+    a.dense = dense ? 1 : 0;
+    a.page_size = ps;
+    auto kern = bf16 ? fog_prefill_tc_kernel<true> : fog_prefill_tc_kernel<false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) != cudaSuccess)
+        return check_launch("prefill_tc: set smem attribute");
+    const int rows = p.Nq * p.G;
+    dim3 grid((rows + 127) / 128, p.Hkv, p.B);
+    kern<<<grid, kThreads, L::kAlloc, st>>>(mq, mk, mv, a);
+    return check_launch("fog_prefill_tc");
+}
+
+}  // namespace kessie

@@ -46,4 +46,16 @@ inline CUresult encode_kv_tile_map(CUtensorMap* map, const void* base, bool bf16
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+// Generic 5-D tiled tensor map with 128-byte swizzle (16-bit elements).
+// strides_bytes: dims 1..4.  Returns the driver's result.
+inline CUresult encode_tiled_5d_sw128(CUtensorMap* map, const void* base, bool bf16, const cuuint64_t dims[5],
+                                      const cuuint64_t strides_bytes[4], const cuuint32_t box[5]) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return CUDA_ERROR_NOT_SUPPORTED;
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+               const_cast<void*>(base), dims, strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
 }  // namespace kessie

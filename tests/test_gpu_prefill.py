@@ -15,11 +15,22 @@ from tests.kessie_testutil import ROUND, TOL, make_paged, random_block_table, rn
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module", autouse=True)
-def _cuda():
+@pytest.fixture(scope="module", autouse=True, params=["tcgen05", "mma"])
+def _cuda(request):
+    """Every prefill test runs on both implementations: the tcgen05/TMEM
+    kernel (default for head_dim 128) and the warp-level mma.sync kernel."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    yield
+    old = os.environ.get("KESSIE_PREFILL_IMPL")
+    if request.param == "mma":
+        os.environ["KESSIE_PREFILL_IMPL"] = "mma"
+    else:
+        os.environ.pop("KESSIE_PREFILL_IMPL", None)
+    yield request.param
+    if old is None:
+        os.environ.pop("KESSIE_PREFILL_IMPL", None)
+    else:
+        os.environ["KESSIE_PREFILL_IMPL"] = old
 
 
 def _legacy(fn_name, q, k, v, fog, W, causal):
