@@ -36,7 +36,7 @@ namespace {
 
 constexpr int kNK = 3;                 // K stages
 constexpr int kNV = 2;                 // V stages
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;     // 7 warps: K producer, MMA, 4 softmax, V producer
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
 constexpr float kRescaleThreshold = 8.0f;    // log2 units
@@ -47,7 +47,7 @@ struct L {
     static constexpr int kQ = 0;
     static constexpr int kK = kQ + kTile;
     static constexpr int kV = kK + kNK * kTile;
-    static constexpr int kW = kV + kNV * kTile;     // 4 softmax warps x 128 fp32 weights
+    static constexpr int kW = kV + kNV * kTile;     // per softmax warp: fog weights of the tile's 128 keys
     static constexpr int kBar = kW + 4 * 128 * 4;
     // q_full, k_full[3], k_empty[3], v_full[2], v_empty[2], s_full[2], p_full[2], o_bar[2]
     static constexpr int kNumBar = 1 + 2 * kNK + 2 * kNV + 6;
@@ -63,12 +63,6 @@ struct TcArgs {
     int dense;         // K/V map page coordinate = batch
     int page_size;
 };
-
-__device__ __forceinline__ float fog_w(const PrefillParams& p, int b, int cs, int key) {
-    if (p.fog_w) return __ldg(p.fog_w + b * p.fog_w_sb + key);
-    if (key >= cs) return 1.f;
-    return powf(__fdiv_rn((float)key, (float)max(cs - 1, 1)), p.fog_alpha);
-}
 
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -106,6 +100,10 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
     const int tile_lo = j_lo / 128, tile_hi = (j_hi + 127) / 128;
     const int n_tiles = tile_hi - tile_lo;
 
+    const int cs = (p.clear_start || p.clear_start_const > 0) && p.fog_alpha > 0.f
+                       ? (p.clear_start ? p.clear_start[b] : p.clear_start_const) : INT_MIN;
+    const bool has_fog = p.fog_w != nullptr || cs > 0;
+
     if (threadIdx.x == 0) {
         ptx::mbar_init(q_full, 1);
         for (int i = 0; i < kNK; ++i) { ptx::mbar_init(&k_full[i], 1); ptx::mbar_init(&k_empty[i], 1); }
@@ -126,28 +124,36 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
     ptx::tc_fence_after();
     const uint32_t tmem = *slot;
 
-    if (warp == 0) {
-        // ================================================================ producer
+    if (warp == 0 || warp == 6) {
+        // ================================================================ producers
+        // warp 0: Q, then the K ring; warp 6: the V ring.  Separate warps so a
+        // V stage waiting for its PV MMA never holds back the K prefetch.
+        const bool is_k = warp == 0;
+        const int NS = is_k ? kNK : kNV;
+        uint64_t* full = is_k ? k_full : v_full;
+        uint64_t* empty = is_k ? k_empty : v_empty;
+        const CUtensorMap* map = is_k ? &tmK : &tmV;
+        const int ring_off = is_k ? L::kK : L::kV;
         const int32_t* bt = a.dense ? nullptr : p.block_table + (int64_t)b * p.bt_stride;
         const int ps = a.page_size, bxt = a.box_tokens, nbox = 128 / bxt;
         const int kv_pages = a.dense ? 0 : (kv_len + ps - 1) / ps;
         const uint64_t pol = ptx::policy_evict_first();
         if (lane == 0 && n_tiles > 0) {
-            ptx::prefetch_tensormap(&tmQ);
-            ptx::prefetch_tensormap(&tmK);
-            ptx::prefetch_tensormap(&tmV);
-            ptx::mbar_arrive_expect_tx(q_full, (uint32_t)L::kTile);
-            for (int dh = 0; dh < 2; ++dh) {
-                if (a.q_mode == 0)
-                    ptx::tma_load_5d(smem + L::kQ + dh * L::kHalf, &tmQ, q_full, 0, 0, b * p.Nq + row0 / G, dh, hk);
-                else
-                    ptx::tma_load_5d(smem + L::kQ + dh * L::kHalf, &tmQ, q_full, 0, row0, dh, hk, b);
+            ptx::prefetch_tensormap(map);
+            if (is_k) {
+                ptx::prefetch_tensormap(&tmQ);
+                ptx::mbar_arrive_expect_tx(q_full, (uint32_t)L::kTile);
+                for (int dh = 0; dh < 2; ++dh) {
+                    if (a.q_mode == 0)
+                        ptx::tma_load_5d(smem + L::kQ + dh * L::kHalf, &tmQ, q_full, 0, 0, b * p.Nq + row0 / G, dh, hk);
+                    else
+                        ptx::tma_load_5d(smem + L::kQ + dh * L::kHalf, &tmQ, q_full, 0, row0, dh, hk, b);
+                }
             }
         }
         int ids_reg = -1, ids_base = -(1 << 30);
-        int k_issued = 0, v_issued = 0;
-        bool ok = true;
-        for (int it = 0; it < n_tiles && ok; ++it) {
+        int issued = 0;
+        for (int it = 0; it < n_tiles; ++it) {
             const int key0 = (tile_lo + it) * 128;
             // page ids of this tile (at most 8 pages); one warp-wide load covers 32 pages
             if (!a.dense) {
@@ -158,7 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                     int id = -1;
                     if (pi < kv_pages) {
                         id = __ldg(bt + pi);
-                        if (id < 0 || id >= p.num_pages) { record_status(p.status, KESSIE_DEV_BAD_PAGE_ID); id = -1; }
+                        if (id < 0 || id >= p.num_pages) {
+                            if (is_k) record_status(p.status, KESSIE_DEV_BAD_PAGE_ID);
+                            id = -1;
+                        }
                     }
                     ids_reg = id;
                 }
@@ -171,106 +180,96 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 int id = __shfl_sync(0xffffffffu, ids_reg, (pi - ids_base) & 31);
                 pages[u] = (u < nbox) ? id : -1;
             }
+            int ok = 1;
             if (lane == 0) {
-                const int ks = it % kNK, vs = it % kNV;
-                if (it >= kNK && !ptx::mbar_wait(&k_empty[ks], ((uint32_t)(it / kNK) & 1u) ^ 1u)) ok = false;
-                if (ok) {
-                    ptx::mbar_arrive_expect_tx(&k_full[ks], (uint32_t)L::kTile);
-                    uint8_t* kt = smem + L::kK + ks * L::kTile;
-                    for (int u = 0; u < nbox; ++u) {
-                        const int key = key0 + u * bxt;
-                        const int c1 = a.dense ? key : key % ps;
-                        const int c4 = a.dense ? b : (pages[u] < 0 ? p.num_pages : pages[u]);
-                        for (int dh = 0; dh < 2; ++dh)
-                            ptx::tma_load_5d_hint(kt + dh * L::kHalf + u * bxt * 128, &tmK, &k_full[ks], 0, c1, dh, hk, c4, pol);
-                    }
-                    k_issued = it + 1;
-                }
-                if (ok && it >= kNV && !ptx::mbar_wait(&v_empty[vs], ((uint32_t)(it / kNV) & 1u) ^ 1u)) ok = false;
-                if (ok) {
-                    ptx::mbar_arrive_expect_tx(&v_full[vs], (uint32_t)L::kTile);
-                    uint8_t* vt = smem + L::kV + vs * L::kTile;
-                    for (int u = 0; u < nbox; ++u) {
-                        const int key = key0 + u * bxt;
-                        const int c1 = a.dense ? key : key % ps;
-                        const int c4 = a.dense ? b : (pages[u] < 0 ? p.num_pages : pages[u]);
-                        for (int dh = 0; dh < 2; ++dh)
-                            ptx::tma_load_5d_hint(vt + dh * L::kHalf + u * bxt * 128, &tmV, &v_full[vs], 0, c1, dh, hk, c4, pol);
-                    }
-                    v_issued = it + 1;
-                } else {
+                const int st = it % NS;
+                if (it >= NS && !ptx::mbar_wait(&empty[st], ((uint32_t)(it / NS) & 1u) ^ 1u)) {
+                    ok = 0;
                     record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+                } else {
+                    ptx::mbar_arrive_expect_tx(&full[st], (uint32_t)L::kTile);
+                    uint8_t* dst = smem + ring_off + st * L::kTile;
+                    for (int u = 0; u < nbox; ++u) {
+                        const int key = key0 + u * bxt;
+                        const int c1 = a.dense ? key : key % ps;
+                        const int c4 = a.dense ? b : (pages[u] < 0 ? p.num_pages : pages[u]);
+                        for (int dh = 0; dh < 2; ++dh)
+                            ptx::tma_load_5d_hint(dst + dh * L::kHalf + u * bxt * 128, map, &full[st], 0, c1, dh, hk, c4, pol);
+                    }
+                    issued = it + 1;
                 }
             }
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         }
         if (lane == 0) {
             // drain: every issued load has landed before the CTA can exit
-            for (int it = max(0, k_issued - kNK); it < k_issued; ++it)
-                if (!ptx::mbar_wait(&k_full[it % kNK], (uint32_t)(it / kNK) & 1u)) break;
-            for (int it = max(0, v_issued - kNV); it < v_issued; ++it)
-                if (!ptx::mbar_wait(&v_full[it % kNV], (uint32_t)(it / kNV) & 1u)) break;
+            for (int it = max(0, issued - NS); it < issued; ++it)
+                if (!ptx::mbar_wait(&full[it % NS], (uint32_t)(it / NS) & 1u)) break;
         }
     } else if (warp == 1) {
         // ================================================================ MMA issuer
+        // order: S_0, S_1, then per tile j: [wait P_j] S_{j+2}, [wait V_j] PV_j.
+        // S_{j+2} reuses S buffer j%2 (softmax j has read it); P buffers are
+        // separate, and softmax j+2 waits for PV_j before overwriting P j%2.
         const uint32_t idS = ptx::umma_idesc_f16(BF16, false, 128);
         const uint32_t idPV = ptx::umma_idesc_f16(BF16, true, 128);
         const uint32_t qa = ptx::smem_u32(smem + L::kQ);
         bool ok = n_tiles > 0 && ptx::mbar_wait(q_full, 0);
-        if (n_tiles > 0 && !ok) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
         ptx::tc_fence_after();
-        for (int it = 0; ok && it <= n_tiles; ++it) {
-            if (it < n_tiles) {
-                const int ks = it % kNK;
-                if (!ptx::mbar_wait(&k_full[ks], (uint32_t)(it / kNK) & 1u)) { ok = false; break; }
-                ptx::tc_fence_after();
-                const uint32_t kb = ptx::smem_u32(smem + L::kK + ks * L::kTile);
-                const uint32_t dS = tmem + kColS + (uint32_t)(it & 1) * 128;
-                if (lane == 0) {
+        auto issue_s = [&](int t) -> bool {
+            const int ks = t % kNK;
+            if (!ptx::mbar_wait(&k_full[ks], (uint32_t)(t / kNK) & 1u)) return false;
+            ptx::tc_fence_after();
+            const uint32_t kb = ptx::smem_u32(smem + L::kK + ks * L::kTile);
+            const uint32_t dS = tmem + kColS + (uint32_t)(t & 1) * 128;
+            if (lane == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t off = (uint32_t)((kk >> 2) * L::kHalf + (kk & 3) * 32);
-                        ptx::umma_ss(dS, ptx::smem_desc_sw128(qa + off, 16, 1024),
-                                     ptx::smem_desc_sw128(kb + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
-                    }
-                    ptx::umma_commit(&s_full[it & 1]);
-                    ptx::umma_commit(&k_empty[ks]);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (uint32_t)((kk >> 2) * L::kHalf + (kk & 3) * 32);
+                    ptx::umma_ss(dS, ptx::smem_desc_sw128(qa + off, 16, 1024), ptx::smem_desc_sw128(kb + off, 16, 1024),
+                                 idS, kk > 0 ? 1u : 0u);
                 }
+                ptx::umma_commit(&s_full[t & 1]);
+                ptx::umma_commit(&k_empty[ks]);
+            }
+            __syncwarp();
+            return true;
+        };
+        if (ok) ok = issue_s(0);
+        if (ok && n_tiles > 1) ok = issue_s(1);
+        for (int j = 0; ok && j < n_tiles; ++j) {
+            if (!ptx::mbar_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u)) { ok = false; break; }
+            if (j + 2 < n_tiles && !issue_s(j + 2)) { ok = false; break; }
+            const int vs = j % kNV;
+            if (!ptx::mbar_wait(&v_full[vs], (uint32_t)(j / kNV) & 1u)) { ok = false; break; }
+            ptx::tc_fence_after();
+            uint8_t* vt = smem + L::kV + vs * L::kTile;
+            const int key0 = (tile_lo + j) * 128;
+            if (!a.dense && key0 + 128 > kv_len) {
+                // stale slots past kv_len in the last page: zero their V rows so
+                // 0 * (stale NaN) cannot reach O
+                const int first = max(0, kv_len - key0);
+                for (int e = lane; e < (128 - first) * 2 * 8; e += 32) {
+                    const int row = first + e / 16, dh = (e >> 3) & 1, ch = e & 7;
+                    *reinterpret_cast<uint4*>(vt + dh * L::kHalf + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+                }
+                ptx::fence_proxy_async_smem();
                 __syncwarp();
             }
-            if (it >= 1) {
-                const int j = it - 1, vs = j % kNV;
-                if (!ptx::mbar_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u)) { ok = false; break; }
-                if (!ptx::mbar_wait(&v_full[vs], (uint32_t)(j / kNV) & 1u)) { ok = false; break; }
-                ptx::tc_fence_after();
-                uint8_t* vt = smem + L::kV + vs * L::kTile;
-                const int key0 = (tile_lo + j) * 128;
-                if (!a.dense && key0 + 128 > kv_len) {
-                    // stale slots past kv_len in the last page: zero their V rows so
-                    // 0 * (stale NaN) cannot reach O
-                    const int first = max(0, kv_len - key0);
-                    for (int e = lane; e < (128 - first) * 2 * 8; e += 32) {
-                        const int row = first + e / 16, dh = (e >> 3) & 1, ch = e & 7;
-                        *reinterpret_cast<uint4*>(vt + dh * L::kHalf + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
-                    }
-                    ptx::fence_proxy_async_smem();
-                    __syncwarp();
-                }
-                const uint32_t vb = ptx::smem_u32(vt);
-                const uint32_t aP = tmem + kColP + (uint32_t)(j & 1) * 64;
-                if (lane == 0) {
+            const uint32_t vb = ptx::smem_u32(vt);
+            const uint32_t aP = tmem + kColP + (uint32_t)(j & 1) * 64;
+            if (lane == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        ptx::umma_ts(tmem + kColO, aP + kk * 8, ptx::smem_desc_sw128(vb + kk * 2048, L::kHalf, 1024),
-                                     idPV, (j > 0 || kk > 0) ? 1u : 0u);
-                    ptx::umma_commit(&v_empty[vs]);
-                    ptx::umma_commit(&o_bar[j & 1]);
-                }
-                __syncwarp();
+                for (int kk = 0; kk < 8; ++kk)
+                    ptx::umma_ts(tmem + kColO, aP + kk * 8, ptx::smem_desc_sw128(vb + kk * 2048, L::kHalf, 1024), idPV,
+                                 (j > 0 || kk > 0) ? 1u : 0u);
+                ptx::umma_commit(&v_empty[vs]);
+                ptx::umma_commit(&o_bar[j & 1]);
             }
+            __syncwarp();
         }
         if (!ok && n_tiles > 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
-    } else {
+    } else if (warp >= 2 && warp <= 5) {
         // ================================================================ softmax warps
         const int q4 = warp & 3;
         const int r = q4 * 32 + lane;
@@ -279,20 +278,28 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         const bool valid_row = rr < rows_total;
         const int tok = rr / G, gh = rr - tok * G;
         const int pos = q0 + tok;
-        float* wbuf = reinterpret_cast<float*>(smem + L::kW) + (warp - 2) * 128;
-        const int cs = (p.clear_start || p.clear_start_const > 0) && p.fog_alpha > 0.f
-                           ? (p.clear_start ? p.clear_start[b] : p.clear_start_const) : INT_MIN;
-        const bool has_fog = p.fog_w != nullptr || cs > 0;
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
+        float* wbuf = reinterpret_cast<float*>(smem + L::kW) + (warp - 2) * 128;
+        const float inv_den = 1.f / (float)max(cs - 1, 1);
         for (int j = 0; j < n_tiles; ++j) {
             const int key0 = (tile_lo + j) * 128;
             if (has_fog) {
+                // this warp's copy of the tile's fog weights (kessie_hip_kernels.py:411-412):
+                // (key / (cs-1))^alpha as 2^(alpha * log2(key / (cs-1))) on the MUFU
+                float4 w4v;
+                float* w = &w4v.x;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int key = key0 + lane * 4 + e;
-                    wbuf[lane * 4 + e] = key < kv_len ? fog_w(p, b, cs, key) : 0.f;
+                    float x;
+                    if (key >= kv_len) x = 0.f;
+                    else if (p.fog_w) x = __ldg(p.fog_w + b * p.fog_w_sb + key);
+                    else if (key >= cs) x = 1.f;
+                    else x = ptx::ex2(p.fog_alpha * ptx::lg2((float)key * inv_den));
+                    w[e] = x;
                 }
+                reinterpret_cast<float4*>(wbuf)[lane] = w4v;
             }
             __syncwarp();
             if (!ptx::mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u)) { ok = false; break; }
@@ -305,34 +312,40 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
             // tile-uniform visibility: no per-element mask for interior tiles
             const bool interior = key0 + 128 <= kv_len && (!(p.causal || p.window > 0) || key0 + 127 <= pos_lo) &&
                                   (p.window <= 0 || key0 >= pos_hi - p.window + 1);
-            float mx = -INFINITY;
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            if (interior && valid_row) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 4; ++c)
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float s = __uint_as_float(sv[c][i]);
-                    if (!interior || !valid_row) {
+                    for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[c][i]));
+            } else {
+                // visible keys of this row: [lo_r, hi_r)
+                int hi_r = min(kv_len, (p.causal || p.window > 0) ? pos + 1 : kv_len);
+                int lo_r = p.window > 0 ? pos - p.window + 1 : 0;
+                if (!valid_row) hi_r = lo_r - 1;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
                         const int key = key0 + c * 32 + i;
-                        bool vis = valid_row && key < kv_len;
-                        if (p.causal || p.window > 0) vis = vis && key <= pos;
-                        if (p.window > 0) vis = vis && pos - key < p.window;
-                        s = vis ? s : -INFINITY;
-                        sv[c][i] = __float_as_uint(s);
+                        const float sx = (key >= lo_r && key < hi_r) ? __uint_as_float(sv[c][i]) : -INFINITY;
+                        sv[c][i] = __float_as_uint(sx);
+                        mx4[i & 3] = fmaxf(mx4[i & 3], sx);
                     }
-                    mx = fmaxf(mx, s);
-                }
+            }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             const float m_tile = mx == -INFINITY ? -INFINITY : mx * p.scale_log2;
             const float m_new = fmaxf(m_used, m_tile);
             const bool need = m_new != -INFINITY && (m_used == -INFINITY || m_new > m_used + kRescaleThreshold);
             float factor = 1.f;
             if (need) {
-                factor = m_used == -INFINITY ? 0.f : exp2f(m_used - m_new);
+                factor = m_used == -INFINITY ? 0.f : ptx::ex2(m_used - m_new);
                 l *= factor;
                 m_used = m_new;
             }
             // O rescale in TMEM (warp-collective; only when some row moved its max
             // after O already holds a partial sum)
-            if (__any_sync(0xffffffffu, need && factor != 0.f && j > 0) ) {
+            if (__any_sync(0xffffffffu, need && factor != 0.f && j > 0)) {
                 if (!ptx::mbar_wait(&o_bar[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u)) { ok = false; break; }
                 ptx::tc_fence_after();
                 const float f = (need && factor != 0.f) ? factor : 1.f;
@@ -347,26 +360,35 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 }
                 ptx::tmem_st_wait();
             }
-            const float base = m_used == -INFINITY ? 0.f : m_used;
-            float lt = 0.f;
+            // P buffer j%2 was last read by PV_{j-2}: wait for it before overwriting
+            if (j >= 2 && !ptx::mbar_wait(&o_bar[j & 1], (uint32_t)((j - 2) >> 1) & 1u)) { ok = false; break; }
+            ptx::tc_fence_after();
+            const float4* w4 = reinterpret_cast<const float4*>(wbuf);
+            const float nb = m_used == -INFINITY ? 0.f : -m_used;
+            float lt4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
                 uint32_t pk[32];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int c0 = h2 * 64 + 2 * i;          // key column
+                for (int i = 0; i < 32; i += 2) {
+                    const int c0 = h2 * 64 + 2 * i;          // key column (4 keys per step)
+                    const float4 w = has_fog ? w4[c0 >> 2] : make_float4(1.f, 1.f, 1.f, 1.f);
                     const float s0 = __uint_as_float(sv[c0 >> 5][c0 & 31]);
                     const float s1 = __uint_as_float(sv[(c0 + 1) >> 5][(c0 + 1) & 31]);
-                    const float p0 = exp2f(fmaf(s0, p.scale_log2, -base));
-                    const float p1 = exp2f(fmaf(s1, p.scale_log2, -base));
-                    lt += p0 + p1;
-                    const float w0 = has_fog ? wbuf[c0] : 1.f, w1 = has_fog ? wbuf[c0 + 1] : 1.f;
-                    pk[i] = ptx::pack2<BF16>(p0 * w0, p1 * w1);
+                    const float s2 = __uint_as_float(sv[(c0 + 2) >> 5][(c0 + 2) & 31]);
+                    const float s3 = __uint_as_float(sv[(c0 + 3) >> 5][(c0 + 3) & 31]);
+                    const float p0 = ptx::ex2(fmaf(s0, p.scale_log2, nb));
+                    const float p1 = ptx::ex2(fmaf(s1, p.scale_log2, nb));
+                    const float p2 = ptx::ex2(fmaf(s2, p.scale_log2, nb));
+                    const float p3 = ptx::ex2(fmaf(s3, p.scale_log2, nb));
+                    lt4[0] += p0; lt4[1] += p1; lt4[2] += p2; lt4[3] += p3;
+                    pk[i] = ptx::pack2<BF16>(p0 * w.x, p1 * w.y);
+                    pk[i + 1] = ptx::pack2<BF16>(p2 * w.z, p3 * w.w);
                 }
                 ptx::tmem_st32(tmem + lane_off + kColP + (uint32_t)(j & 1) * 64 + h2 * 32, pk);
             }
             ptx::tmem_st_wait();
-            l += lt;
+            l += (lt4[0] + lt4[1]) + (lt4[2] + lt4[3]);
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&p_full[j & 1]);

@@ -124,6 +124,20 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     return r;
 }
 
+// 2^x with the MUFU approximation (flush-to-zero): one instruction.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// log2(x) with the MUFU approximation (flush-to-zero): one instruction.
+__device__ __forceinline__ float lg2(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ------------------------------------------------------------------ tcgen05 (5th-gen tensor cores, TMEM)
 // TMEM address: bits [31:16] lane, [15:0] column (32-bit cells).
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
