@@ -296,6 +296,28 @@ int kessie_paged_fog_decode_noalloc_v2(const void* q, int64_t q_stride_b, int64_
                                        int num_kv_heads, int head_dim, int max_seq_len, int dtype,
                                        void* out, float* out_partial, void* stream);
 
+/* kessie_paged_fog_prefill_v2 with a staging workspace: the visible keys of
+ * every sequence (kv_lens[b] <= max_kv_len) are first gathered from the pages
+ * into workspace as head-major [B][Hkv][kv][D] K and V, so the tensor-core
+ * kernel streams 128-token tiles from contiguous memory.  Same results as the
+ * unstaged call.  workspace: kessie_paged_fog_prefill_workspace_size() bytes;
+ * NULL workspace runs the unstaged kernel. */
+size_t kessie_paged_fog_prefill_workspace_size(int batch, int num_kv_heads, int head_dim,
+                                               int max_kv_len);
+int kessie_paged_fog_prefill_ex_v2(const void* q, int64_t q_stride_b, int64_t q_stride_t,
+                                   int64_t q_stride_h, const void* k_cache, const void* v_cache,
+                                   int64_t page_stride, int64_t token_stride, int64_t head_stride,
+                                   int num_pages, int page_size, const int32_t* block_table,
+                                   int64_t block_table_stride, const int32_t* kv_lens,
+                                   const int32_t* q_start, const int32_t* clear_start,
+                                   float fog_alpha, const float* fog_weights,
+                                   int64_t fog_weights_stride_b, int window_size, int is_causal,
+                                   float sm_scale, int batch, int num_q_tokens, int num_q_heads,
+                                   int num_kv_heads, int head_dim, int dtype, void* out,
+                                   int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h,
+                                   int max_kv_len, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
 /* Log-sum-exp merge of S partial triples [S][rows][D+2] (split_stride
  * elements apart) -> out [rows, D] (out_dtype) and/or out_partial
  * [rows, D+2].  Used for the context-parallel combine after the NCCL

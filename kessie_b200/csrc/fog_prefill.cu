@@ -336,6 +336,53 @@ int run_prefill(const PrefillParams& p, const void* kc, const void* vc, int64_t 
     return bf16 ? launch_prefill_t<64, true>(mk, mv, p, st) : launch_prefill_t<64, false>(mk, mv, p, st);
 }
 
+// Copy the first kv_len keys of every sequence from the paged cache into a
+// head-major staging buffer [B][Hkv][kv_max][D] (K and V), zero-filling rows
+// [kv_len, kv_pad) so the tile that straddles kv_len reads zeros.  The
+// tcgen05 prefill then streams 128-token TMA boxes from contiguous memory
+// instead of 16-token boxes scattered over pages (a TMA box costs a fixed
+// ~130 SM cycles, so 2 KB boxes cannot feed the tensor cores).
+// grid (ceil(kv_max / page_size), B); threads over (kv, head, 16-byte chunk).
+template <typename T>
+__global__ void __launch_bounds__(256) stage_kv_kernel(const T* __restrict__ kc, const T* __restrict__ vc,
+                                                       int64_t page_stride, int64_t token_stride, int64_t head_stride,
+                                                       int num_pages, int ps, const int32_t* __restrict__ bt,
+                                                       int64_t bt_stride, const int32_t* __restrict__ kv_lens,
+                                                       int max_kv_len, int kv_max, int Hkv, int D,
+                                                       T* __restrict__ sk, T* __restrict__ sv, int* status) {
+    const int pg = blockIdx.x, b = blockIdx.y;
+    int kv_len = kv_lens[b];
+    if (kv_len > max_kv_len || kv_len < 0) {          // the block table holds max_kv_len keys at most
+        if (pg == 0 && threadIdx.x == 0) record_status(status, KESSIE_DEV_BAD_ARG);
+        kv_len = kv_len < 0 ? 0 : max_kv_len;
+    }
+    const int kv_pad = min(kv_max, (kv_len + 127) / 128 * 128);
+    const int t0 = pg * ps;
+    if (t0 >= kv_pad) return;
+    int id = -1;
+    if (t0 < kv_len) {
+        id = bt[(int64_t)b * bt_stride + pg];
+        if (id < 0 || id >= num_pages) {
+            if (threadIdx.x == 0) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
+            id = -1;
+        }
+    }
+    const int chunks = D / 8;
+    const int items = 2 * Hkv * chunks;
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+        const int kv = it / (Hkv * chunks);
+        const int r = it - kv * Hkv * chunks;
+        const int h = r / chunks, c = r - h * chunks;
+        const T* src = (kv ? vc : kc) + (int64_t)(id < 0 ? 0 : id) * page_stride + (int64_t)h * head_stride + c * 8;
+        T* dst = (kv ? sv : sk) + (((int64_t)b * Hkv + h) * kv_max + t0) * D + c * 8;
+        for (int s = 0; s < ps && t0 + s < kv_pad; ++s) {
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (id >= 0 && t0 + s < kv_len) v = ldg_stream(src + (int64_t)s * token_stride);
+            *reinterpret_cast<uint4*>(dst + (int64_t)s * D) = v;
+        }
+    }
+}
+
 // Legacy dense [B,H,N,D] fp16 entry (kessie_kernels_v2.hip:716-751 / :788-825).
 void legacy_dense(const void* Q, const void* K, const void* V, void* O, const void* fog, float sm_scale, int B, int H,
                   int N, int D, int W, int causal, void* stream, const char* name) {
@@ -409,13 +456,20 @@ extern "C" int kessie_fog_attention_v2(const void* q, const void* k, const void*
     return run_prefill(p, k, v, ksb, head_dim, sh, batch, seq_len, head_dim, dtype == KESSIE_DTYPE_BF16, as_stream(stream));
 }
 
-extern "C" int kessie_paged_fog_prefill_v2(
+extern "C" size_t kessie_paged_fog_prefill_workspace_size(int batch, int num_kv_heads, int head_dim, int max_kv_len) {
+    if (batch <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_kv_len <= 0) return 0;
+    const size_t kv_max = (size_t)(max_kv_len + 127) / 128 * 128;
+    return 2 * (size_t)batch * num_kv_heads * kv_max * head_dim * 2 + 256;
+}
+
+extern "C" int kessie_paged_fog_prefill_ex_v2(
     const void* q, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache, const void* v_cache,
     int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
     const int32_t* block_table, int64_t block_table_stride, const int32_t* kv_lens, const int32_t* q_start,
     const int32_t* clear_start, float fog_alpha, const float* fog_weights, int64_t fog_weights_stride_b,
     int window_size, int is_causal, float sm_scale, int batch, int num_q_tokens, int num_q_heads, int num_kv_heads,
-    int head_dim, int dtype, void* out, int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h, void* stream) {
+    int head_dim, int dtype, void* out, int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h, int max_kv_len,
+    void* workspace, size_t workspace_bytes, void* stream) {
     if (dtype != KESSIE_DTYPE_BF16 && dtype != KESSIE_DTYPE_F16)
         return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_prefill_v2: dtype %d (f16/bf16 only)", dtype);
     if (head_dim != 64 && head_dim != 128)
@@ -440,6 +494,53 @@ extern "C" int kessie_paged_fog_prefill_v2(
     p.B = batch; p.Hq = num_q_heads; p.Hkv = num_kv_heads; p.G = num_q_heads / num_kv_heads;
     p.upp = page_size / 16; p.num_pages = num_pages;
     p.status = device_status_ptr();
+    const bool bf16 = dtype == KESSIE_DTYPE_BF16;
+    cudaStream_t st = as_stream(stream);
+    if (workspace && max_kv_len > 0 && head_dim % 8 == 0 && ((reinterpret_cast<uintptr_t>(workspace) & 15) == 0) &&
+        ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) == 0) {
+        const size_t need = kessie_paged_fog_prefill_workspace_size(batch, num_kv_heads, head_dim, max_kv_len);
+        if (workspace_bytes < need)
+            return set_error(KESSIE_ERR_WORKSPACE, "paged_fog_prefill_ex_v2: workspace %zu < %zu", workspace_bytes, need);
+        const int kv_max = (max_kv_len + 127) / 128 * 128;
+        const size_t half = (size_t)batch * num_kv_heads * kv_max * head_dim;     // elements per K (or V)
+        dim3 grid((kv_max + page_size - 1) / page_size, batch);
+        if (bf16) {
+            auto* sk = static_cast<__nv_bfloat16*>(workspace);
+            stage_kv_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+                (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache, page_stride, token_stride, head_stride,
+                num_pages, page_size, block_table, block_table_stride, kv_lens, max_kv_len, kv_max, num_kv_heads, head_dim,
+                sk, sk + half, p.status);
+        } else {
+            auto* sk = static_cast<__half*>(workspace);
+            stage_kv_kernel<__half><<<grid, 256, 0, st>>>(
+                (const __half*)k_cache, (const __half*)v_cache, page_stride, token_stride, head_stride, num_pages,
+                page_size, block_table, block_table_stride, kv_lens, max_kv_len, kv_max, num_kv_heads, head_dim, sk,
+                sk + half, p.status);
+        }
+        int rc = check_launch("prefill staging");
+        if (rc) return rc;
+        // dense view of the staging buffer: page coordinate = sequence, token = position
+        p.block_table = nullptr;
+        p.num_pages = batch;
+        const char* base = static_cast<const char*>(workspace);
+        return run_prefill(p, base, base + half * 2, (int64_t)num_kv_heads * kv_max * head_dim, head_dim,
+                           (int64_t)kv_max * head_dim, batch, kv_max, head_dim, bf16, st);
+    }
     return run_prefill(p, k_cache, v_cache, page_stride, token_stride, head_stride, num_pages, page_size, head_dim,
-                       dtype == KESSIE_DTYPE_BF16, as_stream(stream));
+                       bf16, st);
+}
+
+extern "C" int kessie_paged_fog_prefill_v2(
+    const void* q, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+    int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
+    const int32_t* block_table, int64_t block_table_stride, const int32_t* kv_lens, const int32_t* q_start,
+    const int32_t* clear_start, float fog_alpha, const float* fog_weights, int64_t fog_weights_stride_b,
+    int window_size, int is_causal, float sm_scale, int batch, int num_q_tokens, int num_q_heads, int num_kv_heads,
+    int head_dim, int dtype, void* out, int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h, void* stream) {
+    return kessie_paged_fog_prefill_ex_v2(q, q_stride_b, q_stride_t, q_stride_h, k_cache, v_cache, page_stride,
+                                          token_stride, head_stride, num_pages, page_size, block_table,
+                                          block_table_stride, kv_lens, q_start, clear_start, fog_alpha, fog_weights,
+                                          fog_weights_stride_b, window_size, is_causal, sm_scale, batch, num_q_tokens,
+                                          num_q_heads, num_kv_heads, head_dim, dtype, out, o_stride_b, o_stride_t,
+                                          o_stride_h, 0, nullptr, 0, stream);
 }

@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         const int32_t* bt = a.dense ? nullptr : p.block_table + (int64_t)b * p.bt_stride;
         const int ps = a.page_size, bxt = a.box_tokens, nbox = 128 / bxt;
         const int kv_pages = a.dense ? 0 : (kv_len + ps - 1) / ps;
-        const uint64_t pol = ptx::policy_evict_first();
+        const uint64_t pol = ptx::policy_evict_last();
         if (lane == 0 && n_tiles > 0) {
             ptx::prefetch_tensormap(map);
             if (is_k) {
@@ -152,24 +152,32 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
             }
         }
         int ids_reg = -1, ids_base = -(1 << 30);
+        int nxt_reg = -1, nxt_base = -(1 << 30);
+        auto load_ids = [&](int base) -> int {
+            const int pi = base + lane;
+            int id = -1;
+            if (pi < kv_pages) {
+                id = __ldg(bt + pi);
+                if (id < 0 || id >= p.num_pages) {
+                    if (is_k) record_status(p.status, KESSIE_DEV_BAD_PAGE_ID);
+                    id = -1;
+                }
+            }
+            return id;
+        };
         int issued = 0;
         for (int it = 0; it < n_tiles; ++it) {
             const int key0 = (tile_lo + it) * 128;
-            // page ids of this tile (at most 8 pages); one warp-wide load covers 32 pages
+            // page ids of this tile (at most 8 pages) from a 32-page window; the
+            // next window is loaded one window ahead so the issue loop never
+            // waits on the page table
             if (!a.dense) {
                 const int pg_first = key0 / ps, pg_last = (key0 + 127) / ps;
                 if (pg_first < ids_base || pg_last >= ids_base + 32) {
-                    ids_base = pg_first;
-                    const int pi = ids_base + lane;
-                    int id = -1;
-                    if (pi < kv_pages) {
-                        id = __ldg(bt + pi);
-                        if (id < 0 || id >= p.num_pages) {
-                            if (is_k) record_status(p.status, KESSIE_DEV_BAD_PAGE_ID);
-                            id = -1;
-                        }
-                    }
-                    ids_reg = id;
+                    if (nxt_base == pg_first) { ids_base = nxt_base; ids_reg = nxt_reg; }
+                    else { ids_base = pg_first; ids_reg = load_ids(ids_base); }
+                    nxt_base = ids_base + 32;
+                    nxt_reg = load_ids(nxt_base);
                 }
             }
             int pages[8];

@@ -306,10 +306,14 @@ def fog_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, fog_weights
 def paged_fog_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                       kv_lens, q_start=None, clear_start=None, fog_alpha: float = 0.5, fog_weights=None,
                       window_size: int = 0, causal: bool = True, sm_scale: Optional[float] = None,
-                      out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, stream=None, staged: bool = True,
+                      max_kv_len: Optional[int] = None) -> torch.Tensor:
     """Chunked prefill: q [B, T, Hq, D] (query t of sequence b at position
     q_start[b] + t, default kv_lens[b] - T) over k_cache / v_cache
-    [P, ps, Hkv, D] views through block_table [B, maxP]."""
+    [P, ps, Hkv, D] views through block_table [B, maxP].  With staged=True the
+    visible K/V are first gathered into a cached head-major workspace so the
+    tensor-core kernel reads 128-token tiles (max_kv_len bounds kv_lens;
+    default: the block table's capacity)."""
     _need_cuda(q, k_cache, v_cache, block_table)
     B, T, Hq, D = q.shape
     P, ps, Hkv, Dk = k_cache.shape
@@ -333,10 +337,18 @@ def paged_fog_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
     if out is None:
         out = torch.empty_like(q)
     lib = _lib.load()
-    _lib.check(lib.kessie_paged_fog_prefill_v2(
+    ws_ptr, ws_n, mkv = None, 0, 0
+    if staged:
+        mkv = int(max_kv_len) if max_kv_len is not None else bt.shape[1] * ps
+        if mkv > bt.shape[1] * ps:
+            raise ValueError(f"max_kv_len {mkv} exceeds the block table capacity {bt.shape[1] * ps}")
+        ws_n = lib.kessie_paged_fog_prefill_workspace_size(B, Hkv, D, mkv)
+        ws = workspace(ws_n, q.device, "prefill_stage")
+        ws_ptr, ws_n = ws.data_ptr(), ws.numel()
+    _lib.check(lib.kessie_paged_fog_prefill_ex_v2(
         q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k_cache.data_ptr(), v_cache.data_ptr(),
         k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), kl.data_ptr(),
         _p(qs), _p(cs), float(fog_alpha), _p(fw), fw_sb, int(window_size), 1 if causal else 0, float(sm_scale),
-        B, T, Hq, Hkv, D, dtype_code(q), out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
-        _stream(stream)), "paged_fog_prefill")
+        B, T, Hq, Hkv, D, dtype_code(q), out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), mkv, ws_ptr,
+        ws_n, _stream(stream)), "paged_fog_prefill")
     return out

@@ -100,11 +100,12 @@ def test_fog_attention_v2_gqa(dt, B, Hq, Hkv, N, D, W, causal):
     np.testing.assert_allclose(to_np(out), want, **TOL[dt])
 
 
+@pytest.mark.parametrize("staged", [True, False])
 @pytest.mark.parametrize("ps", [16, 32])
 @pytest.mark.parametrize("Hq,Hkv,kv_len,T,W,fogw", [(32, 8, 1000, 100, 0, 256), (8, 2, 333, 333, 0, 64),
                                                     (8, 8, 2048, 64, 300, 100), (16, 4, 500, 1, 0, 0),
                                                     (4, 1, 4111, 257, 0, 4096)])
-def test_paged_prefill_matches_oracle(ps, Hq, Hkv, kv_len, T, W, fogw):
+def test_paged_prefill_matches_oracle(staged, ps, Hq, Hkv, kv_len, T, W, fogw):
     from kessie_b200 import ops
     D, dt = 128, "bf16"
     lens = [kv_len]
@@ -116,14 +117,15 @@ def test_paged_prefill_matches_oracle(ps, Hq, Hkv, kv_len, T, W, fogw):
     out = ops.paged_fog_prefill(to_dev(q, dt), kv[:, :, 0], kv[:, :, 1], torch.from_numpy(bt).cuda(),
                                 torch.tensor([kv_len], dtype=torch.int32, device="cuda"),
                                 clear_start=torch.tensor([cs], dtype=torch.int32, device="cuda"), fog_alpha=0.5,
-                                window_size=W)
+                                window_size=W, staged=staged)
     torch.cuda.synchronize()
     want = O.paged_fog_prefill(np.transpose(q[0], (1, 0, 2)), kvn[:, :, 0], kvn[:, :, 1], bt[0], kv_len, kv_len - T,
                                cs, 0.5, W)
     np.testing.assert_allclose(to_np(out)[0], np.transpose(want, (1, 0, 2)), **TOL[dt])
 
 
-def test_paged_prefill_batched_with_stale_nan_and_qstart():
+@pytest.mark.parametrize("staged", [True, False])
+def test_paged_prefill_batched_with_stale_nan_and_qstart(staged):
     from kessie_b200 import ops
     D, dt, ps, Hq, Hkv = 64, "fp16", 16, 8, 2
     lens = [90, 200]
@@ -137,7 +139,7 @@ def test_paged_prefill_batched_with_stale_nan_and_qstart():
     qs = np.array([50, 160], np.int32)
     out = ops.paged_fog_prefill(to_dev(q, dt), kv[:, :, 0], kv[:, :, 1], torch.from_numpy(bt).cuda(),
                                 torch.tensor(lens, dtype=torch.int32, device="cuda"),
-                                q_start=torch.from_numpy(qs).cuda(), clear_start=None, fog_alpha=0.0)
+                                q_start=torch.from_numpy(qs).cuda(), clear_start=None, fog_alpha=0.0, staged=staged)
     torch.cuda.synchronize()
     got = to_np(out)
     assert np.isfinite(got).all()
