@@ -34,22 +34,22 @@
 namespace kessie {
 namespace {
 
-constexpr int kNK = 3;                 // K stages
+constexpr int kNK = 2;                 // K stages
 constexpr int kNV = 2;                 // V stages
-constexpr int kThreads = 224;     // 7 warps: K producer, MMA, 4 softmax, V producer
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
+constexpr int kThreads = 352;          // 11 warps: K producer, MMA, 2 x 4 softmax, V producer
+constexpr int kRowsPerCta = 256;       // two 128-row Q tiles (A, B)
+constexpr uint32_t kTmemCols = 512;    // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
 constexpr float kRescaleThreshold = 8.0f;    // log2 units
 
 struct L {
     static constexpr int kHalf = 128 * 128;         // [128 rows][64 el] x 2 B
     static constexpr int kTile = 2 * kHalf;         // both d-halves: 32 KB
-    static constexpr int kQ = 0;
-    static constexpr int kK = kQ + kTile;
+    static constexpr int kQ = 0;                    // Q_A, Q_B
+    static constexpr int kK = kQ + 2 * kTile;
     static constexpr int kV = kK + kNK * kTile;
     static constexpr int kW = kV + kNV * kTile;     // per softmax warp: fog weights of the tile's 128 keys
-    static constexpr int kBar = kW + 4 * 128 * 4;
-    // q_full, k_full[3], k_empty[3], v_full[2], v_empty[2], s_full[2], p_full[2], o_bar[2]
+    static constexpr int kBar = kW + 8 * 128 * 4;
+    // q_full, k_full[NK], k_empty[NK], v_full[NV], v_empty[NV], s_full[2], p_full[2], o_bar[2]
     static constexpr int kNumBar = 1 + 2 * kNK + 2 * kNV + 6;
     static constexpr int kSlot = kBar + kNumBar * 8;
     static constexpr int kBytes = kSlot + 16;
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
     uint64_t* k_empty = k_full + kNK;
     uint64_t* v_full = k_empty + kNK;
     uint64_t* v_empty = v_full + kNV;
-    uint64_t* s_full = v_empty + kNV;
+    uint64_t* s_full = v_empty + kNV;      // [2]: Q tile A, B
     uint64_t* p_full = s_full + 2;
     uint64_t* o_bar = p_full + 2;
     uint32_t* slot = reinterpret_cast<uint32_t*>(smem + L::kSlot);
@@ -88,18 +88,17 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
     const int hk = blockIdx.y, b = blockIdx.z;
     const int G = p.G;
     const int rows_total = p.Nq * G;
-    const int row0 = tile_m * 128;
+    const int row0 = tile_m * kRowsPerCta;
     const int kv_len = p.kv_lens ? p.kv_lens[b] : p.kv_len_const;
     const int q0 = p.q_start ? p.q_start[b] : (p.q_start_const >= 0 ? p.q_start_const : kv_len - p.Nq);
     const int t_first = row0 / G;
-    const int t_last = (min(row0 + 128, rows_total) - 1) / G;
+    const int t_last = (min(row0 + kRowsPerCta, rows_total) - 1) / G;
     const int pos_lo = q0 + t_first, pos_hi = q0 + t_last;
     int j_lo = p.window > 0 ? max(0, pos_lo - p.window + 1) : 0;
     int j_hi = (p.causal || p.window > 0) ? min(kv_len, pos_hi + 1) : kv_len;
     if (j_hi < j_lo) j_hi = j_lo;
     const int tile_lo = j_lo / 128, tile_hi = (j_hi + 127) / 128;
     const int n_tiles = tile_hi - tile_lo;
-
     const int cs = (p.clear_start || p.clear_start_const > 0) && p.fog_alpha > 0.f
                        ? (p.clear_start ? p.clear_start[b] : p.clear_start_const) : INT_MIN;
     const bool has_fog = p.fog_w != nullptr || cs > 0;
@@ -124,10 +123,9 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
     ptx::tc_fence_after();
     const uint32_t tmem = *slot;
 
-    if (warp == 0 || warp == 6) {
+    if (warp == 0 || warp == 10) {
         // ================================================================ producers
-        // warp 0: Q, then the K ring; warp 6: the V ring.  Separate warps so a
-        // V stage waiting for its PV MMA never holds back the K prefetch.
+        // warp 0: Q (both tiles), then the K ring; warp 10: the V ring.
         const bool is_k = warp == 0;
         const int NS = is_k ? kNK : kNV;
         uint64_t* full = is_k ? k_full : v_full;
@@ -142,13 +140,16 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
             ptx::prefetch_tensormap(map);
             if (is_k) {
                 ptx::prefetch_tensormap(&tmQ);
-                ptx::mbar_arrive_expect_tx(q_full, (uint32_t)L::kTile);
-                for (int dh = 0; dh < 2; ++dh) {
-                    if (a.q_mode == 0)
-                        ptx::tma_load_5d(smem + L::kQ + dh * L::kHalf, &tmQ, q_full, 0, 0, b * p.Nq + row0 / G, dh, hk);
-                    else
-                        ptx::tma_load_5d(smem + L::kQ + dh * L::kHalf, &tmQ, q_full, 0, row0, dh, hk, b);
-                }
+                ptx::mbar_arrive_expect_tx(q_full, (uint32_t)(2 * L::kTile));
+                for (int qt = 0; qt < 2; ++qt)
+                    for (int dh = 0; dh < 2; ++dh) {
+                        uint8_t* dst = smem + L::kQ + qt * L::kTile + dh * L::kHalf;
+                        const int r0 = row0 + qt * 128;
+                        if (a.q_mode == 0)
+                            ptx::tma_load_5d(dst, &tmQ, q_full, 0, 0, b * p.Nq + r0 / G, dh, hk);
+                        else
+                            ptx::tma_load_5d(dst, &tmQ, q_full, 0, r0, dh, hk, b);
+                    }
             }
         }
         int ids_reg = -1, ids_base = -(1 << 30);
@@ -169,8 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         for (int it = 0; it < n_tiles; ++it) {
             const int key0 = (tile_lo + it) * 128;
             // page ids of this tile (at most 8 pages) from a 32-page window; the
-            // next window is loaded one window ahead so the issue loop never
-            // waits on the page table
+            // next window is loaded one window ahead
             if (!a.dense) {
                 const int pg_first = key0 / ps, pg_last = (key0 + 127) / ps;
                 if (pg_first < ids_base || pg_last >= ids_base + 32) {
@@ -216,47 +216,58 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         }
     } else if (warp == 1) {
         // ================================================================ MMA issuer
-        // order: S_0, S_1, then per tile j: [wait P_j] S_{j+2}, [wait V_j] PV_j.
-        // S_{j+2} reuses S buffer j%2 (softmax j has read it); P buffers are
-        // separate, and softmax j+2 waits for PV_j before overwriting P j%2.
+        // S_A(0) S_B(0) | per tile t: [P_A(t)] PV_A(t) S_A(t+1) | [P_B(t)] PV_B(t) S_B(t+1)
+        // One thread issues everything, in order: S_X(t+1) overwrites the S/P
+        // region X only after PV_X(t) has consumed P_X(t), and the commit that
+        // publishes S_X(t+1) also covers PV_X(t).
         const uint32_t idS = ptx::umma_idesc_f16(BF16, false, 128);
         const uint32_t idPV = ptx::umma_idesc_f16(BF16, true, 128);
         const uint32_t qa = ptx::smem_u32(smem + L::kQ);
         bool ok = n_tiles > 0 && ptx::mbar_wait(q_full, 0);
         ptx::tc_fence_after();
-        auto issue_s = [&](int t) -> bool {
-            const int ks = t % kNK;
-            if (!ptx::mbar_wait(&k_full[ks], (uint32_t)(t / kNK) & 1u)) return false;
-            ptx::tc_fence_after();
-            const uint32_t kb = ptx::smem_u32(smem + L::kK + ks * L::kTile);
-            const uint32_t dS = tmem + kColS + (uint32_t)(t & 1) * 128;
+        auto issue_s = [&](int t, int x) {
+            const uint32_t kb = ptx::smem_u32(smem + L::kK + (t % kNK) * L::kTile);
+            const uint32_t qx = qa + (uint32_t)(x * L::kTile);
+            const uint32_t dS = tmem + (uint32_t)(x * 128);
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t off = (uint32_t)((kk >> 2) * L::kHalf + (kk & 3) * 32);
-                    ptx::umma_ss(dS, ptx::smem_desc_sw128(qa + off, 16, 1024), ptx::smem_desc_sw128(kb + off, 16, 1024),
+                    ptx::umma_ss(dS, ptx::smem_desc_sw128(qx + off, 16, 1024), ptx::smem_desc_sw128(kb + off, 16, 1024),
                                  idS, kk > 0 ? 1u : 0u);
                 }
-                ptx::umma_commit(&s_full[t & 1]);
-                ptx::umma_commit(&k_empty[ks]);
+                ptx::umma_commit(&s_full[x]);
+                if (x == 1) ptx::umma_commit(&k_empty[t % kNK]);
             }
             __syncwarp();
-            return true;
         };
-        if (ok) ok = issue_s(0);
-        if (ok && n_tiles > 1) ok = issue_s(1);
-        for (int j = 0; ok && j < n_tiles; ++j) {
-            if (!ptx::mbar_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u)) { ok = false; break; }
-            if (j + 2 < n_tiles && !issue_s(j + 2)) { ok = false; break; }
-            const int vs = j % kNV;
-            if (!ptx::mbar_wait(&v_full[vs], (uint32_t)(j / kNV) & 1u)) { ok = false; break; }
+        auto issue_pv = [&](int t, int x) {
+            const uint32_t vb = ptx::smem_u32(smem + L::kV + (t % kNV) * L::kTile);
+            const uint32_t aP = tmem + (uint32_t)(x * 128);
+            const uint32_t dO = tmem + 256 + (uint32_t)(x * 128);
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    ptx::umma_ts(dO, aP + kk * 8, ptx::smem_desc_sw128(vb + kk * 2048, L::kHalf, 1024), idPV,
+                                 (t > 0 || kk > 0) ? 1u : 0u);
+                ptx::umma_commit(&o_bar[x]);
+                if (x == 1) ptx::umma_commit(&v_empty[t % kNV]);
+            }
+            __syncwarp();
+        };
+        if (ok) {
+            ok = ptx::mbar_wait(&k_full[0], 0);
             ptx::tc_fence_after();
-            uint8_t* vt = smem + L::kV + vs * L::kTile;
-            const int key0 = (tile_lo + j) * 128;
-            if (!a.dense && key0 + 128 > kv_len) {
+            if (ok) { issue_s(0, 0); issue_s(0, 1); }
+        }
+        for (int t = 0; ok && t < n_tiles; ++t) {
+            const bool more = t + 1 < n_tiles;
+            if (!ptx::mbar_wait(&v_full[t % kNV], (uint32_t)(t / kNV) & 1u)) { ok = false; break; }
+            if (!a.dense && (tile_lo + t) * 128 + 128 > kv_len) {
                 // stale slots past kv_len in the last page: zero their V rows so
                 // 0 * (stale NaN) cannot reach O
-                const int first = max(0, kv_len - key0);
+                uint8_t* vt = smem + L::kV + (t % kNV) * L::kTile;
+                const int first = max(0, kv_len - (tile_lo + t) * 128);
                 for (int e = lane; e < (128 - first) * 2 * 8; e += 32) {
                     const int row = first + e / 16, dh = (e >> 3) & 1, ch = e & 7;
                     *reinterpret_cast<uint4*>(vt + dh * L::kHalf + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
@@ -264,28 +275,33 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 ptx::fence_proxy_async_smem();
                 __syncwarp();
             }
-            const uint32_t vb = ptx::smem_u32(vt);
-            const uint32_t aP = tmem + kColP + (uint32_t)(j & 1) * 64;
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    ptx::umma_ts(tmem + kColO, aP + kk * 8, ptx::smem_desc_sw128(vb + kk * 2048, L::kHalf, 1024), idPV,
-                                 (j > 0 || kk > 0) ? 1u : 0u);
-                ptx::umma_commit(&v_empty[vs]);
-                ptx::umma_commit(&o_bar[j & 1]);
+            if (more && !ptx::mbar_wait(&k_full[(t + 1) % kNK], (uint32_t)((t + 1) / kNK) & 1u)) { ok = false; break; }
+            for (int x = 0; x < 2; ++x) {
+                if (!ptx::mbar_wait(&p_full[x], (uint32_t)t & 1u)) { ok = false; break; }
+                ptx::tc_fence_after();
+                issue_pv(t, x);
+                if (more) issue_s(t + 1, x);
             }
-            __syncwarp();
         }
         if (!ok && n_tiles > 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
-    } else if (warp >= 2 && warp <= 5) {
-        // ================================================================ softmax warps
+    } else {
+        // ================================================================ softmax warpgroups
+        const int x = (warp - 2) >> 2;                 // Q tile: 0 (warps 2-5) or 1 (warps 6-9)
         const int q4 = warp & 3;
         const int r = q4 * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-        const int rr = row0 + r;
+        const uint32_t sreg = tmem + lane_off + (uint32_t)(x * 128);
+        const uint32_t oreg = tmem + lane_off + 256 + (uint32_t)(x * 128);
+        const int rr = row0 + x * 128 + r;
         const bool valid_row = rr < rows_total;
         const int tok = rr / G, gh = rr - tok * G;
         const int pos = q0 + tok;
+        // this Q tile's position range (interior-tile test)
+        const int xr0 = min(row0 + x * 128, rows_total - 1), xr1 = min(row0 + x * 128 + 127, rows_total - 1);
+        const int xpos_lo = q0 + xr0 / G, xpos_hi = q0 + xr1 / G;
+        int hi_r = min(kv_len, (p.causal || p.window > 0) ? pos + 1 : kv_len);
+        int lo_r = p.window > 0 ? pos - p.window + 1 : 0;
+        if (!valid_row) hi_r = lo_r - 1;
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
         float* wbuf = reinterpret_cast<float*>(smem + L::kW) + (warp - 2) * 128;
@@ -300,26 +316,24 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int key = key0 + lane * 4 + e;
-                    float x;
-                    if (key >= kv_len) x = 0.f;
-                    else if (p.fog_w) x = __ldg(p.fog_w + b * p.fog_w_sb + key);
-                    else if (key >= cs) x = 1.f;
-                    else x = ptx::ex2(p.fog_alpha * ptx::lg2((float)key * inv_den));
-                    w[e] = x;
+                    float wv;
+                    if (key >= kv_len) wv = 0.f;
+                    else if (p.fog_w) wv = __ldg(p.fog_w + b * p.fog_w_sb + key);
+                    else if (key >= cs) wv = 1.f;
+                    else wv = ptx::ex2(p.fog_alpha * ptx::lg2((float)key * inv_den));
+                    w[e] = wv;
                 }
                 reinterpret_cast<float4*>(wbuf)[lane] = w4v;
             }
             __syncwarp();
-            if (!ptx::mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u)) { ok = false; break; }
+            if (!ptx::mbar_wait(&s_full[x], (uint32_t)j & 1u)) { ok = false; break; }
             ptx::tc_fence_after();
             uint32_t sv[4][32];
-            const uint32_t sbase = tmem + lane_off + kColS + (uint32_t)(j & 1) * 128;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) ptx::tmem_ld32(sbase + c * 32, sv[c]);
+            for (int c = 0; c < 4; ++c) ptx::tmem_ld32(sreg + c * 32, sv[c]);
             ptx::tmem_ld_wait();
-            // tile-uniform visibility: no per-element mask for interior tiles
-            const bool interior = key0 + 128 <= kv_len && (!(p.causal || p.window > 0) || key0 + 127 <= pos_lo) &&
-                                  (p.window <= 0 || key0 >= pos_hi - p.window + 1);
+            const bool interior = key0 + 128 <= kv_len && (!(p.causal || p.window > 0) || key0 + 127 <= xpos_lo) &&
+                                  (p.window <= 0 || key0 >= xpos_hi - p.window + 1);
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             if (interior && valid_row) {
 #pragma unroll
@@ -327,10 +341,6 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
 #pragma unroll
                     for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[c][i]));
             } else {
-                // visible keys of this row: [lo_r, hi_r)
-                int hi_r = min(kv_len, (p.causal || p.window > 0) ? pos + 1 : kv_len);
-                int lo_r = p.window > 0 ? pos - p.window + 1 : 0;
-                if (!valid_row) hi_r = lo_r - 1;
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -351,26 +361,21 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 l *= factor;
                 m_used = m_new;
             }
-            // O rescale in TMEM (warp-collective; only when some row moved its max
-            // after O already holds a partial sum)
+            // O rescale in TMEM (warp-collective, rare).  PV(j-1) is complete:
+            // the commit that published S(j) was issued after it.
             if (__any_sync(0xffffffffu, need && factor != 0.f && j > 0)) {
-                if (!ptx::mbar_wait(&o_bar[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u)) { ok = false; break; }
-                ptx::tc_fence_after();
                 const float f = (need && factor != 0.f) ? factor : 1.f;
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
                     uint32_t ov[32];
-                    ptx::tmem_ld32(tmem + lane_off + kColO + c * 32, ov);
+                    ptx::tmem_ld32(oreg + c * 32, ov);
                     ptx::tmem_ld_wait();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * f);
-                    ptx::tmem_st32(tmem + lane_off + kColO + c * 32, ov);
+                    ptx::tmem_st32(oreg + c * 32, ov);
                 }
                 ptx::tmem_st_wait();
             }
-            // P buffer j%2 was last read by PV_{j-2}: wait for it before overwriting
-            if (j >= 2 && !ptx::mbar_wait(&o_bar[j & 1], (uint32_t)((j - 2) >> 1) & 1u)) { ok = false; break; }
-            ptx::tc_fence_after();
             const float4* w4 = reinterpret_cast<const float4*>(wbuf);
             const float nb = m_used == -INFINITY ? 0.f : -m_used;
             float lt4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -393,19 +398,19 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                     pk[i] = ptx::pack2<BF16>(p0 * w.x, p1 * w.y);
                     pk[i + 1] = ptx::pack2<BF16>(p2 * w.z, p3 * w.w);
                 }
-                ptx::tmem_st32(tmem + lane_off + kColP + (uint32_t)(j & 1) * 64 + h2 * 32, pk);
+                // P (bf16 pairs) over the first 64 columns of this tile's S region
+                ptx::tmem_st32(sreg + h2 * 32, pk);
             }
             ptx::tmem_st_wait();
             l += (lt4[0] + lt4[1]) + (lt4[2] + lt4[3]);
             ptx::tc_fence_before();
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&p_full[j & 1]);
+            if (lane == 0) ptx::mbar_arrive(&p_full[x]);
         }
         // ---- epilogue: O / l -> global
         bool have = n_tiles > 0 && ok;
         if (have) {
-            const int jl = n_tiles - 1;
-            have = ptx::mbar_wait(&o_bar[jl & 1], (uint32_t)(jl >> 1) & 1u);
+            have = ptx::mbar_wait(&o_bar[x], (uint32_t)(n_tiles - 1) & 1u);
             ptx::tc_fence_after();
         }
         if (!ok || (n_tiles > 0 && !have)) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
@@ -416,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         for (int c = 0; c < 4; ++c) {
             uint32_t ov[32];
             if (have) {
-                ptx::tmem_ld32(tmem + lane_off + kColO + c * 32, ov);
+                ptx::tmem_ld32(oreg + c * 32, ov);
                 ptx::tmem_ld_wait();
             } else {
 #pragma unroll
@@ -494,7 +499,7 @@ int run_prefill_tc(const PrefillParams& p, const void* q_base, const void* k_cac
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) != cudaSuccess)
         return check_launch("prefill_tc: set smem attribute");
     const int rows = p.Nq * p.G;
-    dim3 grid((rows + 127) / 128, p.Hkv, p.B);
+    dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, p.Hkv, p.B);
     kern<<<grid, kThreads, L::kAlloc, st>>>(mq, mk, mv, a);
     return check_launch("fog_prefill_tc");
 }
