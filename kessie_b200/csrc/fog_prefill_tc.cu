@@ -36,7 +36,11 @@ namespace {
 
 constexpr int kNK = 2;                 // K stages
 constexpr int kNV = 2;                 // V stages
-constexpr int kThreads = 352;          // 11 warps: K producer, MMA, 2 x 4 softmax, V producer
+constexpr int kThreads = 384;          // warps 0-7: softmax A / B; 8: K producer; 9: MMA; 10: V producer; 11: idle
+// setmaxnreg split: the launch pool is kThreads x kLaunchRegs; the producer
+// warpgroup gives registers back to the two softmax warpgroups.
+constexpr int kLaunchRegs = 168, kSoftmaxRegs = 216, kProducerRegs = 64;
+static_assert(256 * kSoftmaxRegs + 128 * kProducerRegs <= kThreads * kLaunchRegs, "register split exceeds the pool");
 constexpr int kRowsPerCta = 256;       // two 128-row Q tiles (A, B)
 constexpr uint32_t kTmemCols = 512;    // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
 constexpr float kRescaleThreshold = 8.0f;    // log2 units
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         }
         ptx::fence_mbar_init();
     }
-    if (warp == 1) {
+    if (warp == 9) {
         ptx::tmem_alloc(slot, kTmemCols);
         ptx::tmem_relinquish();
     }
@@ -122,11 +126,13 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *slot;
-
-    if (warp == 0 || warp == 10) {
+    if (warp >= 8) {
+    // ==================================================================== producer warpgroup
+    ptx::setmaxnreg_dec<kProducerRegs>();
+    if (warp == 8 || warp == 10) {
         // ================================================================ producers
-        // warp 0: Q (both tiles), then the K ring; warp 10: the V ring.
-        const bool is_k = warp == 0;
+        // warp 8: Q (both tiles), then the K ring; warp 10: the V ring.
+        const bool is_k = warp == 8;
         const int NS = is_k ? kNK : kNV;
         uint64_t* full = is_k ? k_full : v_full;
         uint64_t* empty = is_k ? k_empty : v_empty;
@@ -214,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
             for (int it = max(0, issued - NS); it < issued; ++it)
                 if (!ptx::mbar_wait(&full[it % NS], (uint32_t)(it / NS) & 1u)) break;
         }
-    } else if (warp == 1) {
+    } else if (warp == 9) {
         // ================================================================ MMA issuer
         // S_A(0) S_B(0) | per tile t: [P_A(t)] PV_A(t) S_A(t+1) | [P_B(t)] PV_B(t) S_B(t+1)
         // One thread issues everything, in order: S_X(t+1) overwrites the S/P
@@ -284,9 +290,11 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
             }
         }
         if (!ok && n_tiles > 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+    }
     } else {
         // ================================================================ softmax warpgroups
-        const int x = (warp - 2) >> 2;                 // Q tile: 0 (warps 2-5) or 1 (warps 6-9)
+        ptx::setmaxnreg_inc<kSoftmaxRegs>();
+        const int x = warp >> 2;                       // Q tile: 0 (warps 0-3) or 1 (warps 4-7)
         const int q4 = warp & 3;
         const int r = q4 * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
@@ -304,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         if (!valid_row) hi_r = lo_r - 1;
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
-        float* wbuf = reinterpret_cast<float*>(smem + L::kW) + (warp - 2) * 128;
+        float* wbuf = reinterpret_cast<float*>(smem + L::kW) + warp * 128;
         const float inv_den = 1.f / (float)max(cs - 1, 1);
         for (int j = 0; j < n_tiles; ++j) {
             const int key0 = (tile_lo + j) * 128;
@@ -380,16 +388,16 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
             const float nb = m_used == -INFINITY ? 0.f : -m_used;
             float lt4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-                uint32_t pk[32];
+            for (int h4 = 0; h4 < 4; ++h4) {
+                uint32_t pk[16];
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const int c0 = h2 * 64 + 2 * i;          // key column (4 keys per step)
+                for (int i = 0; i < 16; i += 2) {
+                    const int c0 = h4 * 32 + 2 * i;          // key column (4 keys per step)
                     const float4 w = has_fog ? w4[c0 >> 2] : make_float4(1.f, 1.f, 1.f, 1.f);
-                    const float s0 = __uint_as_float(sv[c0 >> 5][c0 & 31]);
-                    const float s1 = __uint_as_float(sv[(c0 + 1) >> 5][(c0 + 1) & 31]);
-                    const float s2 = __uint_as_float(sv[(c0 + 2) >> 5][(c0 + 2) & 31]);
-                    const float s3 = __uint_as_float(sv[(c0 + 3) >> 5][(c0 + 3) & 31]);
+                    const float s0 = __uint_as_float(sv[h4][2 * i]);
+                    const float s1 = __uint_as_float(sv[h4][2 * i + 1]);
+                    const float s2 = __uint_as_float(sv[h4][2 * i + 2]);
+                    const float s3 = __uint_as_float(sv[h4][2 * i + 3]);
                     const float p0 = ptx::ex2(fmaf(s0, p.scale_log2, nb));
                     const float p1 = ptx::ex2(fmaf(s1, p.scale_log2, nb));
                     const float p2 = ptx::ex2(fmaf(s2, p.scale_log2, nb));
@@ -399,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                     pk[i + 1] = ptx::pack2<BF16>(p2 * w.z, p3 * w.w);
                 }
                 // P (bf16 pairs) over the first 64 columns of this tile's S region
-                ptx::tmem_st32(sreg + h2 * 32, pk);
+                ptx::tmem_st16(sreg + h4 * 16, pk);
             }
             ptx::tmem_st_wait();
             l += (lt4[0] + lt4[1]) + (lt4[2] + lt4[3]);
@@ -440,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
     }
     ptx::tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 9) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, kTmemCols);
     }
@@ -496,6 +504,11 @@ int run_prefill_tc(const PrefillParams& p, const void* q_base, const void* k_cac
     a.dense = dense ? 1 : 0;
     a.page_size = ps;
     auto kern = bf16 ? fog_prefill_tc_kernel<true> : fog_prefill_tc_kernel<false>;
+    // setmaxnreg.inc waits until the CTA's register pool can satisfy it, so the
+    // split is only valid if the kernel was built with kLaunchRegs per thread.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) { cudaGetLastError(); return kTcNotCovered; }
+    if (fa.numRegs < kLaunchRegs) return kTcNotCovered;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) != cudaSuccess)
         return check_launch("prefill_tc: set smem attribute");
     const int rows = p.Nq * p.G;
