@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
     return ap.parse_args()
 
 
@@ -381,6 +382,18 @@ def run_cp_decode(args):
                 "gpu_launches": K * (2 if world == 1 else 3),
                 "gpu_launches_note": "per step: split-KV decode + chunk merge (+ LSE merge of ranks when N>1); NCCL all-gather not counted",
                 "clocks": clocks.summary(), "output_finite": finite, "library": _lib.loaded_path()}
+        if world == 1 and not args.no_secondary:
+            del kv, kc, vc, dec
+            torch.cuda.empty_cache()
+            sec = {}
+            for wl, st in (("decode_128k", 20), ("decode_cfg3", 20), ("page_ops", 50), ("prefill", 10)):
+                r = measure_aux(wl, st)
+                r.pop("workload", None)
+                sec[wl] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}
+                torch.cuda.empty_cache()
+            line["secondary"] = sec
+            line["secondary_note"] = ("other north_star configs, same process, CUDA-event timed: decode_128k/cfg3 = "
+                                      "config 3 (GB/s vs hbm peak), page_ops = config 2, prefill = config 4 (TFLOP/s)")
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -390,20 +403,36 @@ def run_cp_decode(args):
 
 def run_aux_workload(args):
     """Single-GPU measurements of the other configs (not bench lines)."""
+    _setup_dist(args)
+    print(json.dumps(measure_aux(args.workload, args.steps, args.warmup)), flush=True)
+    return 0
+
+
+def measure_aux(workload, steps, warmup=3):
     import numpy as np
     import torch
     from kessie_b200 import ops
-    _setup_dist(args)
     dev = torch.device("cuda", torch.cuda.current_device())
     hbm, tf, tfs, peak_src = load_peaks()
-    res = {"workload": args.workload}
+    res = {"workload": workload}
+
+    class _A:
+        pass
+    args = _A()
+    args.workload, args.steps, args.warmup = workload, steps, warmup
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if workload == "page_ops" else None
 
     def timeit(fn, K):
+        """Mean CUDA-event time of fn; for working sets below the L2 size a
+        256 MB write between iterations (outside the events) flushes L2."""
         for _ in range(max(3, args.warmup)):
             fn()
         torch.cuda.synchronize()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
         for a, b in evs:
+            if flush is not None:
+                flush.zero_()
             a.record(); fn(); b.record()
         torch.cuda.synchronize()
         return sum(a.elapsed_time(b) for a, b in evs) / K
@@ -457,7 +486,7 @@ def run_aux_workload(args):
             valid.fill_(1)
             ops.page_evict(valid, pos, 32768)
         ms_e = timeit(ev_step, args.steps)
-        res.update(evicted=n, gather_ms=ms_g, gather_GBs=268435456 / ms_g / 1e6, remap_ms=ms_r,
+        res.update(l2="256 MB flush between iterations", evicted=n, gather_ms=ms_g, gather_GBs=268435456 / ms_g / 1e6, remap_ms=ms_r,
                    remap_GBs=134217728 / ms_r / 1e6, insert_remap_ms=ms_i, insert_remap_GBs=268435456 / ms_i / 1e6,
                    evict_plus_refill_us=ms_e * 1e3, hbm_peak=hbm)
     elif args.workload in ("prefill", "prefill_small"):
@@ -475,9 +504,9 @@ def run_aux_workload(args):
         ms = timeit(lambda: ops.paged_fog_prefill(q, kv[:, :, 0], kv[:, :, 1], bt, kl, clear_start=cs, fog_alpha=0.5,
                                                   out=out), max(3, args.steps // 20))
         flops = 4 * D * Hq * (T * (Nk - T) + T * (T + 1) // 2)
-        res.update(ms=ms, tflops=flops / ms / 1e9, frac_of_bf16_peak=flops / ms / 1e9 / tf, flops=flops)
-    print(json.dumps(res), flush=True)
-    return 0
+        res.update(ms=ms, tflops=flops / ms / 1e9, frac_of_bf16_peak=flops / ms / 1e9 / tf, flops=flops,
+                   peak_tflops=tf, peak_source=f"{peak_src} bf16_tflops (burst; one launch per timing)")
+    return res
 
 
 if __name__ == "__main__":

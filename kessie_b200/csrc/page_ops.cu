@@ -40,6 +40,19 @@ FreqTable make_freqs(float theta, int half) {
     return t;
 }
 
+// cos / sin of the reference's fp32 angle x = (float)(tgt - orig) * f_d.
+// |x| reaches ~1.6e5 rad, where the accurate sincosf takes its slow
+// large-argument path (and diverges across the lanes of a warp).  x itself is
+// kept bit-for-bit (it carries the reference's fp32 rounding); it is reduced
+// to [-pi, pi] in double precision -- exact to ~1e-11 rad at these magnitudes
+// -- and evaluated with the hardware approximation (abs error < 4e-7).
+__device__ __forceinline__ void rope_sincos(float x, float* s, float* c) {
+    const double xd = (double)x;
+    const double k = rint(xd * 0.15915494309189535);          // 1 / (2 pi)
+    const float r = (float)fma(-k, 6.283185307179586, xd);    // x - 2 pi k
+    __sincosf(r, s, c);
+}
+
 // ------------------------------------------------------------------ vectors
 template <typename T> struct VecOps;
 template <> struct VecOps<__half> {
@@ -111,7 +124,7 @@ __global__ void __launch_bounds__(256) rope_remap_kernel(
         int t = t0 + tl;
         float delta = (float)(tgt[t] - orig[t]) * ft.f[d];
         float s, c;
-        sincosf(delta, &s, &c);
+        rope_sincos(delta, &s, &c);
         cs[i] = c; sn[i] = s;
     }
     __syncthreads();
@@ -146,7 +159,7 @@ __global__ void rope_remap_scalar_kernel(T* __restrict__ k, int num_tokens, int 
     int t = (int)(r / num_heads);
     float delta = (float)(tgt[t] - orig[t]) * ft.f[d];
     float s, c;
-    sincosf(delta, &s, &c);
+    rope_sincos(delta, &s, &c);
     T* row = k + (int64_t)t * tstride + (int64_t)h * hstride;
     float a = to_f32(row[d]), b = to_f32(row[d + half]);
     row[d] = from_f32<T>(a * c - b * s);
@@ -208,7 +221,7 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(
             const int t = t0 + tl;
             const int target = tgt ? tgt[t] : conv_pos + t;
             float sv, cv;
-            sincosf((float)(target - orig[t]) * ft.f[d], &sv, &cv);
+            rope_sincos((float)(target - orig[t]) * ft.f[d], &sv, &cv);
             cs[i] = cv; sn[i] = sv;
         }
     }
@@ -501,7 +514,7 @@ __global__ void __launch_bounds__(256) page_insert_kernel(
             int t = t0 + tl;
             int target = tgt ? tgt[t] : conv_pos + t;
             float s, c;
-            sincosf((float)(target - orig[t]) * ft.f[d], &s, &c);
+            rope_sincos((float)(target - orig[t]) * ft.f[d], &s, &c);
             cs[i] = c; sn[i] = s;
         }
         __syncthreads();
