@@ -465,30 +465,59 @@ def measure_aux(workload, steps, warmup=3):
         res.update(ms_per_step=ms, us_per_step=ms * 1e3, kv_bytes=byts, GBs=byts / ms / 1e6,
                    frac_of_hbm=byts / ms / 1e6 / hbm, total_tokens=int(sum(lens)))
     elif args.workload == "page_ops":
-        P, ps, H, D = 8192, 16, 8, 128
-        kv = torch.randn(P, ps, 2, H, D, device=dev, dtype=torch.bfloat16)
+        # Config 2 on L independent layer caches (each 8192 pages x 64 KB = 512 MB):
+        # 25% of pages (pos = 16 * perm) evicted below 32768, gathered to staging,
+        # K re-rotated old -> new positions (theta 5e5), recalled into shuffled
+        # free slots at conv_pos 131072.  Two timings per op: one launch between
+        # CUDA events after a 256 MB L2 flush, and the L layers back to back
+        # (every launch touches fresh memory; launch gaps amortised as in a
+        # multi-layer recall).
+        L, P, ps, H, D = 8, 8192, 16, 8, 128
+        kvs = [torch.randn(P, ps, 2, H, D, device=dev, dtype=torch.bfloat16) for _ in range(L)]
         perm = np.random.default_rng(2).permutation(P)
         pos = torch.from_numpy((16 * perm).astype(np.int32)).to(dev)
         valid = torch.ones(P, dtype=torch.int8, device=dev)
         cnt, ids = ops.page_evict(valid, pos, 32768)
-        n = cnt.item()
+        n = int(cnt.item())
         ev = ids[:n].clone()
-        Kst, Vst = ops.page_gather(kv, ev)
-        ms_g = timeit(lambda: ops.page_gather(kv, ev, out_keys=Kst, out_values=Vst), args.steps)
+        stK = [torch.empty(n * ps, H, D, device=dev, dtype=torch.bfloat16) for _ in range(L)]
+        stV = [torch.empty(n * ps, H, D, device=dev, dtype=torch.bfloat16) for _ in range(L)]
         oldpos = (pos[ev.long()].view(-1, 1) + torch.arange(16, device=dev, dtype=torch.int32)).reshape(-1)
         newpos = torch.arange(131072, 131072 + n * 16, device=dev, dtype=torch.int32)
-        ms_r = timeit(lambda: ops.rope_remap(Kst, oldpos, newpos, 500000.0), args.steps)
         free = torch.from_numpy(np.random.default_rng(22).permutation(ev.cpu().numpy())).to(dev)
-        ms_i = timeit(lambda: ops.page_insert(kv, Kst, Vst, free, conv_pos=131072, orig_positions=oldpos,
-                                              rope_theta=500000.0), args.steps)
+        ops_by_name = {
+            "gather": lambda l: ops.page_gather(kvs[l], ev, out_keys=stK[l], out_values=stV[l]),
+            "remap": lambda l: ops.rope_remap(stK[l], oldpos, newpos, 500000.0),
+            "insert_remap": lambda l: ops.page_insert(kvs[l], stK[l], stV[l], free, conv_pos=131072,
+                                                      orig_positions=oldpos, rope_theta=500000.0),
+        }
+        nbytes = {"gather": 268435456, "remap": 134217728, "insert_remap": 268435456}
+        for name, fn in ops_by_name.items():
+            ms_one = timeit(lambda: fn(0), args.steps)
+            for l in range(L):
+                fn(l)
+            torch.cuda.synchronize()
+            reps = max(3, args.steps // L)
+            e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                for l in range(L):
+                    fn(l)
+            e1.record()
+            torch.cuda.synchronize()
+            ms_b2b = e0.elapsed_time(e1) / (reps * L)
+            res[name + "_ms"] = ms_one
+            res[name + "_GBs"] = nbytes[name] / ms_one / 1e6
+            res[name + "_b2b_ms"] = ms_b2b
+            res[name + "_b2b_GBs"] = nbytes[name] / ms_b2b / 1e6
+            res[name + "_b2b_frac"] = nbytes[name] / ms_b2b / 1e6 / hbm
 
         def ev_step():
             valid.fill_(1)
             ops.page_evict(valid, pos, 32768)
         ms_e = timeit(ev_step, args.steps)
-        res.update(l2="256 MB flush between iterations", evicted=n, gather_ms=ms_g, gather_GBs=268435456 / ms_g / 1e6, remap_ms=ms_r,
-                   remap_GBs=134217728 / ms_r / 1e6, insert_remap_ms=ms_i, insert_remap_GBs=268435456 / ms_i / 1e6,
-                   evict_plus_refill_us=ms_e * 1e3, hbm_peak=hbm)
+        res.update(l2="one-launch timings: 256 MB flush before each; b2b: 8 layer caches back to back",
+                   evicted=n, evict_plus_refill_us=ms_e * 1e3, hbm_peak=hbm, layers=L)
     elif args.workload in ("prefill", "prefill_small"):
         Hq, Hkv, D, ps, T, Nk = 32, 8, 128, 16, 8192, 262144
         if args.workload == "prefill_small":        # profiling size: 256 MB of KV

@@ -16,6 +16,8 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <algorithm>
+
 namespace kessie {
 namespace {
 
@@ -300,6 +302,138 @@ void launch_rows(int kt, dim3 grid, int threads, size_t smem, cudaStream_t st, T
 #undef KESSIE_ROWS
 }
 
+
+// Token-block RoPE kernel shared by the in-place remap and the fused recall
+// insert.  A CTA owns `tpb` tokens; each thread first issues its loads (one
+// K low/high 16-byte pair, and for the insert its V vectors), then the CTA
+// builds a (cos, sin, cos, sin) float4 table for the tokens' angle pairs, and
+// every thread rotates its pair with 4 vector table reads per 8 elements.
+// INSERT: destination row of token t is page page_ids[t / ps], slot t % ps
+// (first token of a page sets page_valid / page_positions); the V rows are
+// copied alongside.
+template <typename T, bool INSERT, int KPT>
+__global__ void __launch_bounds__(256, INSERT ? 8 : 4) rope_tokens_kernel(
+    T* __restrict__ dst, const T* __restrict__ srck, const T* __restrict__ srcv, int num_tokens, int num_heads,
+    int half, int64_t sts, int64_t shs, int64_t dts, int64_t dhs, int64_t dkv, int64_t page_stride, int ps,
+    const int32_t* __restrict__ page_ids, int max_pages, int8_t* __restrict__ valid, int32_t* __restrict__ positions,
+    int conv_pos, const int32_t* __restrict__ orig, const int32_t* __restrict__ tgt, FreqTable ft, int tpb,
+    int* status) {
+    extern __shared__ float4 tab[];                 // [tpb][half/2] of (cos d, sin d, cos d+1, sin d+1)
+    constexpr int N = VecOps<T>::N;
+    const int hc = half / N;                        // 16-byte chunks per half row
+    const int t0 = blockIdx.x * tpb;
+    const int nt = min(tpb, num_tokens - t0);
+    const int kitems = nt * num_heads * hc;
+    const int vitems = INSERT ? nt * num_heads * 2 * hc : 0;
+    // ---- 1. loads: KPT K pairs and (insert) 2*KPT V vectors per thread, all in flight
+    uint4 lo[KPT], hi[KPT], vv[INSERT ? 2 * KPT : 1];
+#pragma unroll
+    for (int k = 0; k < KPT; ++k) {
+        const int ki = threadIdx.x + k * blockDim.x;
+        if (ki < kitems) {
+            const int kc = ki % hc, r = ki / hc;
+            const int kh = r % num_heads, ktl = r / num_heads;
+            const T* row = srck + (int64_t)(t0 + ktl) * sts + (int64_t)kh * shs;
+            lo[k] = *reinterpret_cast<const uint4*>(row + kc * N);
+            hi[k] = *reinterpret_cast<const uint4*>(row + half + kc * N);
+        }
+    }
+    if (INSERT) {
+#pragma unroll
+        for (int j = 0; j < 2 * KPT; ++j) {
+            const int vi = threadIdx.x + j * blockDim.x;
+            if (vi < vitems) {
+                const int c = vi % (2 * hc), r = vi / (2 * hc);
+                const int h = r % num_heads, tl = r / num_heads;
+                vv[j] = ldg_stream(srcv + (int64_t)(t0 + tl) * sts + (int64_t)h * shs + c * N);
+            }
+        }
+    }
+    // ---- 2. angle table (one float4 = two consecutive d)
+    const int hp = half / 2;
+    for (int i = threadIdx.x; i < nt * hp; i += blockDim.x) {
+        const int tl = i / hp, dp = i - tl * hp;
+        const int t = t0 + tl;
+        const int target = tgt ? tgt[t] : conv_pos + t;
+        const float dlt = (float)(target - orig[t]);
+        float4 cs;
+        rope_sincos(dlt * ft.f[2 * dp], &cs.y, &cs.x);
+        rope_sincos(dlt * ft.f[2 * dp + 1], &cs.w, &cs.z);
+        tab[i] = cs;
+    }
+    __syncthreads();
+    // ---- 3. rotate K pairs, store; copy V
+    auto dst_row = [&](int tl, int h, bool& ok) -> T* {
+        const int t = t0 + tl;
+        if (!INSERT) { ok = true; return dst + (int64_t)t * dts + (int64_t)h * dhs; }
+        const int phys = page_ids[t / ps];
+        ok = phys >= 0 && phys < max_pages;
+        return dst + (int64_t)(ok ? phys : 0) * page_stride + (int64_t)(t % ps) * dts + (int64_t)h * dhs;
+    };
+#pragma unroll
+    for (int k = 0; k < KPT; ++k) {
+        const int ki = threadIdx.x + k * blockDim.x;
+        if (ki >= kitems) break;
+        const int kc = ki % hc, r = ki / hc;
+        const int kh = r % num_heads, ktl = r / num_heads;
+        float a[N], bb[N], ra[N], rb[N];
+        VecOps<T>::unpack(lo[k], a);
+        VecOps<T>::unpack(hi[k], bb);
+        const float4* tp = tab + ktl * hp + kc * (N / 2);
+#pragma unroll
+        for (int j = 0; j < N / 2; ++j) {
+            const float4 cs = tp[j];
+            ra[2 * j] = a[2 * j] * cs.x - bb[2 * j] * cs.y;
+            rb[2 * j] = a[2 * j] * cs.y + bb[2 * j] * cs.x;
+            ra[2 * j + 1] = a[2 * j + 1] * cs.z - bb[2 * j + 1] * cs.w;
+            rb[2 * j + 1] = a[2 * j + 1] * cs.w + bb[2 * j + 1] * cs.z;
+        }
+        bool ok;
+        T* row = dst_row(ktl, kh, ok);
+        if (ok) {
+            *reinterpret_cast<uint4*>(row + kc * N) = VecOps<T>::pack(ra);
+            *reinterpret_cast<uint4*>(row + half + kc * N) = VecOps<T>::pack(rb);
+        }
+        if (INSERT && kh == 0 && kc == 0) {
+            const int t = t0 + ktl;
+            if (t % ps == 0) {
+                const int phys = page_ids[t / ps];
+                if (phys < 0 || phys >= max_pages) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
+                else {
+                    if (valid) valid[phys] = 1;
+                    if (positions) positions[phys] = conv_pos + t;
+                }
+            }
+        }
+    }
+    if (INSERT) {
+#pragma unroll
+        for (int j = 0; j < 2 * KPT; ++j) {
+            const int vi = threadIdx.x + j * blockDim.x;
+            if (vi < vitems) {
+                const int c = vi % (2 * hc), r = vi / (2 * hc);
+                const int h = r % num_heads, tl = r / num_heads;
+                bool ok;
+                T* row = dst_row(tl, h, ok);
+                if (ok) stg_stream(row + dkv + c * N, vv[j]);
+            }
+        }
+    }
+}
+
+// Tokens per CTA for rope_tokens_kernel: one K pair per thread (and at most
+// 4 V vectors per thread for the insert); 0 when the shape does not fit.
+constexpr int kRopeKPT = 1;   // K pairs per thread (more measured slower: registers cost occupancy)
+int tokens_per_block(int H, int half, int N, bool insert) {
+    (void)insert;
+    if (half % N) return 0;
+    const int per_token = H * (half / N);
+    if (per_token > 256 * kRopeKPT) return 0;
+    int tpb = (256 * kRopeKPT) / per_token;
+    const int max_tab = (48 * 1024) / ((half / 2) * 16);     // angle table within the default shared memory
+    return std::min(tpb, max_tab);
+}
+
 template <typename T>
 int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int32_t* orig,
                 const int32_t* tgt, float theta, cudaStream_t st) {
@@ -312,7 +446,13 @@ int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int
     const int tt = 16;
     // The row-parallel kernel measured slower than rope_remap_kernel for the
     // in-place case (56.5 vs 34.5 us at config 2); kept for the insert path.
-    if (false && vec && rows_shape<T>(H, D, tt, threads, cpr, kt)) {
+    const int tpb_t = vec ? tokens_per_block(H, half, N, false) : 0;
+    if (tpb_t > 0) {
+        size_t smem = (size_t)tpb_t * (half / 2) * sizeof(float4);
+        rope_tokens_kernel<T, false, kRopeKPT><<<(T_ + tpb_t - 1) / tpb_t, 256, smem, st>>>(
+            (T*)k, (const T*)k, nullptr, T_, H, half, ts, hs, ts, hs, 0, 0, 1, nullptr, 0, nullptr, nullptr, 0, orig, tgt,
+            ft, tpb_t, nullptr);
+    } else if (vec && rows_shape<T>(H, D, tt, threads, cpr, kt)) {
         size_t smem = (size_t)2 * tt * half * sizeof(float);
         launch_rows<T, 0>(kt, dim3((T_ + tt - 1) / tt), threads, smem, st, (T*)k, (const T*)k, nullptr, T_, H, half,
                           cpr, ts, hs, ts, hs, 0, 0, 0, nullptr, 0, nullptr, nullptr, 0, orig, tgt, ft, tt, nullptr);
@@ -683,7 +823,15 @@ int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv
     int pages = (T_ + g.page_size - 1) / g.page_size;
     if (pages == 0) return check_launch("page_insert (empty)");
     int threads = 0, cpr = 0, kt = 0;
-    if (orig && vec && g.page_size <= 256 && rows_shape<T>(g.num_heads, g.head_dim, g.page_size, threads, cpr, kt)) {
+    const int tpb_i = (orig && vec) ? tokens_per_block(g.num_heads, g.head_dim / 2, N, true) : 0;
+    if (tpb_i > 0) {
+        FreqTable ft = make_freqs(theta, g.head_dim / 2);
+        size_t smem = (size_t)tpb_i * (g.head_dim / 4) * sizeof(float4);
+        rope_tokens_kernel<T, true, kRopeKPT><<<(T_ + tpb_i - 1) / tpb_i, 256, smem, st>>>(
+            (T*)cache, (const T*)nk, (const T*)nv, T_, g.num_heads, g.head_dim / 2, sts, shs, g.token_stride,
+            g.head_stride, g.kv_stride, g.page_stride, g.page_size, ids, g.max_pages, valid, positions, conv_pos, orig,
+            tgt, ft, tpb_i, status);
+    } else if (orig && vec && g.page_size <= 256 && rows_shape<T>(g.num_heads, g.head_dim, g.page_size, threads, cpr, kt)) {
         FreqTable ft = make_freqs(theta, g.head_dim / 2);
         size_t smem = (size_t)2 * g.page_size * (g.head_dim / 2) * sizeof(float);
         if (smem > 48 * 1024) {

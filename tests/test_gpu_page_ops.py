@@ -238,3 +238,28 @@ def test_page_gather_bad_id_zero_and_flag():
     assert np.array_equal(to_np(K)[:16], kvn[1, :, 0].reshape(16, 2, 64))
     assert (to_np(K)[16:] == 0).all() and (to_np(V)[16:] == 0).all()
     assert _status() & 0x1
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp32"])
+def test_fused_insert_remap_ragged_and_bad_page(dt):
+    """Ragged last page (T % ps != 0), explicit target positions, and one
+    out-of-range page id: that page is skipped and flagged, the rest match."""
+    from kessie_b200 import ops
+    _status()
+    P, ps, H, D, T = 20, 16, 4, 128, 45
+    kv = torch.zeros(P, ps, 2, H, D, dtype=TORCH_DT[dt], device="cuda")
+    keys = ROUND[dt](rnd(31, (T, H, D))); vals = ROUND[dt](rnd(32, (T, H, D)))
+    orig = np.random.default_rng(7).integers(0, 50000, T).astype(np.int32)
+    tgt = np.random.default_rng(8).integers(0, 50000, T).astype(np.int32)
+    ids = np.array([4, 999, 11], dtype=np.int32)
+    valid = torch.zeros(P, dtype=torch.int8, device="cuda"); posd = torch.zeros(P, dtype=torch.int32, device="cuda")
+    ops.page_insert(kv, to_dev(keys, dt), to_dev(vals, dt), ids, valid, posd, conv_pos=100, orig_positions=orig,
+                    target_positions=tgt, rope_theta=500000.0)
+    assert _status() & 0x1
+    got = to_np(kv)
+    rot = ROUND[dt](O.rope_remap(keys, orig, tgt, 500000.0))
+    np.testing.assert_allclose(got[4, :, 0], rot[0:16], **TOL[dt])
+    np.testing.assert_allclose(got[11, :13, 0], rot[32:45], **TOL[dt])
+    assert np.array_equal(got[11, :13, 1], vals[32:45]) and (got[11, 13:] == 0).all()
+    assert valid.cpu().numpy()[[4, 11]].tolist() == [1, 1] and int(valid.sum()) == 2
+    assert posd.cpu().numpy()[[4, 11]].tolist() == [100, 132]
