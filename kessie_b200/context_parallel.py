@@ -82,7 +82,9 @@ class ContextParallelFogDecode:
         """Steps 2-3: NCCL all-gather of the triples, then the LSE merge."""
         if self.world == 1:
             return self.state.out
-        dist.all_gather_into_tensor(self.state.gathered, self.state.partial, group=self.group)
+        # concatenated-along-dim-0 output form (accepted by every backend)
+        flat = self.state.gathered.view(-1, *self.state.partial.shape[1:])
+        dist.all_gather_into_tensor(flat, self.state.partial, group=self.group)
         ops.lse_combine(self.state.gathered, out=self.state.out)
         return self.state.out
 
