@@ -9,8 +9,11 @@
  *
  * Conventions
  *   - Every pointer is a device pointer owned by the caller (PyTorch tensor
- *     storage); the library allocates no device memory.  Scratch memory is
- *     passed in as `workspace` and sized by the matching *_workspace_size().
+ *     storage); the library allocates no device memory, except on explicit
+ *     request through kessie_cp_exchange_alloc (the context-parallel
+ *     exchange buffer, which must be cudaMalloc'd to be shared over CUDA
+ *     IPC).  Scratch memory is passed in as `workspace` and sized by the
+ *     matching *_workspace_size().
  *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream),
  *     the value of torch.cuda.Stream.cuda_stream.  All calls are asynchronous
  *     on that stream.
@@ -250,10 +253,12 @@ int kessie_paged_fog_prefill_v2(const void* q, int64_t q_stride_b, int64_t q_str
                                 int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h,
                                 void* stream);
 
-/* kessie_paged_fog_decode_v2 split into its two phases: phases bit 0 runs
- * the split-KV kernel (partials left in `workspace`), bit 1 the per-row
- * merge into out / out_partial; 3 = both.  Both phases must see identical
- * arguments.  For callers that time or overlap the phases separately. */
+/* kessie_paged_fog_decode_v2 with a phase mask.  The split merge runs inside
+ * the decode kernel, so bit 0 (1 or 3) launches the one kernel that writes
+ * out / out_partial, and phases = 2 only checks the arguments.  Kept for
+ * callers written against the earlier two-launch form.
+ * The workspace needs no initialisation: its per-group arrival counters
+ * carry a per-launch tag, so contents left by any earlier use are ignored. */
 int kessie_paged_fog_decode_ex_v2(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                                   const void* k_cache, const void* v_cache, int64_t page_stride,
                                   int64_t token_stride, int64_t head_stride, int num_pages,
@@ -325,6 +330,61 @@ int kessie_paged_fog_prefill_ex_v2(const void* q, int64_t q_stride_b, int64_t q_
 int kessie_lse_combine_v2(const float* partials, int num_splits, int64_t split_stride, int rows,
                           int head_dim, void* out, int out_dtype, float* out_partial,
                           void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Context-parallel decode over NVLink peer memory (no counterpart in the
+ * reference, which has no multi-GPU attention path).  Each of the `world`
+ * ranks (one GPU each, one node, world <= 8) holds a contiguous position
+ * range of every sequence (kv_pos_offset = global position of local key 0).
+ * Every rank allocates one exchange buffer and maps the others':
+ *   kessie_cp_exchange_bytes(world, B, Hq, Hkv, D) -> size
+ *   kessie_cp_exchange_alloc(size, &ptr, handle)    cudaMalloc, zero-fill,
+ *                                                   IPC handle (64 bytes)
+ *   (all-gather the handles over the caller's process group)
+ *   kessie_cp_exchange_open(peer_handle, &peer_ptr) for every other rank
+ *   kessie_cp_exchange_close(peer_ptr) / kessie_cp_exchange_free(ptr) at the
+ *   end, after every rank has finished its last step.
+ * A step, kessie_paged_fog_decode_cp_v2 with exchange_buffers[r] = rank r's
+ * buffer as mapped in this process (this rank's own at [rank]):
+ *   phases bit 0: the decode kernel over the local shard; the CTA that
+ *     completes a (seq, kv_head) group stores the group's merged rows into
+ *     every rank's buffer over NVLink as self-validating (value, epoch)
+ *     8-byte words -- no fence or flag, so the decode never waits;
+ *   phases bit 1: a combine kernel that polls this rank's own buffer until
+ *     every rank's words of a row carry the epoch (at most wait_timeout_ns,
+ *     then KESSIE_DEV_WAIT_TIMEOUT in the device status word and zero rows)
+ *     and writes out [B, Hq, D] and/or out_partial [B, Hq, D+2] (same triple
+ *     as kessie_paged_fog_decode_v2).  With both bits the combine is a
+ *     programmatic dependent launch of the decode.
+ * All ranks call it with the same shapes and the same epoch; epoch starts at
+ * 1 and goes up by one per step (consecutive steps alternate between two
+ * slots of the buffer, so keep the parity alternating across any wrap).
+ * Only the combine waits, and only on memory of its own GPU. */
+#define KESSIE_IPC_HANDLE_BYTES 64
+size_t kessie_cp_exchange_bytes(int world, int batch, int num_q_heads, int num_kv_heads,
+                                int head_dim);
+int kessie_cp_exchange_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+int kessie_cp_exchange_open(const void* ipc_handle, void** dev_ptr);
+int kessie_cp_exchange_close(void* dev_ptr);
+int kessie_cp_exchange_free(void* dev_ptr);
+/* Phase bit 1 of kessie_paged_fog_decode_cp_v2 on its own (needs only the
+ * exchange arguments and the shapes). */
+int kessie_cp_combine_v2(void* const* exchange_buffers, int rank, int world, uint32_t epoch,
+                         int64_t wait_timeout_ns, int batch, int num_q_heads, int num_kv_heads,
+                         int head_dim, int dtype, void* out, float* out_partial, void* stream);
+int kessie_paged_fog_decode_cp_v2(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                  const void* k_cache, const void* v_cache, int64_t page_stride,
+                                  int64_t token_stride, int64_t head_stride, int num_pages,
+                                  int page_size, const int32_t* block_table,
+                                  int64_t block_table_stride, const int32_t* seq_lens,
+                                  const int32_t* kv_pos_offset, const int32_t* q_positions,
+                                  const int32_t* clear_start, float fog_alpha,
+                                  const float* fog_weights, int window_size, float sm_scale,
+                                  int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                  int max_seq_len, int dtype, void* const* exchange_buffers,
+                                  int rank, int world, uint32_t epoch, int64_t wait_timeout_ns,
+                                  void* out, float* out_partial, void* workspace,
+                                  size_t workspace_bytes, int phases, void* stream);
 
 #ifdef __cplusplus
 }

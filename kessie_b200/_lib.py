@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
-from ctypes import c_float, c_int, c_int64, c_size_t, c_void_p, c_char_p, POINTER
+from ctypes import c_float, c_int, c_int64, c_size_t, c_void_p, c_char_p, POINTER, c_uint32
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 DEFAULT_PATHS = [
@@ -78,6 +78,16 @@ SIGNATURES = {
                                                c_int, c_float, c_int, c_int, c_int, c_int, c_int, c_int, P, c_int64,
                                                c_int64, c_int64, c_int, P, c_size_t, P]),
     "kessie_lse_combine_v2": (c_int, [P, c_int, c_int64, c_int, c_int, P, c_int, P, P]),
+    "kessie_cp_exchange_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "kessie_cp_exchange_alloc": (c_int, [c_size_t, P, P]),
+    "kessie_cp_exchange_open": (c_int, [P, P]),
+    "kessie_cp_exchange_close": (c_int, [P]),
+    "kessie_cp_exchange_free": (c_int, [P]),
+    "kessie_cp_combine_v2": (c_int, [P, c_int, c_int, c_uint32, c_int64, c_int, c_int, c_int, c_int, c_int, P, P, P]),
+    "kessie_paged_fog_decode_cp_v2": (c_int, [P, c_int64, c_int64, P, P, c_int64, c_int64, c_int64, c_int, c_int,
+                                              I32P, c_int64, I32P, I32P, I32P, I32P, c_float, P, c_int, c_float,
+                                              c_int, c_int, c_int, c_int, c_int, c_int, P, c_int, c_int, c_uint32,
+                                              c_int64, P, P, P, c_size_t, c_int, P]),
 }
 
 _lock = threading.Lock()

@@ -205,17 +205,10 @@ def decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, max_seq_l
                                                                   max_seq_len, page_size))
 
 
-def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
-                     seq_lens: torch.Tensor, clear_start=None, fog_alpha: float = 0.5, fog_weights=None,
-                     window_size: int = 0, sm_scale: Optional[float] = None, kv_pos_offset=None,
-                     q_positions=None, max_seq_len: Optional[int] = None, out: Optional[torch.Tensor] = None,
-                     out_partial: Optional[torch.Tensor] = None, want_out: bool = True, stream=None,
-                     ws: Optional[torch.Tensor] = None, phases: int = 3):
-    """Paged fog decode: q [B, Hq, D]; k_cache / v_cache [P, ps, Hkv, D]
-    views (any page/token/head strides, D contiguous); block_table [B, maxP]
-    int32; seq_lens [B] int32.  Returns out [B, Hq, D] (q.dtype) and, if
-    requested, out_partial fp32 [B, Hq, D+2] = (O/l, m, l) for the
-    context-parallel combine."""
+def _decode_args(q, k_cache, v_cache, block_table, seq_lens, clear_start, fog_alpha, fog_weights, window_size,
+                 sm_scale, kv_pos_offset, q_positions, max_seq_len, ws, tag="decode"):
+    """Checks + the argument tuple shared by the decode entry points (all
+    arguments up to and including dtype), plus the workspace."""
     _need_cuda(q, k_cache, v_cache, block_table, seq_lens)
     B, Hq, D = q.shape
     P, ps, Hkv, Dk = k_cache.shape
@@ -242,18 +235,144 @@ def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     if fog_weights is not None:
         fw = fog_weights if fog_weights.dtype == torch.float32 else fog_weights.float()
         fw = fw.contiguous()
-    if want_out and out is None:
-        out = torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
     lib = _lib.load()
     need = lib.kessie_paged_fog_decode_workspace_size(B, Hq, Hkv, D, int(max_seq_len), ps)
     if ws is None:
-        ws = workspace(need, q.device, "decode")
-    _lib.check(lib.kessie_paged_fog_decode_ex_v2(
-        q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
-        k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), sl.data_ptr(), _p(off), _p(qp),
-        _p(cs), float(fog_alpha), _p(fw), int(window_size), float(sm_scale), B, Hq, Hkv, D, int(max_seq_len),
-        dtype_code(q), _p(out if want_out else None), _p(out_partial), ws.data_ptr(), ws.numel(), int(phases),
-        _stream(stream)), "paged_fog_decode")
+        ws = workspace(need, q.device, tag)
+    # keep the converted tensors alive until the launch
+    keep = (bt, sl, cs, off, qp, fw)
+    args = (q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
+            k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), sl.data_ptr(), _p(off), _p(qp),
+            _p(cs), float(fog_alpha), _p(fw), int(window_size), float(sm_scale), B, Hq, Hkv, D, int(max_seq_len),
+            dtype_code(q))
+    return lib, args, ws, keep
+
+
+def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                     seq_lens: torch.Tensor, clear_start=None, fog_alpha: float = 0.5, fog_weights=None,
+                     window_size: int = 0, sm_scale: Optional[float] = None, kv_pos_offset=None,
+                     q_positions=None, max_seq_len: Optional[int] = None, out: Optional[torch.Tensor] = None,
+                     out_partial: Optional[torch.Tensor] = None, want_out: bool = True, stream=None,
+                     ws: Optional[torch.Tensor] = None, phases: int = 3):
+    """Paged fog decode: q [B, Hq, D]; k_cache / v_cache [P, ps, Hkv, D]
+    views (any page/token/head strides, D contiguous); block_table [B, maxP]
+    int32; seq_lens [B] int32.  Returns out [B, Hq, D] (q.dtype) and, if
+    requested, out_partial fp32 [B, Hq, D+2] = (O/l, m, l) for the
+    context-parallel combine.  One kernel launch (the split merge is fused)."""
+    B, Hq, D = q.shape
+    if want_out and out is None:
+        out = torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
+    lib, args, ws, keep = _decode_args(q, k_cache, v_cache, block_table, seq_lens, clear_start, fog_alpha,
+                                       fog_weights, window_size, sm_scale, kv_pos_offset, q_positions, max_seq_len, ws)
+    _lib.check(lib.kessie_paged_fog_decode_ex_v2(*args, _p(out if want_out else None), _p(out_partial), ws.data_ptr(),
+                                                 ws.numel(), int(phases), _stream(stream)), "paged_fog_decode")
+    return out
+
+
+class CpExchange:
+    """This rank's context-parallel exchange buffer plus the mapped buffers
+    of the other ranks (CUDA IPC over NVLink).  Created collectively: every
+    rank of `group` constructs it with the same shapes."""
+
+    def __init__(self, world: int, rank: int, batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                 device, group=None):
+        import ctypes
+        import torch.distributed as dist
+        lib = _lib.load()
+        self.world, self.rank = int(world), int(rank)
+        self.shape = (int(batch), int(num_q_heads), int(num_kv_heads), int(head_dim))
+        self.nbytes = lib.kessie_cp_exchange_bytes(self.world, batch, num_q_heads, num_kv_heads, head_dim)
+        if self.nbytes == 0:
+            raise ValueError("cp exchange: unsupported shape / world size")
+        dev = torch.device(device)
+        with torch.cuda.device(dev):
+            own = ctypes.c_void_p()
+            handle = (ctypes.c_uint8 * 64)()
+            _lib.check(lib.kessie_cp_exchange_alloc(self.nbytes, ctypes.byref(own), handle), "cp_exchange_alloc")
+            self._own = own.value
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=dev)
+            allh = torch.empty(self.world * 64, dtype=torch.uint8, device=dev)
+            dist.all_gather_into_tensor(allh, mine, group=group)
+            allh = allh.view(self.world, 64).cpu()
+            self._opened = []
+            ptrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                hb = (ctypes.c_uint8 * 64)(*allh[r].tolist())
+                pp = ctypes.c_void_p()
+                _lib.check(lib.kessie_cp_exchange_open(hb, ctypes.byref(pp)), "cp_exchange_open")
+                self._opened.append(pp.value)
+                ptrs.append(pp.value)
+        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.device = dev
+        self._epoch = 0
+
+    def next_epoch(self) -> int:
+        """1, 2, 3, ...; wraps keeping the odd/even alternation."""
+        self._epoch = self._epoch % 0x7FFFFFFE + 1
+        return self._epoch
+
+    def close(self):
+        """Unmap the peers' buffers, then free this rank's.  Call on every
+        rank after a barrier that follows the last step."""
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                lib.kessie_cp_exchange_close(p)
+            self._opened = []
+            if self._own:
+                lib.kessie_cp_exchange_free(self._own)
+                self._own = None
+
+
+def paged_fog_decode_cp(exchange: "CpExchange", epoch: int, q: torch.Tensor, k_cache: torch.Tensor,
+                        v_cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor, clear_start=None,
+                        fog_alpha: float = 0.5, fog_weights=None, window_size: int = 0,
+                        sm_scale: Optional[float] = None, kv_pos_offset=None, q_positions=None,
+                        max_seq_len: Optional[int] = None, out: Optional[torch.Tensor] = None,
+                        out_partial: Optional[torch.Tensor] = None, wait_timeout_s: float = 2.0, phases: int = 3,
+                        stream=None, ws: Optional[torch.Tensor] = None):
+    """One context-parallel decode step over this rank's shard: the decode
+    kernel pushes the shard result of each (seq, kv_head) group into every
+    rank's exchange buffer (phases bit 0); the combine kernel waits for all
+    ranks and writes out / out_partial (bit 1)."""
+    B, Hq, D = q.shape
+    if tuple(exchange.shape) != (B, Hq, k_cache.shape[2], D):
+        raise ValueError(f"exchange buffers were sized for {tuple(exchange.shape)}, this step is "
+                         f"{(B, Hq, k_cache.shape[2], D)} (B, Hq, Hkv, D)")
+    if (phases & 2) and out is None and out_partial is None:
+        out = torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
+    lib, args, ws, keep = _decode_args(q, k_cache, v_cache, block_table, seq_lens, clear_start, fog_alpha,
+                                       fog_weights, window_size, sm_scale, kv_pos_offset, q_positions, max_seq_len, ws)
+    _lib.check(lib.kessie_paged_fog_decode_cp_v2(
+        *args, exchange.ptrs, exchange.rank, exchange.world, int(epoch), int(wait_timeout_s * 1e9), _p(out),
+        _p(out_partial), ws.data_ptr(), ws.numel(), int(phases), _stream(stream)), "paged_fog_decode_cp")
+    return out
+
+
+def cp_combine(exchange: "CpExchange", epoch: int, batch: int, num_q_heads: int, num_kv_heads: int,
+               out: Optional[torch.Tensor] = None, out_partial: Optional[torch.Tensor] = None,
+               wait_timeout_s: float = 2.0, stream=None):
+    """Phase 2 of paged_fog_decode_cp on its own: wait for every rank's
+    shard results of `epoch` and merge them into out [B, Hq, D] and/or
+    out_partial [B, Hq, D+2]."""
+    t = out if out is not None else out_partial
+    if t is None:
+        raise ValueError("cp_combine needs out or out_partial")
+    _need_cuda(t)
+    D = out.shape[-1] if out is not None else out_partial.shape[-1] - 2
+    if tuple(exchange.shape) != (batch, num_q_heads, num_kv_heads, D):
+        raise ValueError(f"exchange buffers were sized for {tuple(exchange.shape)}, not "
+                         f"{(batch, num_q_heads, num_kv_heads, D)}")
+    for t_ in (out, out_partial):
+        if t_ is not None and (not t_.is_contiguous() or t_.shape[:2] != (batch, num_q_heads)):
+            raise ValueError("cp_combine outputs must be contiguous [B, Hq, ...]")
+    dt = dtype_code(out) if out is not None else 1          # bf16 (unused: no out)
+    _lib.check(_lib.load().kessie_cp_combine_v2(exchange.ptrs, exchange.rank, exchange.world, int(epoch),
+                                                int(wait_timeout_s * 1e9), batch, num_q_heads, num_kv_heads, D, dt,
+                                                _p(out), _p(out_partial), _stream(stream)), "cp_combine")
     return out
 
 

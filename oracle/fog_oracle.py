@@ -143,7 +143,11 @@ def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal:
     as the square reference; validated against its last rows.
     With return_partials, also returns (m, l, O_unnormalised) in natural-log
     units for the LSE combine.  dtype=np.float32 evaluates in fp32 like the
-    reference's torch path (used for the timed CPU baseline)."""
+    reference's torch path (used for the timed CPU baseline).
+    A row with no visible key (N == 0, or every key masked) is 0 with
+    m = -inf, l = 0: the reference's softmax of an all-masked row is NaN, so
+    this build defines the empty row as the neutral element of the merge
+    (a context-parallel shard may hold none of a sequence's window)."""
     q = np.asarray(q, dtype=dtype)
     k = np.asarray(k, dtype=dtype)
     v = np.asarray(v, dtype=dtype)
@@ -162,7 +166,7 @@ def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal:
         kh = h // g
         s = (q[h] @ k[kh].T) * dtype(sm_scale)
         s = np.where(ok, s, dtype(-np.inf))
-        m = s.max(axis=-1, keepdims=True)
+        m = s.max(axis=-1, keepdims=True, initial=-np.inf)
         mf = np.where(np.isfinite(m), m, 0.0)
         p = np.exp(s - mf)
         l = p.sum(axis=-1, keepdims=True)

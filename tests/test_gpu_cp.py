@@ -1,10 +1,13 @@
-"""Multi-GPU parity of the context-parallel decode (NCCL all-gather + CUDA LSE
-merge): two ranks, each holding a contiguous position shard of every
+"""Multi-GPU parity of the context-parallel decode, both exchanges (NVLink
+peer stores from the decode kernel + bounded-wait combine; NCCL all-gather +
+LSE merge kernel): two ranks, each holding a contiguous position shard of every
 sequence, must reproduce the single-GPU decode over the whole cache.
 Skipped with fewer than two GPUs."""
 
 import os
+import queue
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -46,15 +49,22 @@ def _rank(rank, world, port, out_q):
     off = torch.full((B,), a, dtype=torch.int32, device=dev)
     qpos = torch.full((B,), N - 1, dtype=torch.int32, device=dev)
     cs = torch.full((B,), N - 512, dtype=torch.int32, device=dev)
-    dec = ContextParallelFogDecode(B, Hq, D, torch.bfloat16, dev)
-    out = dec(q, kv[:, :, 0], kv[:, :, 1], bt_loc, lens, off, qpos, cs, 0.5, 0, None, (pg1 - pg0) * ps).clone()
-    torch.cuda.synchronize()
+    outs = {}
+    for exchange in ("p2p", "nccl"):
+        dec = ContextParallelFogDecode(B, Hq, D, torch.bfloat16, dev, num_kv_heads=Hkv, exchange=exchange)
+        for _ in range(3):              # several steps: both slots of the exchange buffers
+            out = dec(q, kv[:, :, 0], kv[:, :, 1], bt_loc, lens, off, qpos, cs, 0.5, 0, None, (pg1 - pg0) * ps)
+        outs[exchange] = out.clone()
+        torch.cuda.synchronize()
+        dec.close()
+    status = ops.read_device_status()
     if rank == 0:
         full = ops.paged_fog_decode(q, kv[:, :, 0], kv[:, :, 1], bt_full.to(dev),
                                     torch.full((B,), N, dtype=torch.int32, device=dev),
                                     clear_start=cs, fog_alpha=0.5)
         torch.cuda.synchronize()
-        out_q.put((out.float().cpu().numpy(), full.float().cpu().numpy()))
+        out_q.put((outs["p2p"].float().cpu().numpy(), outs["nccl"].float().cpu().numpy(),
+                   full.float().cpu().numpy(), status))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -68,9 +78,23 @@ def test_context_parallel_two_gpus_matches_single_gpu():
     procs = [ctx.Process(target=_rank, args=(r, 2, port, out_q)) for r in range(2)]
     for p in procs:
         p.start()
-    got, want = out_q.get(timeout=300)
+    deadline = time.time() + 300
+    res = None
+    while res is None:
+        try:
+            res = out_q.get(timeout=2)
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead or time.time() > deadline:
+                for p in procs:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail(f"rank process failed (exit codes {[p.exitcode for p in procs]})")
+    got, got_nccl, want, status = res
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    assert status == 0
     np.testing.assert_allclose(got, want, atol=2e-2, rtol=1e-2)
+    np.testing.assert_allclose(got_nccl, want, atol=2e-2, rtol=1e-2)
     assert np.isfinite(got).all()

@@ -207,3 +207,66 @@ def test_lse_combine_matches_oracle():
     out = ops.lse_combine(parts, out_dtype=torch.float32)
     torch.cuda.synchronize()
     np.testing.assert_allclose(to_np(out), O.lse_combine(ms, ls, os_), atol=1e-5, rtol=1e-5)
+
+
+def test_decode_empty_and_excluded_sequences():
+    """Sequences with no visible key (length 0, or a window that ends before
+    the shard) give zero rows and do not disturb their neighbours."""
+    got, want = run_case(51, 4, 8, 2, 128, "bf16", [0, 300, 0, 45])
+    np.testing.assert_allclose(got, want, **TOL["bf16"])
+    assert (got[0] == 0).all() and (got[2] == 0).all()
+    got, want = run_case(52, 3, 8, 2, 128, "bf16", [200, 700, 64], window=100, q_pos=[5000, 699, 63],
+                         kv_off=[0, 0, 0])
+    np.testing.assert_allclose(got, want, **TOL["bf16"])
+    assert (got[0] == 0).all()
+
+
+@pytest.mark.parametrize("B,D", [(100, 128), (70, 64)])
+def test_decode_large_batch_many_segments(B, D):
+    """More sequences than a warp (multi-round range search) and many short
+    groups per CTA (many segments, many group merges)."""
+    lens = np.random.default_rng(B).integers(1, 400, size=B)
+    got, want = run_case(B + D, B, 8, 2, D, "bf16", lens)
+    np.testing.assert_allclose(got, want, **TOL["bf16"])
+
+
+def test_decode_workspace_reuse_is_deterministic():
+    """The per-group arrival counters return to zero after every call: calls
+    of different shapes that share the cached workspace, then the first
+    shape again, give bit-identical results (the merge order is fixed by
+    slot, not by arrival)."""
+    from kessie_b200 import ops
+    outs = []
+    for lens in ([5000, 3000, 17], [40], [5000, 3000, 17]):
+        B = len(lens)
+        kvn, kv = make_paged(61, 1000, 16, 2, 128, "bf16")
+        bt = torch.from_numpy(random_block_table(62, lens, 16, 1000)).cuda()
+        q = to_dev(rnd(63, (B, 8, 128)), "bf16")
+        o = ops.paged_fog_decode(q, kv[:, :, 0], kv[:, :, 1], bt, torch.tensor(lens, dtype=torch.int32, device="cuda"),
+                                 clear_start=torch.tensor([n - 64 for n in lens], dtype=torch.int32, device="cuda"))
+        outs.append(o.clone())
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[2])
+    assert ops.read_device_status() == 0
+
+
+def test_decode_workspace_garbage_is_ignored():
+    """A workspace full of leftover bytes (another shape's partials, random
+    data) needs no clearing: stale arrival counters carry another tag."""
+    from kessie_b200 import ops, _lib
+    lens = [3000, 40, 999, 1]
+    B = len(lens)
+    kvn, kv = make_paged(81, 400, 16, 2, 128, "bf16")
+    bt_np = random_block_table(82, lens, 16, 400)
+    bt = torch.from_numpy(bt_np).cuda()
+    q = ROUND["bf16"](rnd(83, (B, 8, 128)))
+    need = _lib.load().kessie_paged_fog_decode_workspace_size(B, 8, 2, 128, bt.shape[1] * 16, 16)
+    g = torch.Generator(device="cuda").manual_seed(84)
+    ws = torch.randint(0, 256, (need,), dtype=torch.uint8, device="cuda", generator=g)
+    cs = [n - 64 for n in lens]
+    out = ops.paged_fog_decode(to_dev(q, "bf16"), kv[:, :, 0], kv[:, :, 1], bt,
+                               torch.tensor(lens, dtype=torch.int32, device="cuda"),
+                               clear_start=torch.tensor(cs, dtype=torch.int32, device="cuda"), ws=ws)
+    torch.cuda.synchronize()
+    want = O.paged_fog_decode(q, kvn[:, :, 0], kvn[:, :, 1], bt_np, lens, cs, 0.5)
+    np.testing.assert_allclose(to_np(out), want, **TOL["bf16"])

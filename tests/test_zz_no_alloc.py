@@ -76,13 +76,14 @@ def test_noalloc_decode_matches_workspace_decode_twice():
 def test_noalloc_decode_rejects_shapes_beyond_its_scratch():
     from kessie_b200 import _lib
     lib = _lib.load()
-    # 64 sequences x 64 heads at 1M tokens needs far more than the built-in array
-    need = lib.kessie_paged_fog_decode_workspace_size(64, 64, 8, 128, 1 << 20, 16)
+    # the scratch holds one fp32 partial per query head for every (CTA, group)
+    # segment: 1024 sequences x 128 query heads is far beyond the built-in array
+    need = lib.kessie_paged_fog_decode_workspace_size(1024, 128, 8, 128, 4096, 16)
     assert need > 16 * 1024 * 1024
     z = torch.zeros(16, dtype=torch.int32, device="cuda")
     rc = lib.kessie_paged_fog_decode_noalloc_v2(z.data_ptr(), 0, 0, z.data_ptr(), z.data_ptr(), 0, 0, 0, 1, 16,
                                                 z.data_ptr(), 0, z.data_ptr(), None, None, None, ctypes.c_float(0.5),
-                                                None, 0, ctypes.c_float(0.1), 64, 64, 8, 128, 1 << 20, 1,
+                                                None, 0, ctypes.c_float(0.1), 1024, 128, 8, 128, 4096, 1,
                                                 z.data_ptr(), None, None)
     assert rc == 3
     st, msg = _lib.last_error()
