@@ -86,11 +86,14 @@ def load_traffic(kernel_key):
 
 # ----------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi sampler for the timed region (our own child process)."""
+    """SM clock / throttle-reason sampler for the timed region: an NVML thread
+    polling every 10 ms (reads only), nvidia-smi as the fallback."""
 
     FIELDS = ["clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
               "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
               "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+    # NVML clocks-event reason bits
+    NVML_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, local_rank):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -100,10 +103,34 @@ class ClockSampler:
             if local_rank < len(parts) and parts[local_rank].isdigit():
                 idx = int(parts[local_rank])
         self.idx = idx
+        self.local_rank = local_rank
         self.lines = []
+        self.samples = []          # (sm_mhz, max_mhz, reasons bitmask)
         self.proc = None
+        self.nvml = None
+        self._stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.local_rank).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.idx)
 
     def start(self):
+        try:
+            pynvml, h = self._nvml_handle()
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.nvml = (pynvml, h, mx)
+        except Exception:
+            self.nvml = None
+        if self.nvml is not None:
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + ",".join(self.FIELDS),
                                           "--format=csv,noheader,nounits", "-lms", "50"],
@@ -114,11 +141,29 @@ class ClockSampler:
         self.t = threading.Thread(target=self._read, daemon=True)
         self.t.start()
 
+    def _poll(self):
+        pynvml, h, mx = self.nvml
+        while not self._stop.is_set():
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                try:
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:
+                    rs = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((float(sm), float(mx), int(rs)))
+            except Exception:
+                pass
+            self._stop.wait(0.01)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self):
+        self._stop.set()
+        if self.nvml is not None:
+            self.t.join(timeout=2)
+            return
         if self.proc is None:
             return
         self.proc.terminate()
@@ -131,6 +176,11 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s_, m_, bits in self.samples:
+            sm.append(s_); mx.append(m_)
+            for n, bit in self.NVML_BITS.items():
+                if bits & bit:
+                    reasons.add(n)
         for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 8:
@@ -145,7 +195,7 @@ class ClockSampler:
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvml" if self.samples else "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------- workloads

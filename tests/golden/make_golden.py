@@ -211,9 +211,22 @@ def gen_paged():
     save("paged_cache.npz", **out)
 
 
+def gen_kv_store():
+    """KeSSieCPUKVStore bookkeeping (kessie_kv_connector.py:65-229) on CPU."""
+    import json
+    import kessie_kv_connector as C
+    sys.path.insert(0, HERE)
+    from kv_store_script import run_kv_store_script
+    log = run_kv_store_script(C.KeSSieCPUKVStore, C, torch)
+    with open(os.path.join(HERE, "kv_store.json"), "w") as f:
+        json.dump(log, f, indent=0)
+    print("wrote kv_store.json", len(log), "steps")
+
+
 if __name__ == "__main__":
     gen_fog()
     gen_rope()
     gen_attention()
     gen_config1()
     gen_paged()
+    gen_kv_store()
