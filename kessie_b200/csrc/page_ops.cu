@@ -304,15 +304,18 @@ void launch_rows(int kt, dim3 grid, int threads, size_t smem, cudaStream_t st, T
 
 
 // Token-block RoPE kernel shared by the in-place remap and the fused recall
-// insert.  A CTA owns `tpb` tokens; each thread first issues its loads (one
-// K low/high 16-byte pair, and for the insert its V vectors), then the CTA
-// builds a (cos, sin, cos, sin) float4 table for the tokens' angle pairs, and
-// every thread rotates its pair with 4 vector table reads per 8 elements.
+// insert.  A CTA owns `tpb` tokens.  A thread's item is (token, head group g,
+// 16-byte chunk kc of the low half); it rotates chunk kc of the HPT heads
+// g, g + H/HPT, ..., so every (cos, sin) table entry it reads from shared
+// memory serves HPT heads (the table reads, not DRAM, bounded the one-head
+// form).  Order: issue the loads (HPT K low/high pairs; for the insert the
+// V vectors), build the float4 table (cos d, sin d, cos d+1, sin d+1) of the
+// CTA's tokens, barrier, rotate and store.
 // INSERT: destination row of token t is page page_ids[t / ps], slot t % ps
 // (first token of a page sets page_valid / page_positions); the V rows are
 // copied alongside.
-template <typename T, bool INSERT, int KPT>
-__global__ void __launch_bounds__(256, INSERT ? 8 : 4) rope_tokens_kernel(
+template <typename T, bool INSERT, int HPT>
+__global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
     T* __restrict__ dst, const T* __restrict__ srck, const T* __restrict__ srcv, int num_tokens, int num_heads,
     int half, int64_t sts, int64_t shs, int64_t dts, int64_t dhs, int64_t dkv, int64_t page_stride, int ps,
     const int32_t* __restrict__ page_ids, int max_pages, int8_t* __restrict__ valid, int32_t* __restrict__ positions,
@@ -321,26 +324,32 @@ __global__ void __launch_bounds__(256, INSERT ? 8 : 4) rope_tokens_kernel(
     extern __shared__ float4 tab[];                 // [tpb][half/2] of (cos d, sin d, cos d+1, sin d+1)
     constexpr int N = VecOps<T>::N;
     const int hc = half / N;                        // 16-byte chunks per half row
+    const int hg = num_heads / HPT;                 // head groups
     const int t0 = blockIdx.x * tpb;
     const int nt = min(tpb, num_tokens - t0);
-    const int kitems = nt * num_heads * hc;
+    const int kitems = nt * hg * hc;                // <= blockDim by construction of tpb
     const int vitems = INSERT ? nt * num_heads * 2 * hc : 0;
-    // ---- 1. loads: KPT K pairs and (insert) 2*KPT V vectors per thread, all in flight
-    uint4 lo[KPT], hi[KPT], vv[INSERT ? 2 * KPT : 1];
+    const bool kact = (int)threadIdx.x < kitems;
+    int kc = 0, g = 0, ktl = 0;
+    if (kact) {
+        kc = threadIdx.x % hc;
+        const int r = threadIdx.x / hc;
+        g = r % hg;
+        ktl = r / hg;
+    }
+    // ---- 1. loads: HPT K pairs and (insert) 2*HPT V vectors per thread, all in flight
+    uint4 lo[HPT], hi[HPT], vv[INSERT ? 2 * HPT : 1];
+    if (kact) {
 #pragma unroll
-    for (int k = 0; k < KPT; ++k) {
-        const int ki = threadIdx.x + k * blockDim.x;
-        if (ki < kitems) {
-            const int kc = ki % hc, r = ki / hc;
-            const int kh = r % num_heads, ktl = r / num_heads;
-            const T* row = srck + (int64_t)(t0 + ktl) * sts + (int64_t)kh * shs;
-            lo[k] = *reinterpret_cast<const uint4*>(row + kc * N);
-            hi[k] = *reinterpret_cast<const uint4*>(row + half + kc * N);
+        for (int j = 0; j < HPT; ++j) {
+            const T* row = srck + (int64_t)(t0 + ktl) * sts + (int64_t)(g + j * hg) * shs;
+            lo[j] = *reinterpret_cast<const uint4*>(row + kc * N);
+            hi[j] = *reinterpret_cast<const uint4*>(row + half + kc * N);
         }
     }
     if (INSERT) {
 #pragma unroll
-        for (int j = 0; j < 2 * KPT; ++j) {
+        for (int j = 0; j < 2 * HPT; ++j) {
             const int vi = threadIdx.x + j * blockDim.x;
             if (vi < vitems) {
                 const int c = vi % (2 * hc), r = vi / (2 * hc);
@@ -362,7 +371,7 @@ __global__ void __launch_bounds__(256, INSERT ? 8 : 4) rope_tokens_kernel(
         tab[i] = cs;
     }
     __syncthreads();
-    // ---- 3. rotate K pairs, store; copy V
+    // ---- 3. rotate the K pairs with one table read for all HPT heads; copy V
     auto dst_row = [&](int tl, int h, bool& ok) -> T* {
         const int t = t0 + tl;
         if (!INSERT) { ok = true; return dst + (int64_t)t * dts + (int64_t)h * dhs; }
@@ -370,31 +379,31 @@ __global__ void __launch_bounds__(256, INSERT ? 8 : 4) rope_tokens_kernel(
         ok = phys >= 0 && phys < max_pages;
         return dst + (int64_t)(ok ? phys : 0) * page_stride + (int64_t)(t % ps) * dts + (int64_t)h * dhs;
     };
-#pragma unroll
-    for (int k = 0; k < KPT; ++k) {
-        const int ki = threadIdx.x + k * blockDim.x;
-        if (ki >= kitems) break;
-        const int kc = ki % hc, r = ki / hc;
-        const int kh = r % num_heads, ktl = r / num_heads;
-        float a[N], bb[N], ra[N], rb[N];
-        VecOps<T>::unpack(lo[k], a);
-        VecOps<T>::unpack(hi[k], bb);
+    if (kact) {
+        float4 cs[N / 2];
         const float4* tp = tab + ktl * hp + kc * (N / 2);
 #pragma unroll
-        for (int j = 0; j < N / 2; ++j) {
-            const float4 cs = tp[j];
-            ra[2 * j] = a[2 * j] * cs.x - bb[2 * j] * cs.y;
-            rb[2 * j] = a[2 * j] * cs.y + bb[2 * j] * cs.x;
-            ra[2 * j + 1] = a[2 * j + 1] * cs.z - bb[2 * j + 1] * cs.w;
-            rb[2 * j + 1] = a[2 * j + 1] * cs.w + bb[2 * j + 1] * cs.z;
+        for (int q = 0; q < N / 2; ++q) cs[q] = tp[q];
+#pragma unroll
+        for (int j = 0; j < HPT; ++j) {
+            float a[N], bb[N], ra[N], rb[N];
+            VecOps<T>::unpack(lo[j], a);
+            VecOps<T>::unpack(hi[j], bb);
+#pragma unroll
+            for (int q = 0; q < N / 2; ++q) {
+                ra[2 * q] = a[2 * q] * cs[q].x - bb[2 * q] * cs[q].y;
+                rb[2 * q] = a[2 * q] * cs[q].y + bb[2 * q] * cs[q].x;
+                ra[2 * q + 1] = a[2 * q + 1] * cs[q].z - bb[2 * q + 1] * cs[q].w;
+                rb[2 * q + 1] = a[2 * q + 1] * cs[q].w + bb[2 * q + 1] * cs[q].z;
+            }
+            bool ok;
+            T* row = dst_row(ktl, g + j * hg, ok);
+            if (ok) {
+                *reinterpret_cast<uint4*>(row + kc * N) = VecOps<T>::pack(ra);
+                *reinterpret_cast<uint4*>(row + half + kc * N) = VecOps<T>::pack(rb);
+            }
         }
-        bool ok;
-        T* row = dst_row(ktl, kh, ok);
-        if (ok) {
-            *reinterpret_cast<uint4*>(row + kc * N) = VecOps<T>::pack(ra);
-            *reinterpret_cast<uint4*>(row + half + kc * N) = VecOps<T>::pack(rb);
-        }
-        if (INSERT && kh == 0 && kc == 0) {
+        if (INSERT && g == 0 && kc == 0) {
             const int t = t0 + ktl;
             if (t % ps == 0) {
                 const int phys = page_ids[t / ps];
@@ -408,7 +417,7 @@ __global__ void __launch_bounds__(256, INSERT ? 8 : 4) rope_tokens_kernel(
     }
     if (INSERT) {
 #pragma unroll
-        for (int j = 0; j < 2 * KPT; ++j) {
+        for (int j = 0; j < 2 * HPT; ++j) {
             const int vi = threadIdx.x + j * blockDim.x;
             if (vi < vitems) {
                 const int c = vi % (2 * hc), r = vi / (2 * hc);
@@ -421,15 +430,14 @@ __global__ void __launch_bounds__(256, INSERT ? 8 : 4) rope_tokens_kernel(
     }
 }
 
-// Tokens per CTA for rope_tokens_kernel: one K pair per thread (and at most
-// 4 V vectors per thread for the insert); 0 when the shape does not fit.
-constexpr int kRopeKPT = 1;   // K pairs per thread (more measured slower: registers cost occupancy)
-int tokens_per_block(int H, int half, int N, bool insert) {
-    (void)insert;
-    if (half % N) return 0;
-    const int per_token = H * (half / N);
-    if (per_token > 256 * kRopeKPT) return 0;
-    int tpb = (256 * kRopeKPT) / per_token;
+// Tokens per CTA for rope_tokens_kernel with `hpt` heads per thread: one K
+// item per thread (2*hpt V vectors per thread for the insert); 0 when the
+// shape does not fit.
+int tokens_per_block(int H, int half, int N, int hpt) {
+    if (half % N || H % hpt) return 0;
+    const int per_token = (H / hpt) * (half / N);
+    if (per_token > 256) return 0;
+    int tpb = 256 / per_token;
     const int max_tab = (48 * 1024) / ((half / 2) * 16);     // angle table within the default shared memory
     return std::min(tpb, max_tab);
 }
@@ -446,10 +454,12 @@ int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int
     const int tt = 16;
     // The row-parallel kernel measured slower than rope_remap_kernel for the
     // in-place case (56.5 vs 34.5 us at config 2); kept for the insert path.
-    const int tpb_t = vec ? tokens_per_block(H, half, N, false) : 0;
+    const int hpt = (H % 2 == 0) ? 2 : 1;        // heads per thread sharing one table read
+    const int tpb_t = vec ? tokens_per_block(H, half, N, hpt) : 0;
     if (tpb_t > 0) {
         size_t smem = (size_t)tpb_t * (half / 2) * sizeof(float4);
-        rope_tokens_kernel<T, false, kRopeKPT><<<(T_ + tpb_t - 1) / tpb_t, 256, smem, st>>>(
+        auto kern = hpt == 2 ? rope_tokens_kernel<T, false, 2> : rope_tokens_kernel<T, false, 1>;
+        kern<<<(T_ + tpb_t - 1) / tpb_t, 256, smem, st>>>(
             (T*)k, (const T*)k, nullptr, T_, H, half, ts, hs, ts, hs, 0, 0, 1, nullptr, 0, nullptr, nullptr, 0, orig, tgt,
             ft, tpb_t, nullptr);
     } else if (vec && rows_shape<T>(H, D, tt, threads, cpr, kt)) {
@@ -823,11 +833,13 @@ int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv
     int pages = (T_ + g.page_size - 1) / g.page_size;
     if (pages == 0) return check_launch("page_insert (empty)");
     int threads = 0, cpr = 0, kt = 0;
-    const int tpb_i = (orig && vec) ? tokens_per_block(g.num_heads, g.head_dim / 2, N, true) : 0;
+    const int hpt = (g.num_heads % 2 == 0) ? 2 : 1;
+    const int tpb_i = (orig && vec) ? tokens_per_block(g.num_heads, g.head_dim / 2, N, hpt) : 0;
     if (tpb_i > 0) {
         FreqTable ft = make_freqs(theta, g.head_dim / 2);
         size_t smem = (size_t)tpb_i * (g.head_dim / 4) * sizeof(float4);
-        rope_tokens_kernel<T, true, kRopeKPT><<<(T_ + tpb_i - 1) / tpb_i, 256, smem, st>>>(
+        auto kern = hpt == 2 ? rope_tokens_kernel<T, true, 2> : rope_tokens_kernel<T, true, 1>;
+        kern<<<(T_ + tpb_i - 1) / tpb_i, 256, smem, st>>>(
             (T*)cache, (const T*)nk, (const T*)nv, T_, g.num_heads, g.head_dim / 2, sts, shs, g.token_stride,
             g.head_stride, g.kv_stride, g.page_stride, g.page_size, ids, g.max_pages, valid, positions, conv_pos, orig,
             tgt, ft, tpb_i, status);
