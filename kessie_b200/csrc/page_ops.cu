@@ -307,15 +307,16 @@ void launch_rows(int kt, dim3 grid, int threads, size_t smem, cudaStream_t st, T
 // insert.  A CTA owns `tpb` tokens.  A thread's item is (token, head group g,
 // 16-byte chunk kc of the low half); it rotates chunk kc of the HPT heads
 // g, g + H/HPT, ..., so every (cos, sin) table entry it reads from shared
-// memory serves HPT heads (the table reads, not DRAM, bounded the one-head
-// form).  Order: issue the loads (HPT K low/high pairs; for the insert the
-// V vectors), build the float4 table (cos d, sin d, cos d+1, sin d+1) of the
-// CTA's tokens, barrier, rotate and store.
+// memory serves HPT heads.  Order: start 16-byte cp.async copies of the
+// CTA's K rows (and V rows for the insert) into shared memory -- the bytes in
+// flight cost no registers, so 8 CTAs fit per SM and keep ~128 KB per SM in
+// flight while each CTA builds its float4 table (cos d, sin d, cos d+1,
+// sin d+1); then wait, barrier, rotate out of shared memory and store.
 // INSERT: destination row of token t is page page_ids[t / ps], slot t % ps
 // (first token of a page sets page_valid / page_positions); the V rows are
 // copied alongside.
 template <typename T, bool INSERT, int HPT>
-__global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
+__global__ void __launch_bounds__(256, 6) rope_tokens_kernel(
     T* __restrict__ dst, const T* __restrict__ srck, const T* __restrict__ srcv, int num_tokens, int num_heads,
     int half, int64_t sts, int64_t shs, int64_t dts, int64_t dhs, int64_t dkv, int64_t page_stride, int ps,
     const int32_t* __restrict__ page_ids, int max_pages, int8_t* __restrict__ valid, int32_t* __restrict__ positions,
@@ -325,6 +326,10 @@ __global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
     constexpr int N = VecOps<T>::N;
     const int hc = half / N;                        // 16-byte chunks per half row
     const int hg = num_heads / HPT;                 // head groups
+    const int rowe = num_heads * 2 * half;          // elements of one token's K (or V) row
+    T* ksm = reinterpret_cast<T*>(tab + tpb * (half / 2));   // [tpb][H][D] K rows
+    T* vsm = ksm + tpb * rowe;                               // [tpb][H][D] V rows (insert)
+    long long* rowoff = reinterpret_cast<long long*>(vsm + (INSERT ? tpb * rowe : 0));  // [tpb] insert dst offsets
     const int t0 = blockIdx.x * tpb;
     const int nt = min(tpb, num_tokens - t0);
     const int kitems = nt * hg * hc;                // <= blockDim by construction of tpb
@@ -337,14 +342,15 @@ __global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
         g = r % hg;
         ktl = r / hg;
     }
-    // ---- 1. loads: HPT K pairs and (insert) 2*HPT V vectors per thread, all in flight
-    uint4 lo[HPT], hi[HPT], vv[INSERT ? 2 * HPT : 1];
+    // ---- 1. async copies: HPT K pairs and (insert) 2*HPT V vectors per thread
     if (kact) {
 #pragma unroll
         for (int j = 0; j < HPT; ++j) {
-            const T* row = srck + (int64_t)(t0 + ktl) * sts + (int64_t)(g + j * hg) * shs;
-            lo[j] = *reinterpret_cast<const uint4*>(row + kc * N);
-            hi[j] = *reinterpret_cast<const uint4*>(row + half + kc * N);
+            const int h = g + j * hg;
+            const T* row = srck + (int64_t)(t0 + ktl) * sts + (int64_t)h * shs;
+            T* srow = ksm + ktl * rowe + h * 2 * half;
+            cp_async16(srow + kc * N, row + kc * N);
+            cp_async16(srow + half + kc * N, row + half + kc * N);
         }
     }
     if (INSERT) {
@@ -354,10 +360,12 @@ __global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
             if (vi < vitems) {
                 const int c = vi % (2 * hc), r = vi / (2 * hc);
                 const int h = r % num_heads, tl = r / num_heads;
-                vv[j] = ldg_stream(srcv + (int64_t)(t0 + tl) * sts + (int64_t)h * shs + c * N);
+                cp_async16(vsm + tl * rowe + h * 2 * half + c * N,
+                           srcv + (int64_t)(t0 + tl) * sts + (int64_t)h * shs + c * N);
             }
         }
     }
+    cp_async_commit();
     // ---- 2. angle table (one float4 = two consecutive d)
     const int hp = half / 2;
     for (int i = threadIdx.x; i < nt * hp; i += blockDim.x) {
@@ -370,14 +378,31 @@ __global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
         rope_sincos(dlt * ft.f[2 * dp + 1], &cs.w, &cs.z);
         tab[i] = cs;
     }
+    if (INSERT) {
+        // destination row of each token (page, slot), once per token; the first
+        // token of a page sets page_valid / page_positions
+        for (int tl = threadIdx.x; tl < nt; tl += blockDim.x) {
+            const int t = t0 + tl;
+            const int phys = page_ids[t / ps];
+            const bool ok = phys >= 0 && phys < max_pages;
+            rowoff[tl] = ok ? (long long)phys * page_stride + (long long)(t % ps) * dts : -1ll;
+            if (t % ps == 0) {
+                if (!ok) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
+                else {
+                    if (valid) valid[phys] = 1;
+                    if (positions) positions[phys] = conv_pos + t;
+                }
+            }
+        }
+    }
+    cp_async_wait_all();
     __syncthreads();
     // ---- 3. rotate the K pairs with one table read for all HPT heads; copy V
     auto dst_row = [&](int tl, int h, bool& ok) -> T* {
-        const int t = t0 + tl;
-        if (!INSERT) { ok = true; return dst + (int64_t)t * dts + (int64_t)h * dhs; }
-        const int phys = page_ids[t / ps];
-        ok = phys >= 0 && phys < max_pages;
-        return dst + (int64_t)(ok ? phys : 0) * page_stride + (int64_t)(t % ps) * dts + (int64_t)h * dhs;
+        if (!INSERT) { ok = true; return dst + (int64_t)(t0 + tl) * dts + (int64_t)h * dhs; }
+        const long long off = rowoff[tl];
+        ok = off >= 0;
+        return dst + (ok ? off : 0) + (int64_t)h * dhs;
     };
     if (kact) {
         float4 cs[N / 2];
@@ -387,8 +412,9 @@ __global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
 #pragma unroll
         for (int j = 0; j < HPT; ++j) {
             float a[N], bb[N], ra[N], rb[N];
-            VecOps<T>::unpack(lo[j], a);
-            VecOps<T>::unpack(hi[j], bb);
+            const T* srow = ksm + ktl * rowe + (g + j * hg) * 2 * half;
+            VecOps<T>::unpack(*reinterpret_cast<const uint4*>(srow + kc * N), a);
+            VecOps<T>::unpack(*reinterpret_cast<const uint4*>(srow + half + kc * N), bb);
 #pragma unroll
             for (int q = 0; q < N / 2; ++q) {
                 ra[2 * q] = a[2 * q] * cs[q].x - bb[2 * q] * cs[q].y;
@@ -403,17 +429,6 @@ __global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
                 *reinterpret_cast<uint4*>(row + half + kc * N) = VecOps<T>::pack(rb);
             }
         }
-        if (INSERT && g == 0 && kc == 0) {
-            const int t = t0 + ktl;
-            if (t % ps == 0) {
-                const int phys = page_ids[t / ps];
-                if (phys < 0 || phys >= max_pages) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
-                else {
-                    if (valid) valid[phys] = 1;
-                    if (positions) positions[phys] = conv_pos + t;
-                }
-            }
-        }
     }
     if (INSERT) {
 #pragma unroll
@@ -424,7 +439,7 @@ __global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
                 const int h = r % num_heads, tl = r / num_heads;
                 bool ok;
                 T* row = dst_row(tl, h, ok);
-                if (ok) stg_stream(row + dkv + c * N, vv[j]);
+                if (ok) stg_stream(row + dkv + c * N, *reinterpret_cast<const uint4*>(vsm + tl * rowe + h * 2 * half + c * N));
             }
         }
     }
@@ -433,13 +448,17 @@ __global__ void __launch_bounds__(256, 4) rope_tokens_kernel(
 // Tokens per CTA for rope_tokens_kernel with `hpt` heads per thread: one K
 // item per thread (2*hpt V vectors per thread for the insert); 0 when the
 // shape does not fit.
-int tokens_per_block(int H, int half, int N, int hpt) {
+int tokens_per_block(int H, int half, int N, int hpt, int elem_bytes, bool insert) {
     if (half % N || H % hpt) return 0;
     const int per_token = (H / hpt) * (half / N);
     if (per_token > 256) return 0;
     int tpb = 256 / per_token;
-    const int max_tab = (48 * 1024) / ((half / 2) * 16);     // angle table within the default shared memory
-    return std::min(tpb, max_tab);
+    // angle table + staged K (and V) rows within the default 48 KB of shared memory
+    const int per_tok_smem = (half / 2) * 16 + H * 2 * half * elem_bytes * (insert ? 2 : 1) + (insert ? 8 : 0);
+    return std::min(tpb, (48 * 1024) / per_tok_smem);
+}
+size_t rope_tokens_smem(int tpb, int H, int half, int elem_bytes, bool insert) {
+    return (size_t)tpb * ((half / 2) * 16 + (size_t)H * 2 * half * elem_bytes * (insert ? 2 : 1) + (insert ? 8 : 0));
 }
 
 template <typename T>
@@ -455,9 +474,9 @@ int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int
     // The row-parallel kernel measured slower than rope_remap_kernel for the
     // in-place case (56.5 vs 34.5 us at config 2); kept for the insert path.
     const int hpt = (H % 2 == 0) ? 2 : 1;        // heads per thread sharing one table read
-    const int tpb_t = vec ? tokens_per_block(H, half, N, hpt) : 0;
+    const int tpb_t = vec ? tokens_per_block(H, half, N, hpt, (int)sizeof(T), false) : 0;
     if (tpb_t > 0) {
-        size_t smem = (size_t)tpb_t * (half / 2) * sizeof(float4);
+        size_t smem = rope_tokens_smem(tpb_t, H, half, (int)sizeof(T), false);
         auto kern = hpt == 2 ? rope_tokens_kernel<T, false, 2> : rope_tokens_kernel<T, false, 1>;
         kern<<<(T_ + tpb_t - 1) / tpb_t, 256, smem, st>>>(
             (T*)k, (const T*)k, nullptr, T_, H, half, ts, hs, ts, hs, 0, 0, 1, nullptr, 0, nullptr, nullptr, 0, orig, tgt,
@@ -834,10 +853,10 @@ int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv
     if (pages == 0) return check_launch("page_insert (empty)");
     int threads = 0, cpr = 0, kt = 0;
     const int hpt = (g.num_heads % 2 == 0) ? 2 : 1;
-    const int tpb_i = (orig && vec) ? tokens_per_block(g.num_heads, g.head_dim / 2, N, hpt) : 0;
+    const int tpb_i = (orig && vec) ? tokens_per_block(g.num_heads, g.head_dim / 2, N, hpt, es, true) : 0;
     if (tpb_i > 0) {
         FreqTable ft = make_freqs(theta, g.head_dim / 2);
-        size_t smem = (size_t)tpb_i * (g.head_dim / 4) * sizeof(float4);
+        size_t smem = rope_tokens_smem(tpb_i, g.num_heads, g.head_dim / 2, es, true);
         auto kern = hpt == 2 ? rope_tokens_kernel<T, true, 2> : rope_tokens_kernel<T, true, 1>;
         kern<<<(T_ + tpb_i - 1) / tpb_i, 256, smem, st>>>(
             (T*)cache, (const T*)nk, (const T*)nv, T_, g.num_heads, g.head_dim / 2, sts, shs, g.token_stride,
