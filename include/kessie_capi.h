@@ -332,6 +332,63 @@ int kessie_lse_combine_v2(const float* partials, int num_splits, int64_t split_s
                           void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Additive fog bias of the vLLM attention path.  The reference computes it in
+ * _FogCache._compute_into (kessie_attention.py:114-139) and hands it to vLLM
+ * as attn_bias, which vLLM's attention ignores; here it is applied inside the
+ * attention kernels, added to the scaled scores:
+ *   fb = int(kv_len * (1.0 - fog_start))                      (per sequence)
+ *   bias(j) = -fog_alpha * (1 - j/fb)^2 for j < fb, else 0;
+ *   bias(j) = recall_boost where bit j of recall_bits is set (overrides).
+ * The value of every step is rounded to `dtype` as the reference's torch ops
+ * on a buffer of that dtype round it (KESSIE_DTYPE_F32 / BF16 / F16).
+ * A null kessie_fog_bias pointer, or fog_alpha <= 0 with no recall bits,
+ * means no bias. */
+typedef struct kessie_fog_bias {
+    float fog_alpha;
+    double fog_start;
+    float recall_boost;
+    const uint32_t* recall_bits;   /* device bitmap over key positions, nullable */
+    int recall_nbits;
+    int dtype;
+} kessie_fog_bias;
+
+/* The reference's bias buffer: out[j] = bias(j) for j < kv_len, in out_dtype
+ * (the (1, 1, 1, kv_len) tensor _FogCache.get_fog_bias returns). */
+int kessie_build_fog_bias_v2(void* out, int out_dtype, int kv_len, const kessie_fog_bias* bias,
+                             void* stream);
+
+/* kessie_paged_fog_prefill_ex_v2 with the additive fog bias on the scores
+ * instead of the V fog (the vLLM attention path): the bias of sequence b uses
+ * kv_len = kv_lens[b] and key positions j < kv_lens[b]. */
+int kessie_paged_fog_prefill_biased_v2(const void* q, int64_t q_stride_b, int64_t q_stride_t,
+                                       int64_t q_stride_h, const void* k_cache, const void* v_cache,
+                                       int64_t page_stride, int64_t token_stride, int64_t head_stride,
+                                       int num_pages, int page_size, const int32_t* block_table,
+                                       int64_t block_table_stride, const int32_t* kv_lens,
+                                       const int32_t* q_start, int window_size, int is_causal,
+                                       float sm_scale, int batch, int num_q_tokens, int num_q_heads,
+                                       int num_kv_heads, int head_dim, int dtype,
+                                       const kessie_fog_bias* bias, void* out, int64_t o_stride_b,
+                                       int64_t o_stride_t, int64_t o_stride_h, int max_kv_len,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* kessie_paged_fog_decode_v2 with the additive fog bias on the scores; the
+ * bias of sequence b uses kv_len = q_positions[b] + 1 (the query is the last
+ * token) and global key positions. */
+int kessie_paged_fog_decode_biased_v2(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                      const void* k_cache, const void* v_cache,
+                                      int64_t page_stride, int64_t token_stride,
+                                      int64_t head_stride, int num_pages, int page_size,
+                                      const int32_t* block_table, int64_t block_table_stride,
+                                      const int32_t* seq_lens, const int32_t* kv_pos_offset,
+                                      const int32_t* q_positions, const int32_t* clear_start,
+                                      float fog_alpha, const float* fog_weights, int window_size,
+                                      float sm_scale, int batch, int num_q_heads,
+                                      int num_kv_heads, int head_dim, int max_seq_len, int dtype,
+                                      const kessie_fog_bias* bias, void* out, float* out_partial,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Context-parallel decode over NVLink peer memory (no counterpart in the
  * reference, which has no multi-GPU attention path).  Each of the `world`
  * ranks (one GPU each, one node, world <= 8) holds a contiguous position

@@ -21,6 +21,12 @@ DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 DEV_BAD_PAGE_ID, DEV_WAIT_TIMEOUT, DEV_BAD_ARG = 0x1, 0x2, 0x4
 
 
+class KessieFogBias(ctypes.Structure):
+    """C layout of kessie_fog_bias (include/kessie_capi.h)."""
+    _fields_ = [("fog_alpha", ctypes.c_float), ("fog_start", ctypes.c_double), ("recall_boost", ctypes.c_float),
+                ("recall_bits", ctypes.c_void_p), ("recall_nbits", ctypes.c_int), ("dtype", ctypes.c_int)]
+
+
 class KessieLibraryError(RuntimeError):
     """The CUDA library is missing or could not be loaded."""
 
@@ -78,6 +84,14 @@ SIGNATURES = {
                                                c_int, c_float, c_int, c_int, c_int, c_int, c_int, c_int, P, c_int64,
                                                c_int64, c_int64, c_int, P, c_size_t, P]),
     "kessie_lse_combine_v2": (c_int, [P, c_int, c_int64, c_int, c_int, P, c_int, P, P]),
+    "kessie_build_fog_bias_v2": (c_int, [P, c_int, c_int, P, P]),
+    "kessie_paged_fog_decode_biased_v2": (c_int, [P, c_int64, c_int64, P, P, c_int64, c_int64, c_int64, c_int, c_int,
+                                                  I32P, c_int64, I32P, I32P, I32P, I32P, c_float, P, c_int, c_float,
+                                                  c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, c_size_t, P]),
+    "kessie_paged_fog_prefill_biased_v2": (c_int, [P, c_int64, c_int64, c_int64, P, P, c_int64, c_int64, c_int64,
+                                                   c_int, c_int, I32P, c_int64, I32P, I32P, c_int, c_int, c_float,
+                                                   c_int, c_int, c_int, c_int, c_int, c_int, P, P, c_int64, c_int64,
+                                                   c_int64, c_int, P, c_size_t, P]),
     "kessie_cp_exchange_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "kessie_cp_exchange_alloc": (c_int, [c_size_t, P, P]),
     "kessie_cp_exchange_open": (c_int, [P, P]),

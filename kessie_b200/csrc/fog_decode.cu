@@ -49,6 +49,7 @@
 //           per step, no collective library call.
 #include "common.cuh"
 #include "cp_layout.cuh"
+#include "fog_bias.cuh"
 #include "ptx.cuh"
 #include "tma_host.cuh"
 
@@ -91,12 +92,14 @@ struct DecodeParams {
     void* out;            // [B][Hq][D] q dtype, or null
     float* out_part;      // [B][Hq][D+2] (O/l, ln m, l), or null
     CpLink cp;            // cp.world > 0: push merged rows into every rank's exchange buffer
+    FogBias bias;         // additive fog bias on the scores (vLLM path), bias.on == 0: none
     int* status;
 };
 
 // Visible local key range of one sequence.
 struct SeqInfo {
     int k_lo, k_hi, off;  // keys [k_lo, k_hi) of the local shard; global position of key 0
+    int qp;               // query position (global); the sequence holds qp + 1 keys in total
     int ulo, n;           // first visible 16-token unit and the unit count (0: nothing visible)
 };
 
@@ -109,6 +112,7 @@ __device__ __forceinline__ SeqInfo seq_info(const DecodeParams& p, int b) {
     }
     s.off = p.kv_off ? p.kv_off[b] : 0;
     const int qp = p.q_pos ? p.q_pos[b] : s.off + n - 1;
+    s.qp = qp;
     s.k_hi = min(n, qp - s.off + 1);
     s.k_lo = p.window > 0 ? max(0, qp - p.window + 1 - s.off) : 0;
     if (s.k_hi > s.k_lo) {
@@ -496,6 +500,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
         }
         const int cs = (p.clear_start && p.fog_alpha > 0.f) ? p.clear_start[b] : INT_MIN;
         const bool has_fog = p.fog_w != nullptr || cs > 0;
+        const bool has_bias = p.bias.on != 0;
+        const int bias_fb = has_bias ? fog_bias_boundary(p.bias, sg.si.qp + 1) : 0;
 
         const int n_iter = (sg.nu + kNCW - 1) / kNCW;
         for (int it = 0; it < n_iter; ++it, ++itg) {
@@ -547,13 +553,18 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
                     wa = va ? fog_weight(p, cs, off + ja) : 0.f;
                     wb = vb ? fog_weight(p, cs, off + jb) : 0.f;
                 }
+                float ba = 0.f, bb2 = 0.f;   // additive bias, log2 units
+                if (has_bias) {
+                    ba = va ? fog_bias_at(p.bias, bias_fb, off + ja) * kLog2e : 0.f;
+                    bb2 = vb ? fog_bias_at(p.bias, bias_fb, off + jb) * kLog2e : 0.f;
+                }
                 uint32_t pb0[NT], pb1[NT];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    const float s00 = va ? sacc[nt][0] * p.scale_log2 : -INFINITY;
-                    const float s01 = va ? sacc[nt][1] * p.scale_log2 : -INFINITY;
-                    const float s10 = vb ? sacc[nt][2] * p.scale_log2 : -INFINITY;
-                    const float s11 = vb ? sacc[nt][3] * p.scale_log2 : -INFINITY;
+                    const float s00 = va ? fmaf(sacc[nt][0], p.scale_log2, ba) : -INFINITY;
+                    const float s01 = va ? fmaf(sacc[nt][1], p.scale_log2, ba) : -INFINITY;
+                    const float s10 = vb ? fmaf(sacc[nt][2], p.scale_log2, bb2) : -INFINITY;
+                    const float s11 = vb ? fmaf(sacc[nt][3], p.scale_log2, bb2) : -INFINITY;
                     float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
 #pragma unroll
                     for (int o = 4; o < 32; o <<= 1) {
@@ -954,13 +965,15 @@ extern "C" size_t kessie_paged_fog_decode_workspace_size(int batch, int num_q_he
     return make_plan(batch, num_q_heads, num_kv_heads, head_dim, max_seq_len).ws;
 }
 
-extern "C" int kessie_paged_fog_decode_ex_v2(
-    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache, const void* v_cache,
-    int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
-    const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens, const int32_t* kv_pos_offset,
-    const int32_t* q_positions, const int32_t* clear_start, float fog_alpha, const float* fog_weights,
-    int window_size, float sm_scale, int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_seq_len,
-    int dtype, void* out, float* out_partial, void* workspace, size_t workspace_bytes, int phases, void* stream) {
+namespace kessie {
+namespace {
+int decode_entry(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+                 int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
+                 const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens,
+                 const int32_t* kv_pos_offset, const int32_t* q_positions, const int32_t* clear_start, float fog_alpha,
+                 const float* fog_weights, int window_size, float sm_scale, int batch, int num_q_heads,
+                 int num_kv_heads, int head_dim, int max_seq_len, int dtype, const kessie_fog_bias* bias, void* out,
+                 float* out_partial, void* workspace, size_t workspace_bytes, int phases, void* stream) {
     if (phases < 1 || phases > 3) return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: phases %d", phases);
     DecodeParams p;
     Plan pl;
@@ -968,6 +981,8 @@ extern "C" int kessie_paged_fog_decode_ex_v2(
                             num_pages, page_size, block_table, block_table_stride, seq_lens, kv_pos_offset,
                             q_positions, clear_start, fog_alpha, fog_weights, window_size, sm_scale, batch,
                             num_q_heads, num_kv_heads, head_dim, max_seq_len, dtype, workspace, workspace_bytes);
+    if (rc) return rc;
+    rc = fog_bias_from_c(bias, &p.bias);
     if (rc) return rc;
     if (!out && !out_partial) return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: no output");
     if ((reinterpret_cast<uintptr_t>(out) & 7) || (reinterpret_cast<uintptr_t>(out_partial) & 7))
@@ -978,6 +993,35 @@ extern "C" int kessie_paged_fog_decode_ex_v2(
     p.cp.world = 0;
     return run_decode(p, k_cache, v_cache, page_stride, token_stride, head_stride, page_size, head_dim,
                       dtype == KESSIE_DTYPE_BF16, as_stream(stream));
+}
+}  // namespace
+}  // namespace kessie
+
+extern "C" int kessie_paged_fog_decode_ex_v2(
+    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+    int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
+    const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens, const int32_t* kv_pos_offset,
+    const int32_t* q_positions, const int32_t* clear_start, float fog_alpha, const float* fog_weights,
+    int window_size, float sm_scale, int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_seq_len,
+    int dtype, void* out, float* out_partial, void* workspace, size_t workspace_bytes, int phases, void* stream) {
+    return decode_entry(q, q_stride_b, q_stride_h, k_cache, v_cache, page_stride, token_stride, head_stride, num_pages,
+                        page_size, block_table, block_table_stride, seq_lens, kv_pos_offset, q_positions, clear_start,
+                        fog_alpha, fog_weights, window_size, sm_scale, batch, num_q_heads, num_kv_heads, head_dim,
+                        max_seq_len, dtype, nullptr, out, out_partial, workspace, workspace_bytes, phases, stream);
+}
+
+extern "C" int kessie_paged_fog_decode_biased_v2(
+    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+    int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
+    const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens, const int32_t* kv_pos_offset,
+    const int32_t* q_positions, const int32_t* clear_start, float fog_alpha, const float* fog_weights,
+    int window_size, float sm_scale, int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_seq_len,
+    int dtype, const kessie_fog_bias* bias, void* out, float* out_partial, void* workspace, size_t workspace_bytes,
+    void* stream) {
+    return decode_entry(q, q_stride_b, q_stride_h, k_cache, v_cache, page_stride, token_stride, head_stride, num_pages,
+                        page_size, block_table, block_table_stride, seq_lens, kv_pos_offset, q_positions, clear_start,
+                        fog_alpha, fog_weights, window_size, sm_scale, batch, num_q_heads, num_kv_heads, head_dim,
+                        max_seq_len, dtype, bias, out, out_partial, workspace, workspace_bytes, 3, stream);
 }
 
 extern "C" int kessie_paged_fog_decode_v2(

@@ -188,6 +188,8 @@ __global__ void __launch_bounds__(kPThreads, 1) fog_prefill_kernel(const __grid_
     const int cs = (p.clear_start || p.clear_start_const > 0) && p.fog_alpha > 0.f
                        ? (p.clear_start ? p.clear_start[b] : p.clear_start_const) : INT_MIN;
     const bool has_fog = p.fog_w != nullptr || cs > 0;
+    const bool has_bias = p.bias.on != 0;
+    const int bias_fb = has_bias ? fog_bias_boundary(p.bias, kv_len) : 0;
 
     const int mi = lane >> 3, rr = lane & 7;
     const int kkey = rr + 8 * (mi >> 1), kch = mi & 1;     // K (B operand, non-trans)
@@ -238,8 +240,9 @@ __global__ void __launch_bounds__(kPThreads, 1) fog_prefill_kernel(const __grid_
                     vA = vA && j <= posA && posA - j < p.window;
                     vB = vB && j <= posB && posB - j < p.window;
                 }
-                sc[n][e] = vA ? sc[n][e] * p.scale_log2 : -INFINITY;
-                sc[n][2 + e] = vB ? sc[n][2 + e] * p.scale_log2 : -INFINITY;
+                const float bj = (has_bias && j < kv_len) ? fog_bias_at(p.bias, bias_fb, j) * kLog2e : 0.f;
+                sc[n][e] = vA ? fmaf(sc[n][e], p.scale_log2, bj) : -INFINITY;
+                sc[n][2 + e] = vB ? fmaf(sc[n][2 + e], p.scale_log2, bj) : -INFINITY;
                 mxA = fmaxf(mxA, sc[n][e]);
                 mxB = fmaxf(mxB, sc[n][2 + e]);
             }
@@ -462,14 +465,16 @@ extern "C" size_t kessie_paged_fog_prefill_workspace_size(int batch, int num_kv_
     return 2 * (size_t)batch * num_kv_heads * kv_max * head_dim * 2 + 256;
 }
 
-extern "C" int kessie_paged_fog_prefill_ex_v2(
+namespace kessie {
+namespace {
+int prefill_entry(
     const void* q, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache, const void* v_cache,
     int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
     const int32_t* block_table, int64_t block_table_stride, const int32_t* kv_lens, const int32_t* q_start,
     const int32_t* clear_start, float fog_alpha, const float* fog_weights, int64_t fog_weights_stride_b,
     int window_size, int is_causal, float sm_scale, int batch, int num_q_tokens, int num_q_heads, int num_kv_heads,
-    int head_dim, int dtype, void* out, int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h, int max_kv_len,
-    void* workspace, size_t workspace_bytes, void* stream) {
+    int head_dim, int dtype, const kessie_fog_bias* bias, void* out, int64_t o_stride_b, int64_t o_stride_t,
+    int64_t o_stride_h, int max_kv_len, void* workspace, size_t workspace_bytes, void* stream) {
     if (dtype != KESSIE_DTYPE_BF16 && dtype != KESSIE_DTYPE_F16)
         return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_prefill_v2: dtype %d (f16/bf16 only)", dtype);
     if (head_dim != 64 && head_dim != 128)
@@ -494,6 +499,8 @@ extern "C" int kessie_paged_fog_prefill_ex_v2(
     p.B = batch; p.Hq = num_q_heads; p.Hkv = num_kv_heads; p.G = num_q_heads / num_kv_heads;
     p.upp = page_size / 16; p.num_pages = num_pages;
     p.status = device_status_ptr();
+    int brc = fog_bias_from_c(bias, &p.bias);
+    if (brc) return brc;
     const bool bf16 = dtype == KESSIE_DTYPE_BF16;
     cudaStream_t st = as_stream(stream);
     if (workspace && max_kv_len > 0 && head_dim % 8 == 0 && ((reinterpret_cast<uintptr_t>(workspace) & 15) == 0) &&
@@ -528,6 +535,37 @@ extern "C" int kessie_paged_fog_prefill_ex_v2(
     }
     return run_prefill(p, k_cache, v_cache, page_stride, token_stride, head_stride, num_pages, page_size, head_dim,
                        bf16, st);
+}
+}  // namespace
+}  // namespace kessie
+
+extern "C" int kessie_paged_fog_prefill_ex_v2(
+    const void* q, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+    int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
+    const int32_t* block_table, int64_t block_table_stride, const int32_t* kv_lens, const int32_t* q_start,
+    const int32_t* clear_start, float fog_alpha, const float* fog_weights, int64_t fog_weights_stride_b,
+    int window_size, int is_causal, float sm_scale, int batch, int num_q_tokens, int num_q_heads, int num_kv_heads,
+    int head_dim, int dtype, void* out, int64_t o_stride_b, int64_t o_stride_t, int64_t o_stride_h, int max_kv_len,
+    void* workspace, size_t workspace_bytes, void* stream) {
+    return prefill_entry(q, q_stride_b, q_stride_t, q_stride_h, k_cache, v_cache, page_stride, token_stride,
+                         head_stride, num_pages, page_size, block_table, block_table_stride, kv_lens, q_start,
+                         clear_start, fog_alpha, fog_weights, fog_weights_stride_b, window_size, is_causal, sm_scale,
+                         batch, num_q_tokens, num_q_heads, num_kv_heads, head_dim, dtype, nullptr, out, o_stride_b,
+                         o_stride_t, o_stride_h, max_kv_len, workspace, workspace_bytes, stream);
+}
+
+extern "C" int kessie_paged_fog_prefill_biased_v2(
+    const void* q, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache, const void* v_cache,
+    int64_t page_stride, int64_t token_stride, int64_t head_stride, int num_pages, int page_size,
+    const int32_t* block_table, int64_t block_table_stride, const int32_t* kv_lens, const int32_t* q_start,
+    int window_size, int is_causal, float sm_scale, int batch, int num_q_tokens, int num_q_heads, int num_kv_heads,
+    int head_dim, int dtype, const kessie_fog_bias* bias, void* out, int64_t o_stride_b, int64_t o_stride_t,
+    int64_t o_stride_h, int max_kv_len, void* workspace, size_t workspace_bytes, void* stream) {
+    return prefill_entry(q, q_stride_b, q_stride_t, q_stride_h, k_cache, v_cache, page_stride, token_stride,
+                         head_stride, num_pages, page_size, block_table, block_table_stride, kv_lens, q_start, nullptr,
+                         0.f, nullptr, 0, window_size, is_causal, sm_scale, batch, num_q_tokens, num_q_heads,
+                         num_kv_heads, head_dim, dtype, bias, out, o_stride_b, o_stride_t, o_stride_h, max_kv_len,
+                         workspace, workspace_bytes, stream);
 }
 
 extern "C" int kessie_paged_fog_prefill_v2(

@@ -44,6 +44,7 @@ static_assert(256 * kSoftmaxRegs + 128 * kProducerRegs <= kThreads * kLaunchRegs
 constexpr int kRowsPerCta = 256;       // two 128-row Q tiles (A, B)
 constexpr uint32_t kTmemCols = 512;    // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
 constexpr float kRescaleThreshold = 8.0f;    // log2 units
+constexpr float kLog2eTc = 1.4426950408889634f;
 
 struct L {
     static constexpr int kHalf = 128 * 128;         // [128 rows][64 el] x 2 B
@@ -52,7 +53,8 @@ struct L {
     static constexpr int kK = kQ + 2 * kTile;
     static constexpr int kV = kK + kNK * kTile;
     static constexpr int kW = kV + kNV * kTile;     // per softmax warp: fog weights of the tile's 128 keys
-    static constexpr int kBar = kW + 8 * 128 * 4;
+    static constexpr int kB = kW + 8 * 128 * 4;     // per softmax warp: additive bias / sm_scale of those keys
+    static constexpr int kBar = kB + 8 * 128 * 4;
     // q_full, k_full[NK], k_empty[NK], v_full[NV], v_empty[NV], s_full[2], p_full[2], o_bar[2]
     static constexpr int kNumBar = 1 + 2 * kNK + 2 * kNV + 6;
     static constexpr int kSlot = kBar + kNumBar * 8;
@@ -313,6 +315,12 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
         float* wbuf = reinterpret_cast<float*>(smem + L::kW) + warp * 128;
+        float* bbuf = reinterpret_cast<float*>(smem + L::kB) + warp * 128;
+        const bool has_bias = p.bias.on != 0;
+        const int bias_fb = has_bias ? fog_bias_boundary(p.bias, kv_len) : 0;
+        // the bias enters as raw-score units (bias / sm_scale) so the exponent
+        // s * scale * log2e below adds exactly bias * log2e
+        const float bias_to_raw = has_bias ? kLog2eTc / p.scale_log2 : 0.f;
         const float inv_den = 1.f / (float)max(cs - 1, 1);
         for (int j = 0; j < n_tiles; ++j) {
             const int key0 = (tile_lo + j) * 128;
@@ -333,6 +341,16 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 }
                 reinterpret_cast<float4*>(wbuf)[lane] = w4v;
             }
+            if (has_bias) {
+                float4 b4v;
+                float* bq = &b4v.x;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int key = key0 + lane * 4 + e;
+                    bq[e] = key < kv_len ? fog_bias_at(p.bias, bias_fb, key) * bias_to_raw : 0.f;
+                }
+                reinterpret_cast<float4*>(bbuf)[lane] = b4v;
+            }
             __syncwarp();
             if (!ptx::mbar_wait(&s_full[x], (uint32_t)j & 1u)) { ok = false; break; }
             ptx::tc_fence_after();
@@ -340,7 +358,8 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
 #pragma unroll
             for (int c = 0; c < 4; ++c) ptx::tmem_ld32(sreg + c * 32, sv[c]);
             ptx::tmem_ld_wait();
-            const bool interior = key0 + 128 <= kv_len && (!(p.causal || p.window > 0) || key0 + 127 <= xpos_lo) &&
+            const bool interior = !has_bias && key0 + 128 <= kv_len &&
+                                  (!(p.causal || p.window > 0) || key0 + 127 <= xpos_lo) &&
                                   (p.window <= 0 || key0 >= xpos_hi - p.window + 1);
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             if (interior && valid_row) {
@@ -354,7 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const int key = key0 + c * 32 + i;
-                        const float sx = (key >= lo_r && key < hi_r) ? __uint_as_float(sv[c][i]) : -INFINITY;
+                        const float sb = has_bias ? bbuf[c * 32 + i] : 0.f;
+                        const float sx = (key >= lo_r && key < hi_r) ? __uint_as_float(sv[c][i]) + sb : -INFINITY;
                         sv[c][i] = __float_as_uint(sx);
                         mx4[i & 3] = fmaxf(mx4[i & 3], sx);
                     }

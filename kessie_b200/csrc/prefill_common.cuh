@@ -2,6 +2,8 @@
 // (warp-level mma.sync in fog_prefill.cu, tcgen05/TMEM in fog_prefill_tc.cu).
 #pragma once
 
+#include "fog_bias.cuh"
+
 #include <cuda.h>
 #include <stdint.h>
 
@@ -20,6 +22,7 @@ struct PrefillParams {
     const float* fog_w; int64_t fog_w_sb;
     float scale_log2;
     int B, Hq, Hkv, G, upp, num_pages;
+    FogBias bias;          // additive fog bias on the scores (vLLM path), bias.on == 0: none
     int* status;
 };
 

@@ -11,6 +11,7 @@ strides so both the KeSSie layout [P, ps, 2, H, D]
 
 from __future__ import annotations
 
+import ctypes
 import math
 import threading
 from typing import Optional, Tuple
@@ -199,6 +200,48 @@ def page_gather(kv: torch.Tensor, page_ids, layout: str = "kessie", out_keys=Non
     return out_keys, out_values
 
 
+# --------------------------------------------------------------------- additive fog bias
+class FogBias:
+    """Additive fog bias of the vLLM attention path (kessie_attention.py:114-139),
+    applied inside the attention kernels: per sequence of kv_len keys,
+    fb = int(kv_len * (1 - fog_start)); bias(j) = -fog_alpha * (1 - j/fb)^2
+    for j < fb, 0 after, recall_boost at recalled positions.  ``dtype`` is the
+    dtype whose rounding the bias follows (the reference builds it in the
+    query dtype).  Holds the device bitmap of the recalled positions."""
+
+    def __init__(self, fog_alpha: float = 0.5, fog_start: float = 0.5, recall_positions=(),
+                 recall_boost: float = 0.1, dtype=torch.bfloat16, device=None):
+        import numpy as np
+        self.fog_alpha, self.fog_start, self.recall_boost = float(fog_alpha), float(fog_start), float(recall_boost)
+        self.dtype = dtype
+        pos = np.asarray(sorted(int(x) for x in recall_positions if int(x) >= 0), dtype=np.int64)
+        self.recall_nbits = int(pos[-1]) + 1 if pos.size else 0
+        self.bits = None
+        if pos.size:
+            words = np.zeros((self.recall_nbits + 31) // 32, dtype=np.uint32)
+            np.bitwise_or.at(words, pos >> 5, (np.uint32(1) << (pos & 31).astype(np.uint32)))
+            dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+            self.bits = torch.from_numpy(words.view(np.int32)).to(dev)
+
+    def c_struct(self):
+        return _lib.KessieFogBias(self.fog_alpha, self.fog_start, self.recall_boost, _p(self.bits),
+                                  self.recall_nbits, _DT[self.dtype])
+
+
+def build_fog_bias(kv_len: int, bias: "FogBias", out: Optional[torch.Tensor] = None, device=None,
+                   stream=None) -> torch.Tensor:
+    """The reference's bias buffer (1, 1, 1, kv_len) in bias.dtype."""
+    dev = torch.device(device) if device is not None else (bias.bits.device if bias.bits is not None
+                                                           else torch.device("cuda", torch.cuda.current_device()))
+    if out is None:
+        out = torch.empty(kv_len, dtype=bias.dtype, device=dev)
+    _need_cuda(out)
+    cs = bias.c_struct()
+    _lib.check(_lib.load().kessie_build_fog_bias_v2(out.data_ptr(), dtype_code(out), int(kv_len), ctypes.byref(cs),
+                                                    _stream(stream)), "build_fog_bias")
+    return out.view(1, 1, 1, kv_len)
+
+
 # --------------------------------------------------------------------- decode
 def decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, max_seq_len, page_size=16) -> int:
     return int(_lib.load().kessie_paged_fog_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim,
@@ -253,7 +296,7 @@ def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                      window_size: int = 0, sm_scale: Optional[float] = None, kv_pos_offset=None,
                      q_positions=None, max_seq_len: Optional[int] = None, out: Optional[torch.Tensor] = None,
                      out_partial: Optional[torch.Tensor] = None, want_out: bool = True, stream=None,
-                     ws: Optional[torch.Tensor] = None, phases: int = 3):
+                     ws: Optional[torch.Tensor] = None, phases: int = 3, bias: Optional["FogBias"] = None):
     """Paged fog decode: q [B, Hq, D]; k_cache / v_cache [P, ps, Hkv, D]
     views (any page/token/head strides, D contiguous); block_table [B, maxP]
     int32; seq_lens [B] int32.  Returns out [B, Hq, D] (q.dtype) and, if
@@ -264,6 +307,12 @@ def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         out = torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
     lib, args, ws, keep = _decode_args(q, k_cache, v_cache, block_table, seq_lens, clear_start, fog_alpha,
                                        fog_weights, window_size, sm_scale, kv_pos_offset, q_positions, max_seq_len, ws)
+    if bias is not None:
+        cs = bias.c_struct()
+        _lib.check(lib.kessie_paged_fog_decode_biased_v2(*args, ctypes.byref(cs), _p(out if want_out else None),
+                                                         _p(out_partial), ws.data_ptr(), ws.numel(), _stream(stream)),
+                   "paged_fog_decode")
+        return out
     _lib.check(lib.kessie_paged_fog_decode_ex_v2(*args, _p(out if want_out else None), _p(out_partial), ws.data_ptr(),
                                                  ws.numel(), int(phases), _stream(stream)), "paged_fog_decode")
     return out
@@ -426,7 +475,7 @@ def paged_fog_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
                       kv_lens, q_start=None, clear_start=None, fog_alpha: float = 0.5, fog_weights=None,
                       window_size: int = 0, causal: bool = True, sm_scale: Optional[float] = None,
                       out: Optional[torch.Tensor] = None, stream=None, staged: bool = True,
-                      max_kv_len: Optional[int] = None) -> torch.Tensor:
+                      max_kv_len: Optional[int] = None, bias: Optional["FogBias"] = None) -> torch.Tensor:
     """Chunked prefill: q [B, T, Hq, D] (query t of sequence b at position
     q_start[b] + t, default kv_lens[b] - T) over k_cache / v_cache
     [P, ps, Hkv, D] views through block_table [B, maxP].  With staged=True the
@@ -464,6 +513,15 @@ def paged_fog_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
         ws_n = lib.kessie_paged_fog_prefill_workspace_size(B, Hkv, D, mkv)
         ws = workspace(ws_n, q.device, "prefill_stage")
         ws_ptr, ws_n = ws.data_ptr(), ws.numel()
+    if bias is not None:
+        cb = bias.c_struct()
+        _lib.check(lib.kessie_paged_fog_prefill_biased_v2(
+            q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), kl.data_ptr(),
+            _p(qs), int(window_size), 1 if causal else 0, float(sm_scale), B, T, Hq, Hkv, D, dtype_code(q),
+            ctypes.byref(cb), out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), mkv, ws_ptr, ws_n,
+            _stream(stream)), "paged_fog_prefill")
+        return out
     _lib.check(lib.kessie_paged_fog_prefill_ex_v2(
         q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k_cache.data_ptr(), v_cache.data_ptr(),
         k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), kl.data_ptr(),

@@ -53,6 +53,38 @@ def round_f16(x: np.ndarray) -> np.ndarray:
 
 
 # ---------------------------------------------------------------------------
+# Additive fog bias of the vLLM path -- kessie_attention.py:114-139
+# (_FogCache._compute_into)
+# ---------------------------------------------------------------------------
+
+_ROUND = {"float32": lambda x: np.asarray(x, dtype=np.float32), "bfloat16": round_bf16, "float16": round_f16}
+
+
+def fog_bias_values(kv_len: int, fog_alpha: float, fog_start: float, recall_positions=(),
+                    recall_boost: float = 0.1, dtype: str = "float32") -> np.ndarray:
+    """The reference's bias buffer of kv_len entries: -fog_alpha * (1 - j/fb)^2
+    for j < fb = int(kv_len * (1 - fog_start)), 0 after, recall_boost at the
+    recalled positions; every torch op of the reference (arange, divide,
+    rsub, square, scale) rounded to `dtype` like its buffer, the arange
+    element by element (as on the GPU the reference runs it on).  fp32 values."""
+    rnd = _ROUND[dtype]
+    out = np.zeros(kv_len, dtype=np.float32)
+    fb = int(kv_len * (1.0 - fog_start))
+    if fb > 0:
+        with np.errstate(over="ignore", invalid="ignore"):     # fp16 positions above 65504 are inf
+            pos = rnd(np.arange(fb, dtype=np.float32))
+            t = rnd(pos / np.float32(fb))
+            d = rnd(np.float32(1.0) - t)
+            d = rnd(d * d)
+            out[:fb] = rnd(d * np.float32(-fog_alpha))
+    boost = np.asarray(rnd(np.array([recall_boost], dtype=np.float32)), dtype=np.float32)[0]
+    for p in recall_positions:
+        if 0 <= p < kv_len:
+            out[p] = boost
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Fog weights -- kessie_hip_kernels.py:403-413 (kessie_build_fog_weights)
 # ---------------------------------------------------------------------------
 
@@ -134,7 +166,7 @@ def fused_fog_attention(q, k, v, fog_weights, window_size: int = 0, causal: bool
 
 def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal: bool = True,
                        sm_scale: Optional[float] = None, k_pos=None,
-                       return_partials: bool = False, dtype=np.float64):
+                       return_partials: bool = False, dtype=np.float64, score_bias=None):
     """Query-offset, GQA restatement of kessie_hip_kernels.py:577-593.
 
     q: [Hq, Nq, D] at absolute positions q_pos[Nq]; k, v: [Hkv, N, D] at
@@ -147,7 +179,9 @@ def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal:
     A row with no visible key (N == 0, or every key masked) is 0 with
     m = -inf, l = 0: the reference's softmax of an all-masked row is NaN, so
     this build defines the empty row as the neutral element of the merge
-    (a context-parallel shard may hold none of a sequence's window)."""
+    (a context-parallel shard may hold none of a sequence's window).
+    score_bias: optional [N] added to the scaled scores (the vLLM path's
+    additive fog bias, kessie_attention.py:114-139)."""
     q = np.asarray(q, dtype=dtype)
     k = np.asarray(k, dtype=dtype)
     v = np.asarray(v, dtype=dtype)
@@ -165,6 +199,8 @@ def fog_attention_rows(q, k, v, q_pos, fog_w=None, window_size: int = 0, causal:
     for h in range(Hq):
         kh = h // g
         s = (q[h] @ k[kh].T) * dtype(sm_scale)
+        if score_bias is not None:
+            s = s + np.asarray(score_bias, dtype=dtype)[None, :]
         s = np.where(ok, s, dtype(-np.inf))
         m = s.max(axis=-1, keepdims=True, initial=-np.inf)
         mf = np.where(np.isfinite(m), m, 0.0)
@@ -385,7 +421,7 @@ def _gather_seq(pages: np.ndarray, block_row: np.ndarray, n: int, page_size: int
 
 def paged_fog_decode(q, k_pages, v_pages, block_table, seq_lens, clear_start, fog_alpha,
                      window_size=0, sm_scale=None, kv_pos_offset=None, q_pos=None,
-                     fog_weights=None, return_partials=False):
+                     fog_weights=None, return_partials=False, bias_spec=None):
     """Decode restatement over a paged cache.
 
     q: [B, Hq, D]; k_pages/v_pages: [P, ps, Hkv, D] (values); block_table:
@@ -393,7 +429,9 @@ def paged_fog_decode(q, k_pages, v_pages, block_table, seq_lens, clear_start, fo
     local key 0 (context-parallel shards, default 0); q_pos[b] query
     position (default offset+len-1); clear_start[b] in global positions.
     Fog weight of key at global position j: kessie_hip_kernels.py:411-412
-    with clear_start[b] (or fog_weights[j] when given)."""
+    with clear_start[b] (or fog_weights[j] when given).  bias_spec =
+    (fog_alpha, fog_start, recall_positions, recall_boost, dtype) adds the
+    vLLM path's fog bias of a qp+1-key sequence to the scores."""
     B, Hq, D = q.shape
     ps = k_pages.shape[1]
     out = np.zeros((B, Hq, D))
@@ -410,9 +448,12 @@ def paged_fog_decode(q, k_pages, v_pages, block_table, seq_lens, clear_start, fo
             w = fog_weights_from_clear_start(off + n, cs, fog_alpha)[off:off + n]
         kk = _gather_seq(k_pages, block_table[b], n, ps)
         vv = _gather_seq(v_pages, block_table[b], n, ps)
+        sb = None
+        if bias_spec is not None:
+            sb = fog_bias_values(qp + 1, *bias_spec)[kpos] if n else np.zeros(0, np.float32)
         o, (m, l, ou) = fog_attention_rows(q[b][:, None, :], kk, vv, np.array([qp]), w,
                                            window_size, True, sm_scale, k_pos=kpos,
-                                           return_partials=True)
+                                           return_partials=True, score_bias=sb)
         out[b] = o[:, 0]
         parts.append((m[:, 0], l[:, 0], ou[:, 0]))
     if return_partials:
@@ -423,10 +464,11 @@ def paged_fog_decode(q, k_pages, v_pages, block_table, seq_lens, clear_start, fo
 
 
 def paged_fog_prefill(q, k_pages, v_pages, block_table, kv_len, q_start, clear_start, fog_alpha,
-                      window_size=0, sm_scale=None, fog_weights=None):
+                      window_size=0, sm_scale=None, fog_weights=None, bias_spec=None):
     """Chunked-prefill restatement: q [Hq, Nq, D] are the queries at absolute
     positions q_start..q_start+Nq-1 attending causally (plus optional window)
-    over kv_len paged keys; one sequence."""
+    over kv_len paged keys; one sequence.  bias_spec as in paged_fog_decode
+    (the bias of a kv_len-key sequence; no V fog is applied with it)."""
     ps = k_pages.shape[1]
     n = int(kv_len)
     Nq = q.shape[1]
@@ -436,4 +478,5 @@ def paged_fog_prefill(q, k_pages, v_pages, block_table, kv_len, q_start, clear_s
         w = fog_weights_from_clear_start(n, clear_start, fog_alpha)
     kk = _gather_seq(k_pages, block_table, n, ps)
     vv = _gather_seq(v_pages, block_table, n, ps)
-    return fog_attention_rows(q, kk, vv, q_start + np.arange(Nq), w, window_size, True, sm_scale)
+    sb = fog_bias_values(n, *bias_spec) if bias_spec is not None else None
+    return fog_attention_rows(q, kk, vv, q_start + np.arange(Nq), w, window_size, True, sm_scale, score_bias=sb)

@@ -223,6 +223,33 @@ def gen_kv_store():
     print("wrote kv_store.json", len(log), "steps")
 
 
+FOG_BIAS_CASES = [  # (kv_len, fog_alpha, fog_start, recall positions, recall_boost)
+    (128, 0.5, 0.5, [], 0.1),
+    (128, 0.5, 0.5, [10, 50, 100], 0.1),
+    (256, 0.8, 0.3, [5], 0.1),
+    (4096, 0.5, 0.5, [100, 200, 300], 0.1),
+    (131072, 0.5, 0.03125, [1000, 70000, 130000], 0.25),
+    (1000, 0.0, 0.5, [3], 0.1),
+    (777, 1.3, 0.9, [0, 776, 800], 0.5),
+    (50000, 0.5, 0.5, [], 0.1),
+]
+
+
+def gen_fog_bias():
+    """_FogCache._compute_into (kessie_attention.py:114-139): the additive fog
+    bias of the vLLM path, in buffers of each dtype."""
+    import kessie_attention as A
+    A._torch = torch
+    out = {}
+    for ci, (n, alpha, fs, rec, boost) in enumerate(FOG_BIAS_CASES):
+        for dn in ("float32", "bfloat16", "float16"):
+            buf = torch.zeros(n + 7, dtype=getattr(torch, dn))
+            A._FogCache._compute_into(buf, n, alpha, fs, set(rec), boost)
+            out[f"case{ci}_{dn}"] = buf[:n].float().numpy()
+    out["cases"] = np.array(repr(FOG_BIAS_CASES))
+    save("fog_bias.npz", **out)
+
+
 if __name__ == "__main__":
     gen_fog()
     gen_rope()
@@ -230,3 +257,4 @@ if __name__ == "__main__":
     gen_config1()
     gen_paged()
     gen_kv_store()
+    gen_fog_bias()

@@ -180,3 +180,34 @@ def test_group_decode_fp32_equals_rows():
     a = O.fog_decode_group_fp32(q, k, v, w)
     b = O.fog_attention_rows(q[:, None], k[None], v[None], np.array([2999]), w)[:, 0]
     np.testing.assert_allclose(a, b, atol=1e-5)
+
+
+def test_fog_bias_values_match_reference_buffers(golden_dir):
+    """The additive fog bias (kessie_attention.py:114-139) against the
+    reference's torch buffers.  fp32: bit for bit.  bf16 / fp16: the golden
+    ran torch's CPU arange, which for reduced types rounds each vector chunk's
+    base and adds the offsets in the reduced type (4113 -> 4096 in bf16); the
+    reference runs this buffer on the query's device, whose arange rounds every
+    element (4113 -> 4128), and that is the definition followed here.  Where
+    the two aranges differ the bias differs by at most one ulp of the dtype at
+    the bias magnitude; elsewhere it is bit for bit."""
+    import ast
+    d = np.load(os.path.join(golden_dir, "fog_bias.npz"))
+    cases = ast.literal_eval(str(d["cases"]))
+    ulp = {"bfloat16": 2.0 ** -8, "float16": 2.0 ** -11}
+    for ci, (n, alpha, fs, rec, boost) in enumerate(cases):
+        for dn in ("float32", "bfloat16", "float16"):
+            with np.errstate(over="ignore", invalid="ignore"):
+                got = O.fog_bias_values(n, alpha, fs, rec, boost, dn)
+            want = d[f"case{ci}_{dn}"]
+            if dn == "float32":
+                np.testing.assert_array_equal(got, want, err_msg=f"case {ci} {dn}")
+                continue
+            same = (got == want) | (np.isinf(got) & np.isinf(want) & (np.sign(got) == np.sign(want)))
+            finite = np.isfinite(want) & np.isfinite(got)
+            diff = np.abs(got[finite] - want[finite])
+            assert diff.max(initial=0.0) <= ulp[dn], f"case {ci} {dn}: {diff.max()}"
+            assert (~same).mean() < 0.05, f"case {ci} {dn}: {(~same).mean()}"
+            # the two aranges agree below 256 (bf16) / 2048 (fp16): bit for bit there
+            k = min(n, 256 if dn == "bfloat16" else 2048)
+            np.testing.assert_array_equal(got[:k], want[:k], err_msg=f"case {ci} {dn} head")
