@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["kessie", "reference"], default="kessie")
     ap.add_argument("--workload", default="cp_decode_1m",
-                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "page_ops", "prefill", "prefill_small"])
+                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "page_ops", "prefill",
+                             "prefill_small", "vllm_fog_decode"])
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -460,14 +461,17 @@ def run_cp_decode(args):
             del kv, kc, vc, dec
             torch.cuda.empty_cache()
             sec = {}
-            for wl, st in (("decode_128k", 20), ("decode_cfg3", 20), ("page_ops", 50), ("prefill", 10)):
+            for wl, st in (("decode_128k", 20), ("decode_cfg3", 20), ("vllm_fog_decode", 20), ("page_ops", 50),
+                           ("prefill", 10)):
                 r = measure_aux(wl, st)
                 r.pop("workload", None)
                 sec[wl] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}
                 torch.cuda.empty_cache()
             line["secondary"] = sec
             line["secondary_note"] = ("other north_star configs, same process, CUDA-event timed: decode_128k/cfg3 = "
-                                      "config 3 (GB/s vs hbm peak), page_ops = config 2, prefill = config 4 (TFLOP/s)")
+                                      "config 3 (GB/s vs hbm peak), vllm_fog_decode = config 3 through the vLLM "
+                                      "attention mirror with the fog bias, page_ops = config 2, prefill = config 4 "
+                                      "(TFLOP/s)")
         print(json.dumps(line), flush=True)
     if world > 1:
         dec.close()                       # collective: barrier, then unmap / free the exchange buffers
@@ -539,6 +543,48 @@ def measure_aux(workload, steps, warmup=3):
         byts = int(sum(lens)) * Hkv * D * 4
         res.update(ms_per_step=ms, us_per_step=ms * 1e3, kv_bytes=byts, GBs=byts / ms / 1e6,
                    frac_of_hbm=byts / ms / 1e6 / hbm, total_tokens=int(sum(lens)))
+    elif args.workload == "vllm_fog_decode":
+        # Config-3 decode step through the vLLM attention mirror
+        # (KeSSieAttentionImpl.forward) with the fog bias and recall boosts on:
+        # vLLM cache layout [2, num_blocks, block_size, Hkv, D], flattened
+        # query [B, Hq, D]; the unbiased paged decode on the same data beside it.
+        from types import SimpleNamespace
+        from kessie_b200 import kessie_attention as KA
+        c = CFG3
+        B, Hq, Hkv, D, bs = c["batch"], c["q_heads"], c["kv_heads"], c["head_dim"], c["page"]
+        lens = np.random.default_rng(3).integers(c["lo"], c["hi"] + 1, B)
+        need = [(int(n) + bs - 1) // bs for n in lens]
+        nb = sum(need)
+        cache = torch.empty(2, nb, bs, Hkv, D, dtype=torch.bfloat16, device=dev)
+        cache.normal_().mul_(1 / math.sqrt(128))
+        perm = torch.randperm(nb, device=dev).to(torch.int32)
+        bt = torch.zeros(B, max(need), dtype=torch.int32, device=dev)
+        o = 0
+        for b, k in enumerate(need):
+            bt[b, :k] = perm[o:o + k]; o += k
+        sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+        q = (torch.randn(B, Hq, D, device=dev) / math.sqrt(128)).to(torch.bfloat16)
+        out = torch.empty(B, Hq * D, dtype=torch.bfloat16, device=dev)
+        md = SimpleNamespace(num_actual_tokens=B, max_query_len=1, seq_lens=sl, block_table=bt,
+                             query_start_loc=torch.arange(B + 1, dtype=torch.int32, device=dev))
+
+        class _Inner:       # the wrapped vLLM impl is not reached with the fog on
+            num_heads, num_kv_heads, head_size, scale = Hq, Hkv, D, D ** -0.5
+            sliding_window, alibi_slopes, sinks, logits_soft_cap = (-1, -1), None, None, None
+
+        impl = KA.KeSSieAttentionImpl(_inner_impl=_Inner())
+        KA.KESSIE_STATE.update(fog_alpha=0.5, fog_start=1.0 - 4096 / 131072, prompt_len=int(lens.max()),
+                               recall_positions=range(0, 60000, 997), recall_boost=0.1)
+        ms = timeit(lambda: impl.forward(None, q, q, q, cache, md, out), args.steps)
+        plain = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
+        ms_plain = timeit(lambda: ops.paged_fog_decode(q, cache[0], cache[1], bt, sl, fog_alpha=0.0, out=plain),
+                          args.steps)
+        KA.KESSIE_STATE.update(prompt_len=0)
+        byts = int(sum(lens)) * Hkv * D * 4
+        res.update(ms_per_step=ms, us_per_step=ms * 1e3, kv_bytes=byts, GBs=byts / ms / 1e6,
+                   frac_of_hbm=byts / ms / 1e6 / hbm, unbiased_kernel_ms=ms_plain,
+                   note="KeSSieAttentionImpl.forward decode step (fog bias + 61 recall positions) vs the unbiased "
+                        "paged decode on the same cache")
     elif args.workload == "page_ops":
         # Config 2 on L independent layer caches (each 8192 pages x 64 KB = 512 MB):
         # 25% of pages (pos = 16 * perm) evicted below 32768, gathered to staging,
