@@ -389,6 +389,22 @@ int kessie_paged_fog_decode_biased_v2(const void* q, int64_t q_stride_b, int64_t
                                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Conversation-index query: cosine similarity of one fp32 query [dim] against
+ * an fp32 index [num_rows, dim] (row-major, 16-byte aligned, dim % 4 == 0),
+ * as _kessie_index_query_kernel (kessie_hip_kernels.py:343-360):
+ *   sim_i = (q / sqrt(|q|^2 + 1e-8)) . (x_i / sqrt(|x_i|^2 + 1e-8))
+ * (normalize_rows = 0: the rows are already normalised, VectorIndex style,
+ * kessie_exp3.py:69-81, and only the query is normalised).  Optional outputs:
+ * sims [num_rows]; the top_k (<= 32) rows by similarity, descending, ties to
+ * the lower row index (top_idx -1 / top_scores -FLT_MAX past num_rows).
+ * workspace: kessie_index_query_workspace_size(num_rows, top_k) bytes. */
+size_t kessie_index_query_workspace_size(int num_rows, int top_k);
+int kessie_index_query_v2(const float* query, const float* index, int num_rows, int dim,
+                          int normalize_rows, float* sims, int top_k, int32_t* top_idx,
+                          float* top_scores, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* ---------------------------------------------------------------------------
  * Context-parallel decode over NVLink peer memory (no counterpart in the
  * reference, which has no multi-GPU attention path).  Each of the `world`
  * ranks (one GPU each, one node, world <= 8) holds a contiguous position

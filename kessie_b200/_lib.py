@@ -85,6 +85,8 @@ SIGNATURES = {
                                                c_int64, c_int64, c_int, P, c_size_t, P]),
     "kessie_lse_combine_v2": (c_int, [P, c_int, c_int64, c_int, c_int, P, c_int, P, P]),
     "kessie_build_fog_bias_v2": (c_int, [P, c_int, c_int, P, P]),
+    "kessie_index_query_workspace_size": (c_size_t, [c_int, c_int]),
+    "kessie_index_query_v2": (c_int, [P, P, c_int, c_int, c_int, P, c_int, P, P, P, c_size_t, P]),
     "kessie_paged_fog_decode_biased_v2": (c_int, [P, c_int64, c_int64, P, P, c_int64, c_int64, c_int64, c_int, c_int,
                                                   I32P, c_int64, I32P, I32P, I32P, I32P, c_float, P, c_int, c_float,
                                                   c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, c_size_t, P]),

@@ -249,3 +249,14 @@ def _rope_remap_ref(k_tensor, orig_positions, target_positions, rope_theta=10000
     k_tensor[:, :, :half_dim] = (k1 * cos_d - k2 * sin_d).to(k_tensor.dtype)
     k_tensor[:, :, half_dim:] = (k1 * sin_d + k2 * cos_d).to(k_tensor.dtype)
     return k_tensor
+
+
+def kessie_index_query(query_embed: torch.Tensor, index_embeds: torch.Tensor, top_k: int = 0):
+    """Cosine similarity between a query and every index embedding -- the
+    operation of the reference's _kessie_index_query_kernel
+    (kessie_hip_kernels.py:343-360), whose module docstring lists
+    kessie_index_query without defining it.  Returns sims [N]; with top_k > 0
+    also (top ids, top scores), descending, ties to the lower row index."""
+    ids, scores, sims = ops.index_query(query_embed.float(), index_embeds.float(), top_k=max(top_k, 1),
+                                        normalize_rows=True, return_sims=True)
+    return (sims, ids, scores) if top_k > 0 else sims

@@ -529,3 +529,37 @@ def paged_fog_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
         B, T, Hq, Hkv, D, dtype_code(q), out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), mkv, ws_ptr,
         ws_n, _stream(stream)), "paged_fog_prefill")
     return out
+
+
+# --------------------------------------------------------------------- conversation index
+def index_query(query: torch.Tensor, index: torch.Tensor, top_k: int = 5, normalize_rows: bool = True,
+                return_sims: bool = False, stream=None):
+    """Cosine similarity of query [dim] against index [N, dim] (fp32, CUDA):
+    (top ids int32 [k'], top scores fp32 [k'][, sims [N]]) with k' = min(top_k, N),
+    descending, ties to the lower row index (kessie_hip_kernels.py:343-360; with
+    normalize_rows=False the rows are taken as already normalised, as
+    VectorIndex keeps them, kessie_exp3.py:69-81)."""
+    _need_cuda(query, index)
+    if query.dtype != torch.float32 or index.dtype != torch.float32:
+        raise TypeError("index_query: fp32 query and index")
+    q = query.contiguous().view(-1)
+    x = index.contiguous()
+    N, dim = x.shape
+    if q.numel() != dim:
+        raise ValueError("query and index rows differ in length")
+    if top_k > 32:
+        raise ValueError("index_query: top_k <= 32")
+    sims = torch.empty(N, dtype=torch.float32, device=x.device) if return_sims else None
+    k = max(int(top_k), 0)
+    ids = torch.empty(max(k, 1), dtype=torch.int32, device=x.device)
+    scores = torch.empty(max(k, 1), dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ws = None
+    if k > 0:
+        ws = workspace(lib.kessie_index_query_workspace_size(N, k), x.device, "index_query")
+    _lib.check(lib.kessie_index_query_v2(q.data_ptr(), x.data_ptr(), N, dim, 1 if normalize_rows else 0, _p(sims), k,
+                                         ids.data_ptr() if k else None, scores.data_ptr() if k else None, _p(ws),
+                                         ws.numel() if ws is not None else 0, _stream(stream)), "index_query")
+    kk = min(k, N)
+    out = (ids[:kk], scores[:kk])
+    return out + (sims,) if return_sims else out

@@ -480,3 +480,31 @@ def paged_fog_prefill(q, k_pages, v_pages, block_table, kv_len, q_start, clear_s
     vv = _gather_seq(v_pages, block_table, n, ps)
     sb = fog_bias_values(n, *bias_spec) if bias_spec is not None else None
     return fog_attention_rows(q, kk, vv, q_start + np.arange(Nq), w, window_size, True, sm_scale, score_bias=sb)
+
+
+# ---------------------------------------------------------------------------
+# Conversation-index query -- kessie_hip_kernels.py:343-360 (the GPU kernel)
+# and VectorIndex (kessie_exp3.py:58-110, rows stored normalised)
+# ---------------------------------------------------------------------------
+
+def vector_index_rows(index: np.ndarray) -> np.ndarray:
+    """Rows normalised as VectorIndex.rebuild stores them (norm < 1e-8 -> 1)."""
+    mat = np.asarray(index, dtype=np.float32)
+    norms = np.linalg.norm(mat, axis=1, keepdims=True)
+    norms[norms < 1e-8] = 1.0
+    return mat / norms
+
+
+def index_query(query: np.ndarray, index: np.ndarray, normalize_rows: bool = True, top_k: int = 0):
+    """(sims, top ids, top scores) in float64.  The query is divided by
+    sqrt(|q|^2 + 1e-8); with normalize_rows each row by sqrt(|x|^2 + 1e-8)
+    (the GPU kernel), else the rows are taken as stored.  Top-k: descending
+    score, ties to the lower row index."""
+    q = np.asarray(query, dtype=np.float64)
+    x = np.asarray(index, dtype=np.float64)
+    qn = q / np.sqrt((q * q).sum() + 1e-8)
+    if normalize_rows:
+        x = x / np.sqrt((x * x).sum(axis=1, keepdims=True) + 1e-8)
+    sims = x @ qn
+    order = np.lexsort((np.arange(len(sims)), -sims))[:top_k]
+    return sims, order, sims[order]

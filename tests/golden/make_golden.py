@@ -250,6 +250,25 @@ def gen_fog_bias():
     save("fog_bias.npz", **out)
 
 
+def gen_index_query():
+    """VectorIndex.search (kessie_exp3.py:58-110, numpy path): top-k ids and
+    cosine scores over a seeded index (row 7 all zero: the norm guard)."""
+    import kessie_exp3 as E
+    n, dim, seed = 20000, 256, 77
+    mat = rnd(seed, (n, dim))
+    mat[7] = 0.0
+    vi = E.VectorIndex(dim=dim)
+    vi.rebuild([mat[i] for i in range(n)], list(range(n)))
+    out = {"cfg": np.array([n, dim, seed])}
+    for qi in range(3):
+        q = rnd(seed + 1 + qi, (dim,))
+        res = vi.search(q, top_k=10)
+        out[f"q{qi}_ids"] = np.array([r[0] for r in res], dtype=np.int64)
+        out[f"q{qi}_scores"] = np.array([r[1] for r in res], dtype=np.float64)
+    out["tiny_query_result_len"] = np.array(len(vi.search(np.full(dim, 1e-12, np.float32), top_k=10)))
+    save("index_query.npz", **out)
+
+
 if __name__ == "__main__":
     gen_fog()
     gen_rope()
@@ -258,3 +277,4 @@ if __name__ == "__main__":
     gen_paged()
     gen_kv_store()
     gen_fog_bias()
+    gen_index_query()

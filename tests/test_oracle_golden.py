@@ -211,3 +211,19 @@ def test_fog_bias_values_match_reference_buffers(golden_dir):
             # the two aranges agree below 256 (bf16) / 2048 (fp16): bit for bit there
             k = min(n, 256 if dn == "bfloat16" else 2048)
             np.testing.assert_array_equal(got[:k], want[:k], err_msg=f"case {ci} {dn} head")
+
+
+def test_index_query_matches_vector_index(golden_dir):
+    """Top-k ids and cosine scores of VectorIndex.search (kessie_exp3.py:58-110)
+    from the oracle over the VectorIndex-normalised rows."""
+    d = np.load(os.path.join(golden_dir, "index_query.npz"))
+    n, dim, seed = (int(x) for x in d["cfg"])
+    mat = np.random.default_rng(seed).standard_normal((n, dim), dtype=np.float32)
+    mat[7] = 0.0
+    rows = O.vector_index_rows(mat)
+    for qi in range(3):
+        q = np.random.default_rng(seed + 1 + qi).standard_normal((dim,), dtype=np.float32)
+        _, ids, scores = O.index_query(q, rows, normalize_rows=False, top_k=10)
+        np.testing.assert_array_equal(ids, d[f"q{qi}_ids"])
+        np.testing.assert_allclose(scores, d[f"q{qi}_scores"], rtol=1e-5, atol=1e-6)
+    assert int(d["tiny_query_result_len"]) == 0      # VectorIndex returns nothing for a ~zero query
