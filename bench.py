@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--impl", choices=["kessie", "reference"], default="kessie")
     ap.add_argument("--workload", default="cp_decode_1m",
                     choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "page_ops", "prefill",
-                             "prefill_small", "vllm_fog_decode"])
+                             "prefill_small", "vllm_fog_decode", "index_query"])
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -462,7 +462,7 @@ def run_cp_decode(args):
             torch.cuda.empty_cache()
             sec = {}
             for wl, st in (("decode_128k", 20), ("decode_cfg3", 20), ("vllm_fog_decode", 20), ("page_ops", 50),
-                           ("prefill", 10)):
+                           ("prefill", 10), ("index_query", 50)):
                 r = measure_aux(wl, st)
                 r.pop("workload", None)
                 sec[wl] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}
@@ -471,7 +471,7 @@ def run_cp_decode(args):
             line["secondary_note"] = ("other north_star configs, same process, CUDA-event timed: decode_128k/cfg3 = "
                                       "config 3 (GB/s vs hbm peak), vllm_fog_decode = config 3 through the vLLM "
                                       "attention mirror with the fog bias, page_ops = config 2, prefill = config 4 "
-                                      "(TFLOP/s)")
+                                      "(TFLOP/s), index_query = conversation-index top-5 (GB/s vs hbm peak)")
         print(json.dumps(line), flush=True)
     if world > 1:
         dec.close()                       # collective: barrier, then unmap / free the exchange buffers
@@ -500,21 +500,41 @@ def measure_aux(workload, steps, warmup=3):
     args = _A()
     args.workload, args.steps, args.warmup = workload, steps, warmup
 
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if workload == "page_ops" else None
+    flush = (torch.empty(256 << 20, dtype=torch.uint8, device=dev) if workload in ("page_ops", "index_query")
+             else None)
 
-    def timeit(fn, K):
+    def timeit(fn, K, cold=True):
         """Mean CUDA-event time of fn; for working sets below the L2 size a
-        256 MB write between iterations (outside the events) flushes L2."""
+        256 MB write between iterations (outside the events) flushes L2
+        unless cold is False, and a short device-side sleep after it keeps
+        the host's enqueue time of fn out of the events."""
         for _ in range(max(3, args.warmup)):
             fn()
         torch.cuda.synchronize()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
         for a, b in evs:
-            if flush is not None:
+            if flush is not None and cold:
                 flush.zero_()
+                torch.cuda._sleep(200000)
             a.record(); fn(); b.record()
         torch.cuda.synchronize()
         return sum(a.elapsed_time(b) for a, b in evs) / K
+
+    def timeit_b2b(fn, K):
+        """Mean device time of K back-to-back calls: a device-side sleep ahead
+        of the first event lets the host enqueue all K calls, so host-side
+        overhead of the Python wrapper is not in the events."""
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(int(K * 2e5))
+        a.record()
+        for _ in range(K):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / K
 
     if args.workload in ("decode_cfg3", "decode_128k", "decode_small"):
         c = CFG3
@@ -639,6 +659,26 @@ def measure_aux(workload, steps, warmup=3):
         ms_e = timeit(ev_step, args.steps)
         res.update(l2="one-launch timings: 256 MB flush before each; b2b: 8 layer caches back to back",
                    evicted=n, evict_plus_refill_us=ms_e * 1e3, hbm_peak=hbm, layers=L)
+    elif args.workload == "index_query":
+        # Conversation-index query (fp32 cosine similarity + top-5): the
+        # reference index shape (78,125 rows x 256, 80 MB: under L2, so timed
+        # cold after a 256 MB flush and warm without) and a 1M-row index
+        # (1 GB) for the HBM roofline.  Algorithmic bytes = rows * dim * 4.
+        dim = 256
+        for n in (78125, 1000000):
+            x = torch.randn(n, dim, device=dev)
+            q = torch.randn(dim, device=dev)
+            byts = n * dim * 4
+            tag = f"n{n}"
+            ms_cold = timeit(lambda: ops.index_query(q, x, top_k=5), args.steps)
+            ms_warm = timeit_b2b(lambda: ops.index_query(q, x, top_k=5), args.steps)
+            ms_sims = timeit(lambda: ops.index_query(q, x, top_k=5, return_sims=True), args.steps)
+            res.update({tag + "_topk_us": ms_cold * 1e3, tag + "_topk_GBs": byts / ms_cold / 1e6,
+                        tag + "_topk_frac": byts / ms_cold / 1e6 / hbm, tag + "_topk_warm_us": ms_warm * 1e3,
+                        tag + "_with_sims_us": ms_sims * 1e3})
+            del x
+        res.update(hbm_peak=hbm, note="top-5 over fp32 rows, normalize_rows=1; cold = 256 MB L2 flush before each "
+                                      "launch pair (query + merge); warm = back-to-back calls, index resident in L2 (n78125 only fits)")
     elif args.workload in ("prefill", "prefill_small"):
         Hq, Hkv, D, ps, T, Nk = 32, 8, 128, 16, 8192, 262144
         if args.workload == "prefill_small":        # profiling size: 256 MB of KV

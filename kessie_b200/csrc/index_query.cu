@@ -9,14 +9,21 @@
 //                                                          kessie_exp3.py:69-81)
 // top-k: the k largest sims, descending, ties to the lower row index.
 //
-// Design (B200, HBM-bound: N * dim * 4 bytes per query): one warp per row
-// (each lane reads 16-byte chunks of the row, four rows in flight per warp),
-// a warp-wide reduction gives the row's dot product and squared norm; every
-// warp keeps its running top-k in registers (lane s holds rank s) and inserts
-// each row with one ballot + shuffle; the CTA merges its warps' lists in
-// shared memory and writes one list per CTA; a one-CTA second launch merges
-// the CTA lists.
+// Design (B200, HBM-bound: N * dim * 4 bytes per query): eight lanes per
+// row, so one warp covers four rows per step and each lane has eight 16-byte
+// chunks of its row in flight at once (a whole 256-float row slice in one
+// load round); a three-step shuffle gives the row's dot product and squared
+// norm.  Every warp keeps its running top-k in registers (lane s holds rank s,
+// lanes >= k hold worse entries or sentinels) with the k-th entry as a
+// threshold: a ballot offers the four rows at once and only rows above the
+// threshold are inserted (ballot + shuffle-up), so once the list fills a step
+// costs one ballot.  Lists are combined with bitonic networks across the 32
+// lanes (sort 32 / merge two sorted 32-lists: five shuffle stages each): the
+// CTA folds its warps' lists as a tree and writes one list; a one-CTA second
+// launch takes the k best list heads, and only the k lists they head can hold
+// the global top-k, so at most k * k candidates go through the final tree.
 #include "common.cuh"
+#include "ptx.cuh"
 
 #include <float.h>
 
@@ -27,142 +34,227 @@ constexpr int kIqWarps = 8;
 constexpr int kIqThreads = kIqWarps * 32;
 constexpr int kIqMaxK = 32;
 constexpr int kIqMergeThreads = 1024;
+constexpr int kIqLanesPerRow = 8;
+constexpr int kIqRowsPerStep = 32 / kIqLanesPerRow;        // rows per warp step
+constexpr int kIqUnroll = 8;                               // 16-byte chunks in flight per lane
+constexpr int kIqMinBlocks = 4;                            // resident CTAs per SM
+constexpr unsigned kFull = 0xffffffffu;
 
-// (score, index) order: higher score first, lower index first on ties.
+// (score, index) order: higher score first, lower index first on ties.  A
+// strict total order, so the selected set and its order do not depend on the
+// order in which rows are offered; (-FLT_MAX, INT_MAX) is the empty sentinel.
 __device__ __forceinline__ bool iq_better(float a, int ia, float b, int ib) {
     return a > b || (a == b && ia < ib);
 }
 
-// Warp-register top-k: lane s < k holds rank s.  Inserts (v, iv) (warp-uniform).
-__device__ __forceinline__ void iq_insert(float& val, int& idx, int k, float v, int iv, int lane) {
-    const float last = __shfl_sync(0xffffffffu, val, k - 1);
-    const int last_i = __shfl_sync(0xffffffffu, idx, k - 1);
-    if (!iq_better(v, iv, last, last_i)) return;
-    // rank of the newcomer = number of entries better than it
-    const unsigned better = __ballot_sync(0xffffffffu, lane < k && iq_better(val, idx, v, iv));
-    const int pos = __popc(better);
-    const float up_v = __shfl_up_sync(0xffffffffu, val, 1);
-    const int up_i = __shfl_up_sync(0xffffffffu, idx, 1);
-    if (lane < k) {
-        if (lane > pos) { val = up_v; idx = up_i; }
-        else if (lane == pos) { val = v; idx = iv; }
+// Compare-exchange with lane ^ m: keep the better entry when keep_better.
+__device__ __forceinline__ void iq_cas(float& v, int& i, int m, bool keep_better) {
+    const float ov = __shfl_xor_sync(kFull, v, m);
+    const int oi = __shfl_xor_sync(kFull, i, m);
+    if (iq_better(ov, oi, v, i) == keep_better) { v = ov; i = oi; }
+}
+
+// Bitonic sort of one entry per lane, best first.
+__device__ __forceinline__ void iq_sort32(float& v, int& i, int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+        for (int m = size >> 1; m > 0; m >>= 1)
+            iq_cas(v, i, m, ((lane & m) == 0) == ((lane & size) == 0));
+}
+
+// (v, i) <- best 32 of two lists sorted best first, sorted best first.
+__device__ __forceinline__ void iq_merge32(float& v, int& i, float bv, int bi, int lane) {
+    const float rv = __shfl_sync(kFull, bv, 31 - lane);
+    const int ri = __shfl_sync(kFull, bi, 31 - lane);
+    if (iq_better(rv, ri, v, i)) { v = rv; i = ri; }      // bitonic: the best 32 of both
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) iq_cas(v, i, m, (lane & m) == 0);
+}
+
+// Tree fold of the sorted lists of warps [0, nact) into warp 0 (block-wide
+// call: every thread reaches the barriers; nact is block-uniform).
+__device__ __forceinline__ void iq_block_fold(float& v, int& i, float* s_v, int* s_i, int nact, int warp,
+                                              int lane) {
+    int span = 1;
+    while (span < nact) span <<= 1;
+    if (warp < nact) { s_v[warp * 32 + lane] = v; s_i[warp * 32 + lane] = i; }
+    for (int half = span >> 1; half >= 1; half >>= 1) {
+        __syncthreads();
+        if (warp < half && warp + half < nact) {
+            iq_merge32(v, i, s_v[(warp + half) * 32 + lane], s_i[(warp + half) * 32 + lane], lane);
+            s_v[warp * 32 + lane] = v;
+            s_i[warp * 32 + lane] = i;
+        }
     }
 }
 
-__device__ __forceinline__ float iq_warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
+// A warp's top-k list: lane s < k holds rank s; (tv, ti) is the k-th entry.
+struct IqList {
+    float val = -FLT_MAX, tv = -FLT_MAX;
+    int idx = INT_MAX, ti = INT_MAX;
+
+    // Offer one (v, iv) per lane where ok is set (warp-wide call).
+    __device__ __forceinline__ void offer(int k, float v, int iv, bool ok, int lane) {
+        unsigned m = __ballot_sync(kFull, ok && iq_better(v, iv, tv, ti));
+        while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const float cv = __shfl_sync(kFull, v, src);
+            const int ci = __shfl_sync(kFull, iv, src);
+            if (!iq_better(cv, ci, tv, ti)) continue;      // warp-uniform
+            const int pos = __popc(__ballot_sync(kFull, lane < k && iq_better(val, idx, cv, ci)));
+            const float up_v = __shfl_up_sync(kFull, val, 1);
+            const int up_i = __shfl_up_sync(kFull, idx, 1);
+            if (lane < k) {
+                if (lane > pos) { val = up_v; idx = up_i; }
+                else if (lane == pos) { val = cv; idx = ci; }
+            }
+            tv = __shfl_sync(kFull, val, k - 1);
+            ti = __shfl_sync(kFull, idx, k - 1);
+        }
+    }
+};
 
 // Pass 1: similarities (optional output) and one top-k list per CTA.
-__global__ void __launch_bounds__(kIqThreads) index_query_kernel(const float* __restrict__ query,
-                                                                 const float* __restrict__ index, int n, int dim,
-                                                                 int normalize_rows, float* __restrict__ sims,
-                                                                 int k, float* __restrict__ cand_val,
-                                                                 int* __restrict__ cand_idx) {
-    __shared__ float s_val[kIqWarps][kIqMaxK];
-    __shared__ int s_idx[kIqWarps][kIqMaxK];
+template <bool NORM>
+__global__ void __launch_bounds__(kIqThreads, kIqMinBlocks) index_query_kernel(
+    const float* __restrict__ query, const float* __restrict__ index, int n, int dim, float* __restrict__ sims, int k,
+    float* __restrict__ cand_val, int* __restrict__ cand_idx) {
+    __shared__ float s_val[kIqWarps * 32];
+    __shared__ int s_idx[kIqWarps * 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the merge launch (programmatic dependent launch) may be scheduled now:
+    // it waits for this grid's completion before reading the lists
+    ptx::launch_dependents();
     const int d4 = dim >> 2;                               // 16-byte chunks per row
-    // query norm (every warp computes it; dim is small)
+    const float4* q4 = reinterpret_cast<const float4*>(query);
     float qq = 0.f;
     for (int c = lane; c < d4; c += 32) {
-        const float4 x = __ldg(reinterpret_cast<const float4*>(query) + c);
+        const float4 x = __ldg(q4 + c);
         qq += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
     }
-    const float qinv = 1.f / sqrtf(iq_warp_sum(qq) + 1e-8f);
-    float val = -FLT_MAX;
-    int idx = INT_MAX;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) qq += __shfl_xor_sync(kFull, qq, o);
+    const float qinv = 1.f / sqrtf(qq + 1e-8f);
+    const int sub = lane % kIqLanesPerRow, rsub = lane / kIqLanesPerRow;
+    IqList list;
     const int gw = blockIdx.x * kIqWarps + warp, nw = gridDim.x * kIqWarps;
-    constexpr int R = 4;                                   // rows in flight per warp
-    for (int r0 = gw * R; r0 < n; r0 += nw * R) {
-        float dot[R], sq[R];
+    const int wstride = nw * kIqRowsPerStep;
+    for (long long r0 = (long long)gw * kIqRowsPerStep; r0 < n; r0 += wstride) {
+        const int r = (int)min(r0 + rsub, (long long)INT_MAX);
+        const bool live = r < n;
+        const float4* x4 = reinterpret_cast<const float4*>(index + (size_t)(live ? r : 0) * dim);
+        float dot = 0.f, sq = 0.f;
+        for (int c0 = sub; c0 < d4; c0 += kIqLanesPerRow * kIqUnroll) {
+            float4 x[kIqUnroll];
 #pragma unroll
-        for (int u = 0; u < R; ++u) { dot[u] = 0.f; sq[u] = 0.f; }
-        for (int c = lane; c < d4; c += 32) {
-            const float4 qv = __ldg(reinterpret_cast<const float4*>(query) + c);
-            float4 x[R];
-#pragma unroll
-            for (int u = 0; u < R; ++u) {
-                const int r = r0 + u;
-                x[u] = r < n ? ldg_stream_f4(index + (size_t)r * dim + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int u = 0; u < kIqUnroll; ++u) {
+                const int c = c0 + u * kIqLanesPerRow;
+                x[u] = (live && c < d4) ? ldg_stream_f4(reinterpret_cast<const float*>(x4 + c))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-            for (int u = 0; u < R; ++u) {
-                dot[u] += qv.x * x[u].x + qv.y * x[u].y + qv.z * x[u].z + qv.w * x[u].w;
-                sq[u] += x[u].x * x[u].x + x[u].y * x[u].y + x[u].z * x[u].z + x[u].w * x[u].w;
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < R; ++u) {
-            const int r = r0 + u;
-            const float dt = iq_warp_sum(dot[u]);
-            const float s2 = normalize_rows ? iq_warp_sum(sq[u]) : 0.f;
-            if (r < n) {
-                const float sim = normalize_rows ? dt * qinv * (1.f / sqrtf(s2 + 1e-8f)) : dt * qinv;
-                if (sims && lane == 0) sims[r] = sim;
-                if (k > 0) iq_insert(val, idx, k, sim, r, lane);
+            for (int u = 0; u < kIqUnroll; ++u) {
+                const int c = c0 + u * kIqLanesPerRow;
+                const float4 qv = c < d4 ? __ldg(q4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                dot += qv.x * x[u].x + qv.y * x[u].y + qv.z * x[u].z + qv.w * x[u].w;
+                if (NORM) sq += x[u].x * x[u].x + x[u].y * x[u].y + x[u].z * x[u].z + x[u].w * x[u].w;
             }
         }
+#pragma unroll
+        for (int o = 1; o < kIqLanesPerRow; o <<= 1) {
+            dot += __shfl_xor_sync(kFull, dot, o);
+            if (NORM) sq += __shfl_xor_sync(kFull, sq, o);
+        }
+        const float sim = NORM ? dot * qinv * (1.f / sqrtf(sq + 1e-8f)) : dot * qinv;
+        const bool lead = live && sub == 0;
+        if (sims && lead) sims[r] = sim;
+        if (k > 0) list.offer(k, sim, r, lead, lane);
     }
-    if (k <= 0) return;
-    if (lane < k) { s_val[warp][lane] = val; s_idx[warp][lane] = idx; }
-    __syncthreads();
-    if (warp == 0) {
-        for (int w = 1; w < kIqWarps; ++w)
-            for (int s = 0; s < k; ++s) {
-                const float v = s_val[w][s];
-                const int iv = s_idx[w][s];
-                if (iv != INT_MAX) iq_insert(val, idx, k, v, iv, lane);
-            }
-        if (lane < k) {
-            cand_val[(size_t)blockIdx.x * k + lane] = val;
-            cand_idx[(size_t)blockIdx.x * k + lane] = idx;
-        }
+    if (k <= 0) return;                                    // block-uniform
+    float v = list.val;
+    int i = list.idx;
+    iq_block_fold(v, i, s_val, s_idx, kIqWarps, warp, lane);
+    if (warp == 0 && lane < k) {
+        cand_val[(size_t)blockIdx.x * k + lane] = v;
+        cand_idx[(size_t)blockIdx.x * k + lane] = i;
     }
 }
 
-// Pass 2: merge ncand candidate lists of k (one CTA of 32 warps).
+// Pass 2: merge nlists sorted candidate lists of k (one CTA of 32 warps).
 __global__ void __launch_bounds__(kIqMergeThreads) index_merge_kernel(const float* __restrict__ cand_val,
                                                                       const int* __restrict__ cand_idx, int nlists,
                                                                       int k, float* __restrict__ top_val,
                                                                       int32_t* __restrict__ top_idx) {
     constexpr int W = kIqMergeThreads / 32;
-    __shared__ float s_val[W][kIqMaxK];
-    __shared__ int s_idx[W][kIqMaxK];
+    __shared__ float s_val[W * 32];
+    __shared__ int s_idx[W * 32];
+    __shared__ int s_sel[32];
+    __shared__ int s_nsel;
+    __shared__ float s_tv;
+    __shared__ int s_ti;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float val = -FLT_MAX;
-    int idx = INT_MAX;
-    const int total = nlists * k;
-    for (int base = warp * 32; base < total; base += W * 32) {
-        const int e = base + lane;
-        const float v = e < total ? cand_val[e] : -FLT_MAX;
-        const int iv = e < total ? cand_idx[e] : INT_MAX;
-        for (int j = 0; j < 32; ++j) {
-            const float vj = __shfl_sync(0xffffffffu, v, j);
-            const int ij = __shfl_sync(0xffffffffu, iv, j);
-            if (ij != INT_MAX) iq_insert(val, idx, k, vj, ij, lane);
+    ptx::grid_dependency_wait();                           // pass 1 complete, its lists visible
+    if (threadIdx.x == 0) s_nsel = 0;
+    // 1. the k best list heads (each list is sorted, best first)
+    float v = -FLT_MAX;
+    int i = INT_MAX;
+    for (int b = warp * 32; b < nlists; b += kIqMergeThreads) {
+        const int l = b + lane;
+        float hv = -FLT_MAX;
+        int hi = INT_MAX;
+        if (l < nlists) { hv = cand_val[(size_t)l * k]; hi = cand_idx[(size_t)l * k]; }
+        iq_sort32(hv, hi, lane);
+        iq_merge32(v, i, hv, hi, lane);
+    }
+    const int nact = min(W, (nlists + 31) / 32);
+    iq_block_fold(v, i, s_val, s_idx, nact, warp, lane);
+    if (warp == 0) {
+        const float tv = __shfl_sync(kFull, v, k - 1);
+        const int ti = __shfl_sync(kFull, i, k - 1);
+        if (lane == 0) { s_tv = tv; s_ti = ti; }
+    }
+    __syncthreads();
+    // 2. the lists headed by those k heads hold every entry of the top-k
+    const float tv = s_tv;
+    const int ti = s_ti;
+    for (int l = threadIdx.x; l < nlists; l += kIqMergeThreads) {
+        const float hv = cand_val[(size_t)l * k];
+        const int hi = cand_idx[(size_t)l * k];
+        if (hi != INT_MAX && !iq_better(tv, ti, hv, hi)) {
+            const int slot = atomicAdd(&s_nsel, 1);
+            if (slot < 32) s_sel[slot] = l;
         }
     }
-    if (lane < k) { s_val[warp][lane] = val; s_idx[warp][lane] = idx; }
     __syncthreads();
-    if (warp == 0) {
-        for (int w = 1; w < W; ++w)
-            for (int s = 0; s < k; ++s)
-                if (s_idx[w][s] != INT_MAX) iq_insert(val, idx, k, s_val[w][s], s_idx[w][s], lane);
-        if (lane < k) {
-            top_val[lane] = idx == INT_MAX ? -FLT_MAX : val;
-            top_idx[lane] = idx == INT_MAX ? -1 : idx;
-        }
+    const int nsel = min(s_nsel, 32);
+    const int ncand = nsel * k;
+    v = -FLT_MAX;
+    i = INT_MAX;
+    if ((int)threadIdx.x < ncand) {
+        const size_t e = (size_t)s_sel[threadIdx.x / k] * k + threadIdx.x % k;
+        v = cand_val[e];
+        i = cand_idx[e];
+    }
+    const int nact2 = max(1, (ncand + 31) / 32);
+    if (warp < nact2) iq_sort32(v, i, lane);
+    iq_block_fold(v, i, s_val, s_idx, nact2, warp, lane);
+    if (warp == 0 && lane < k) {
+        top_val[lane] = i == INT_MAX ? -FLT_MAX : v;
+        top_idx[lane] = i == INT_MAX ? -1 : i;
     }
 }
 
+// One wave of resident CTAs at most, sized so that every warp gets the same
+// number of row steps (the last DRAM round then has every warp loading).
 int iq_grid(int n) {
-    const int per_cta = kIqWarps * 4;                      // rows per CTA per grid-stride step
-    int g = (n + per_cta - 1) / per_cta;
-    const int cap = sm_count() * 8;                        // 8 CTAs of 8 warps per SM
-    return g < 1 ? 1 : (g > cap ? cap : g);
+    const long long steps = ((long long)n + kIqRowsPerStep - 1) / kIqRowsPerStep;
+    const long long max_warps = (long long)sm_count() * kIqMinBlocks * kIqWarps;
+    const long long per_warp = (steps + max_warps - 1) / max_warps;
+    const long long warps = (steps + per_warp - 1) / per_warp;
+    const long long g = (warps + kIqWarps - 1) / kIqWarps;
+    return (int)(g < 1 ? 1 : g);
 }
 
 }  // namespace
@@ -178,8 +270,8 @@ extern "C" size_t kessie_index_query_workspace_size(int num_rows, int top_k) {
 extern "C" int kessie_index_query_v2(const float* query, const float* index, int num_rows, int dim,
                                      int normalize_rows, float* sims, int top_k, int32_t* top_idx, float* top_scores,
                                      void* workspace, size_t workspace_bytes, void* stream) {
-    if (!query || !index || num_rows <= 0 || dim <= 0 || dim % 4 || top_k < 0 || top_k > kIqMaxK)
-        return set_error(KESSIE_ERR_ARG, "index_query_v2: bad arguments (dim %% 4 == 0, 0 <= top_k <= %d)", kIqMaxK);
+    if (!query || !index || num_rows <= 0 || dim <= 0 || dim % 4 || dim > (1 << 24) || top_k < 0 || top_k > kIqMaxK)
+        return set_error(KESSIE_ERR_ARG, "index_query_v2: bad arguments (0 < dim <= 2^24, dim %% 4 == 0, 0 <= top_k <= %d)", kIqMaxK);
     if ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(index)) & 15)
         return set_error(KESSIE_ERR_ARG, "index_query_v2: query / index must be 16-byte aligned");
     if (top_k > 0 && (!top_idx || !top_scores))
@@ -196,10 +288,23 @@ extern "C" int kessie_index_query_v2(const float* query, const float* index, int
         ci = reinterpret_cast<int*>(cv + (size_t)grid * top_k);
     }
     cudaStream_t st = as_stream(stream);
-    index_query_kernel<<<grid, kIqThreads, 0, st>>>(query, index, num_rows, dim, normalize_rows ? 1 : 0, sims, top_k,
-                                                    cv, ci);
+    if (normalize_rows)
+        index_query_kernel<true><<<grid, kIqThreads, 0, st>>>(query, index, num_rows, dim, sims, top_k, cv, ci);
+    else
+        index_query_kernel<false><<<grid, kIqThreads, 0, st>>>(query, index, num_rows, dim, sims, top_k, cv, ci);
     int rc = check_launch("index_query");
     if (rc || top_k == 0) return rc;
-    index_merge_kernel<<<1, kIqMergeThreads, 0, st>>>(cv, ci, grid, top_k, top_scores, top_idx);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kIqMergeThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, index_merge_kernel, (const float*)cv, (const int*)ci, grid, top_k,
+                                             top_scores, top_idx);
+    if (e != cudaSuccess) return set_error(KESSIE_ERR_CUDA, "index_query merge: %s", cudaGetErrorString(e));
     return check_launch("index_query merge");
 }

@@ -239,6 +239,9 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 // Lets a kernel launched after this one with programmatic stream
 // serialization start once every CTA of this grid has issued it (or exited).
 __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Wait until the grids this one depends on (programmatic stream serialization)
+// have completed and their memory is visible; a no-op without that attribute.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ------------------------------------------------------------------ cross-GPU flags (plain peer loads/stores)
 // System-scope release store / acquire load of a 32-bit flag; the address may
