@@ -500,21 +500,22 @@ def measure_aux(workload, steps, warmup=3):
     args = _A()
     args.workload, args.steps, args.warmup = workload, steps, warmup
 
-    flush = (torch.empty(256 << 20, dtype=torch.uint8, device=dev) if workload in ("page_ops", "index_query")
+    flush = (torch.ones(256 << 20, dtype=torch.uint8, device=dev) if workload in ("page_ops", "index_query")
              else None)
 
     def timeit(fn, K, cold=True):
         """Mean CUDA-event time of fn; for working sets below the L2 size a
-        256 MB write between iterations (outside the events) flushes L2
-        unless cold is False, and a short device-side sleep after it keeps
-        the host's enqueue time of fn out of the events."""
+        256 MB read between iterations (outside the events) flushes L2
+        unless cold is False -- a read, so that L2 holds no dirty lines whose
+        write-back would land inside the events -- and a short device-side
+        sleep after it keeps the host's enqueue time of fn out of them."""
         for _ in range(max(3, args.warmup)):
             fn()
         torch.cuda.synchronize()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
         for a, b in evs:
             if flush is not None and cold:
-                flush.zero_()
+                flush.max()
                 torch.cuda._sleep(200000)
             a.record(); fn(); b.record()
         torch.cuda.synchronize()
@@ -657,7 +658,7 @@ def measure_aux(workload, steps, warmup=3):
             valid.fill_(1)
             ops.page_evict(valid, pos, 32768)
         ms_e = timeit(ev_step, args.steps)
-        res.update(l2="one-launch timings: 256 MB flush before each; b2b: 8 layer caches back to back",
+        res.update(l2="one-launch timings: 256 MB read (L2 flush) before each; b2b: 8 layer caches back to back",
                    evicted=n, evict_plus_refill_us=ms_e * 1e3, hbm_peak=hbm, layers=L)
     elif args.workload == "index_query":
         # Conversation-index query (fp32 cosine similarity + top-5): the
@@ -676,9 +677,28 @@ def measure_aux(workload, steps, warmup=3):
             res.update({tag + "_topk_us": ms_cold * 1e3, tag + "_topk_GBs": byts / ms_cold / 1e6,
                         tag + "_topk_frac": byts / ms_cold / 1e6 / hbm, tag + "_topk_warm_us": ms_warm * 1e3,
                         tag + "_with_sims_us": ms_sims * 1e3})
+            if n == 78125:
+                # end to end through the VectorIndex drop-in: host query in,
+                # (id, score) list out (query upload + result download inside)
+                import time
+                from kessie_b200.vector_index import VectorIndex
+                vi = VectorIndex(dim=dim)
+                xh = x.cpu().numpy()
+                vi.rebuild(list(xh), list(range(n)))
+                qh = q.cpu().numpy()
+                for _ in range(3):
+                    vi.search(qh, top_k=5)
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                for _ in range(args.steps):
+                    vi.search(qh, top_k=5)
+                res[tag + "_search_e2e_us"] = (time.perf_counter() - t0) / args.steps * 1e6
+                del vi, xh
             del x
-        res.update(hbm_peak=hbm, note="top-5 over fp32 rows, normalize_rows=1; cold = 256 MB L2 flush before each "
-                                      "launch pair (query + merge); warm = back-to-back calls, index resident in L2 (n78125 only fits)")
+        res.update(hbm_peak=hbm, note="top-5 over fp32 rows, normalize_rows=1; cold = 256 MB read (L2 flush) before each "
+                                      "launch pair (query + merge); warm = back-to-back calls, index resident in L2 (n78125 only fits); "
+                                      "search_e2e = VectorIndex.search wall time per call (host query in, host "
+                                      "results out)")
     elif args.workload in ("prefill", "prefill_small"):
         Hq, Hkv, D, ps, T, Nk = 32, 8, 128, 16, 8192, 262144
         if args.workload == "prefill_small":        # profiling size: 256 MB of KV

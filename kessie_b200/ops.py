@@ -533,12 +533,14 @@ def paged_fog_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
 
 # --------------------------------------------------------------------- conversation index
 def index_query(query: torch.Tensor, index: torch.Tensor, top_k: int = 5, normalize_rows: bool = True,
-                return_sims: bool = False, stream=None):
+                return_sims: bool = False, stream=None, out_ids: torch.Tensor = None, out_scores: torch.Tensor = None):
     """Cosine similarity of query [dim] against index [N, dim] (fp32, CUDA):
     (top ids int32 [k'], top scores fp32 [k'][, sims [N]]) with k' = min(top_k, N),
     descending, ties to the lower row index (kessie_hip_kernels.py:343-360; with
     normalize_rows=False the rows are taken as already normalised, as
-    VectorIndex keeps them, kessie_exp3.py:69-81)."""
+    VectorIndex keeps them, kessie_exp3.py:69-81).  out_ids (int32) /
+    out_scores (fp32), contiguous with at least top_k elements, receive the
+    results instead of fresh tensors."""
     _need_cuda(query, index)
     if query.dtype != torch.float32 or index.dtype != torch.float32:
         raise TypeError("index_query: fp32 query and index")
@@ -551,8 +553,15 @@ def index_query(query: torch.Tensor, index: torch.Tensor, top_k: int = 5, normal
         raise ValueError("index_query: top_k <= 32")
     sims = torch.empty(N, dtype=torch.float32, device=x.device) if return_sims else None
     k = max(int(top_k), 0)
-    ids = torch.empty(max(k, 1), dtype=torch.int32, device=x.device)
-    scores = torch.empty(max(k, 1), dtype=torch.float32, device=x.device)
+    ids, scores = out_ids, out_scores
+    for t, dt, name in ((ids, torch.int32, "out_ids"), (scores, torch.float32, "out_scores")):
+        if t is not None and (t.dtype != dt or not t.is_contiguous() or t.numel() < k or t.device != x.device):
+            raise ValueError(f"index_query: {name} must be a contiguous {dt} tensor of >= top_k elements on "
+                             f"the index's device")
+    if ids is None:
+        ids = torch.empty(max(k, 1), dtype=torch.int32, device=x.device)
+    if scores is None:
+        scores = torch.empty(max(k, 1), dtype=torch.float32, device=x.device)
     lib = _lib.load()
     ws = None
     if k > 0:

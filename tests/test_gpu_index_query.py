@@ -79,3 +79,36 @@ def test_index_query_drop_in_function():
     np.testing.assert_allclose(sims.cpu().numpy(), want[0], rtol=1e-5, atol=1e-6)
     assert torch.equal(sims, sims2)
     np.testing.assert_array_equal(ids.cpu().numpy(), want[1])
+
+
+def test_vector_index_mirror_matches_reference(golden_dir):
+    """kessie_b200.vector_index.VectorIndex against the reference VectorIndex's
+    golden results (ids mapped through the stored id list), the tiny-query
+    guard, k = min(top_k, count), and top_k above the device list length."""
+    from kessie_b200.vector_index import VectorIndex
+    d = np.load(os.path.join(golden_dir, "index_query.npz"))
+    n, dim, seed = (int(v) for v in d["cfg"])
+    mat = np.random.default_rng(seed).standard_normal((n, dim), dtype=np.float32)
+    mat[7] = 0.0
+    vi = VectorIndex(dim=dim)
+    assert vi.search(mat[0]) == [] and vi.count == 0
+    vi.rebuild([mat[i] for i in range(n)], [5000 + i for i in range(n)])
+    assert vi.count == n
+    for qi in range(3):
+        q = np.random.default_rng(seed + 1 + qi).standard_normal((dim,), dtype=np.float32)
+        got = vi.search(q, top_k=10)
+        assert [g[0] for g in got] == [5000 + int(i) for i in d[f"q{qi}_ids"]]
+        np.testing.assert_allclose([g[1] for g in got], d[f"q{qi}_scores"], rtol=1e-5, atol=1e-6)
+    assert len(vi.search(np.full(dim, 1e-12, np.float32), top_k=10)) == int(d["tiny_query_result_len"])
+    q = np.random.default_rng(3).standard_normal((dim,), dtype=np.float32)
+    big = vi.search(q, top_k=100)                                  # beyond 32: similarity output + stable sort
+    rows = O.vector_index_rows(mat)
+    _, want_ids, want_scores = O.index_query(q / np.linalg.norm(q), rows, False, 100)
+    assert [g[0] for g in big] == [5000 + int(i) for i in want_ids]
+    np.testing.assert_allclose([g[1] for g in big], want_scores, rtol=1e-5, atol=1e-6)
+    small = VectorIndex(dim=4)
+    small.rebuild([np.array([1, 0, 0, 0], np.float32), np.array([0, 1, 0, 0], np.float32)], [11, 12])
+    got = small.search(np.array([1, 0.5, 0, 0], np.float32), top_k=5)
+    assert [g[0] for g in got] == [11, 12]
+    small.rebuild([], [])
+    assert small.search(np.ones(4, np.float32)) == [] and small.count == 0
