@@ -405,6 +405,37 @@ int kessie_index_query_v2(const float* query, const float* index, int num_rows, 
                           void* stream);
 
 /* ---------------------------------------------------------------------------
+ * HF tiered KV cache (KeSSieCache, kessie_exp3.py:342-627) on per-layer stores
+ * [B, H, cap, D] (dtype elements, live tokens at [lo, hi) of the cap axis).
+ *
+ * kessie_tiered_update_v2 replaces KeSSieCache.update (:425-450): appends the
+ * T new tokens k_new / v_new [B, H, T, D] (element strides b, h, t; head_dim
+ * contiguous; K and V share the strides) at [hi, hi + T) and, when the
+ * reference's _compute_fog_mask (:415-423) gives a mask for S = hi + T - lo
+ * (fog_alpha > 0, fc = S - max(1, int(S * fog_start)) > 0), writes
+ *   v_fog[b, h, s, :] = dtype(float(v[b, h, lo + s, :]) * w(s)),
+ *   w(s) = max((s / max(fc - 1, 1)) ^ fog_alpha, 0.01) for s < fc, else 1
+ * into v_fog, contiguous [B, H, S, D]; with no mask v_fog is not touched.
+ * Needs hi + T <= cap, D * element size a multiple of 16, 16-byte aligned
+ * buffers.
+ *
+ * kessie_strided_pack_v2 replaces the per-layer slicing copies of
+ * evict_if_needed / recall_from_cpu (:452-533): for every store m of
+ * num_stores, store_bases[m] = device address of (row 0, token t0) and
+ * store_pitch_bytes[m] = bytes between its rows (cap * D * element size),
+ * rows_per_store rows (B * H) of `tokens` tokens of row_bytes (D * element
+ * size, a multiple of 16) are copied to (unpack = 0) or from (unpack = 1) a
+ * contiguous staging [num_stores][rows_per_store][tokens][row_bytes].
+ * store_bases and store_pitch_bytes are DEVICE arrays. */
+int kessie_tiered_update_v2(void* k_store, void* v_store, long long cap, long long lo, long long hi,
+                            const void* k_new, const void* v_new, long long new_stride_b,
+                            long long new_stride_h, long long new_stride_t, int B, int H, int T, int D,
+                            int dtype, void* v_fog, float fog_alpha, double fog_start, void* stream);
+int kessie_strided_pack_v2(const unsigned long long* store_bases, const long long* store_pitch_bytes,
+                           int num_stores, int rows_per_store, long long tokens, int row_bytes,
+                           void* staging, int unpack, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Context-parallel decode over NVLink peer memory (no counterpart in the
  * reference, which has no multi-GPU attention path).  Each of the `world`
  * ranks (one GPU each, one node, world <= 8) holds a contiguous position

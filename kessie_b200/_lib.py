@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
-from ctypes import c_float, c_int, c_int64, c_size_t, c_void_p, c_char_p, POINTER, c_uint32
+from ctypes import c_double, c_float, c_int, c_int64, c_size_t, c_void_p, c_char_p, POINTER, c_uint32
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 DEFAULT_PATHS = [
@@ -87,6 +87,9 @@ SIGNATURES = {
     "kessie_build_fog_bias_v2": (c_int, [P, c_int, c_int, P, P]),
     "kessie_index_query_workspace_size": (c_size_t, [c_int, c_int]),
     "kessie_index_query_v2": (c_int, [P, P, c_int, c_int, c_int, P, c_int, P, P, P, c_size_t, P]),
+    "kessie_tiered_update_v2": (c_int, [P, P, c_int64, c_int64, c_int64, P, P, c_int64, c_int64, c_int64, c_int, c_int,
+                                        c_int, c_int, c_int, P, c_float, c_double, P]),
+    "kessie_strided_pack_v2": (c_int, [P, P, c_int, c_int, c_int64, c_int, P, c_int, P]),
     "kessie_paged_fog_decode_biased_v2": (c_int, [P, c_int64, c_int64, P, P, c_int64, c_int64, c_int64, c_int, c_int,
                                                   I32P, c_int64, I32P, I32P, I32P, I32P, c_float, P, c_int, c_float,
                                                   c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, c_size_t, P]),

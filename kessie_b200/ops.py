@@ -572,3 +572,54 @@ def index_query(query: torch.Tensor, index: torch.Tensor, top_k: int = 5, normal
     kk = min(k, N)
     out = (ids[:kk], scores[:kk])
     return out + (sims,) if return_sims else out
+
+
+# --------------------------------------------------------------------- tiered cache
+def tiered_update(k_store: torch.Tensor, v_store: torch.Tensor, lo: int, hi: int, k_new: torch.Tensor,
+                  v_new: torch.Tensor, v_fog: Optional[torch.Tensor], fog_alpha: float, fog_start: float,
+                  stream=None) -> bool:
+    """KeSSieCache.update's device work (kessie_exp3.py:425-450) on a store
+    pair [B, H, cap, D]: appends k_new / v_new [B, H, T, D] at [hi, hi + T)
+    and, when the reference's fog mask exists for S = hi + T - lo, writes the
+    fogged V of [lo, hi + T) into v_fog (>= B*H*S*D contiguous elements).
+    Returns whether the fog was applied."""
+    _need_cuda(k_store, v_store, k_new, v_new, v_fog)
+    B, H, cap, D = k_store.shape
+    T = k_new.shape[2]
+    if v_store.shape != k_store.shape or k_new.shape != (B, H, T, D) or v_new.shape != k_new.shape:
+        raise ValueError("tiered_update: store / new-token shapes differ")
+    for t in (k_store, v_store, k_new, v_new):
+        if t.dtype != k_store.dtype:
+            raise TypeError("tiered_update: one dtype for stores and new tokens")
+    if not (k_store.is_contiguous() and v_store.is_contiguous()):
+        raise ValueError("tiered_update: stores must be contiguous [B, H, cap, D]")
+    if k_new.stride() != v_new.stride() or k_new.stride(3) != 1:
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+    S = hi + T - lo
+    if v_fog is not None and (not v_fog.is_contiguous() or v_fog.numel() < B * H * S * D or v_fog.dtype != k_store.dtype):
+        raise ValueError("tiered_update: v_fog must be contiguous with >= B*H*S*D elements of the store dtype")
+    cc = max(1, int(S * fog_start))
+    fog_on = fog_alpha > 0 and S > 0 and S - cc > 0
+    _lib.check(_lib.load().kessie_tiered_update_v2(
+        k_store.data_ptr(), v_store.data_ptr(), cap, int(lo), int(hi), k_new.data_ptr(), v_new.data_ptr(),
+        k_new.stride(0), k_new.stride(1), k_new.stride(2), B, H, T, D, dtype_code(k_store),
+        _p(v_fog) if fog_on else None, float(fog_alpha), float(fog_start), _stream(stream)), "tiered_update")
+    return fog_on
+
+
+def strided_pack(bases: torch.Tensor, pitch_bytes: torch.Tensor, rows_per_store: int, tokens: int, row_bytes: int,
+                 staging: torch.Tensor, unpack: bool, stream=None):
+    """Copy tokens of len(bases) strided stores to (unpack=False) or from
+    (unpack=True) the contiguous staging [stores][rows][tokens][row_bytes]
+    (kessie_exp3.py:452-533's per-layer slicing copies, in one launch).
+    bases / pitch_bytes: int64 CUDA tensors (device address of each store's
+    first copied token, bytes between its rows)."""
+    _need_cuda(bases, pitch_bytes, staging)
+    if bases.dtype != torch.int64 or pitch_bytes.dtype != torch.int64 or bases.numel() != pitch_bytes.numel():
+        raise ValueError("strided_pack: int64 bases / pitch_bytes of one length")
+    if staging.numel() * staging.element_size() < bases.numel() * rows_per_store * tokens * row_bytes:
+        raise ValueError("strided_pack: staging too small")
+    _lib.check(_lib.load().kessie_strided_pack_v2(bases.data_ptr(), pitch_bytes.data_ptr(), bases.numel(),
+                                                   int(rows_per_store), int(tokens), int(row_bytes),
+                                                   staging.data_ptr(), 1 if unpack else 0, _stream(stream)),
+               "strided_pack")

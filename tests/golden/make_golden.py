@@ -269,6 +269,64 @@ def gen_index_query():
     save("index_query.npz", **out)
 
 
+# Tiered-cache schedule (window 48, 3 layers, [1, 2, T, 32]): prefill 70,
+# decode steps with an eviction check after each, recalls (one of a position
+# that is not stored), a 5-token append.  ("u", T, seed) = update every layer
+# with rnd(seed + layer) K and rnd(seed + 50 + layer) V; "rec" entries record
+# the returned fogged V of every layer, layer 0's K and the stats (bf16 arrays
+# as uint16 bit patterns).
+TIERED_SCHEDULE = ([["u", 70, 100], ["rec"]] +
+                   sum([[["u", 1, 200 + i], ["e"]] + ([["rec"]] if i in (0, 26, 29) else []) for i in range(30)], []) +
+                   [["r", 10], ["rec"], ["u", 1, 300], ["rec"], ["e"], ["rec"], ["r", 5000], ["u", 5, 400], ["rec"],
+                    ["r", 52], ["u", 1, 500], ["rec"]])
+TIERED_CASES = [("bf16_a05", "bfloat16", 0.5, 0.5), ("f32_a07", "float32", 0.7, 0.3), ("bf16_off", "bfloat16", 0.0, 0.5)]
+TIERED_SHAPE = (1, 2, 32)          # B, H, D
+TIERED_LAYERS = 3
+TIERED_WINDOW = 48
+
+
+def gen_tiered_cache():
+    """KeSSieCache (kessie_exp3.py:342-627) on CPU torch through TIERED_SCHEDULE."""
+    import json
+    import kessie_exp3 as E
+    B, H, D = TIERED_SHAPE
+    out = {"schedule": np.array(json.dumps(TIERED_SCHEDULE))}
+    for tag, dt, alpha, fstart in TIERED_CASES:
+        tdt = getattr(torch, dt)
+        c = E.KeSSieCache(window_size=TIERED_WINDOW, fog_alpha=alpha, fog_start=fstart)
+        last = None
+        stats, rec = [], 0
+        for op in TIERED_SCHEDULE:
+            if op[0] == "u":
+                _, T, seed = op
+                last = []
+                for l in range(TIERED_LAYERS):
+                    k = torch.from_numpy(rnd(seed + l, (B, H, T, D))).to(tdt)
+                    v = torch.from_numpy(rnd(seed + 50 + l, (B, H, T, D))).to(tdt)
+                    ko, vo = c.update(k, v, l)
+                    last.append((ko.float().numpy().copy(), vo.float().numpy().copy()))
+            elif op[0] == "e":
+                c.evict_if_needed()
+            elif op[0] == "r":
+                stats.append({"recall": op[1], "ok": bool(c.recall_from_cpu(op[1], "cpu"))})
+            elif op[0] == "rec":
+                # fogged V of every layer, K of layer 0 (K is a copy); bf16 as bit patterns
+                pack = ((lambda a: torch.from_numpy(a).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16))
+                        if dt == "bfloat16" else (lambda a: a))
+                out[f"{tag}_r{rec}_l0_k"] = pack(last[0][0])
+                for l, (ko, vo) in enumerate(last):
+                    out[f"{tag}_r{rec}_l{l}_v"] = pack(vo)
+                st = c.get_stats()
+                stats.append({k: st[k] for k in ("kv_seq_len", "kv_window_start", "kv_layers", "kv_gpu_bytes",
+                                                 "kv_cpu_chunks", "kv_cpu_tokens", "fog_tokens", "clear_tokens",
+                                                 "total_evictions", "total_recalls")} |
+                             {"cpu_kv_bytes": c.cpu_kv_bytes, "seen_tokens": c.seen_tokens,
+                              "chunks": [[s_, e_] for s_, e_, _ in c.cpu_kv_store]})
+                rec += 1
+        out[f"{tag}_stats"] = np.array(json.dumps(stats))
+    save("tiered_cache.npz", **out)
+
+
 if __name__ == "__main__":
     gen_fog()
     gen_rope()
@@ -278,3 +336,4 @@ if __name__ == "__main__":
     gen_kv_store()
     gen_fog_bias()
     gen_index_query()
+    gen_tiered_cache()
