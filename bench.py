@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--impl", choices=["kessie", "reference"], default="kessie")
     ap.add_argument("--workload", default="cp_decode_1m",
                     choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "page_ops", "prefill",
-                             "prefill_small", "vllm_fog_decode", "index_query"])
+                             "prefill_small", "vllm_fog_decode", "index_query", "tiered_cache"])
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -462,7 +462,7 @@ def run_cp_decode(args):
             torch.cuda.empty_cache()
             sec = {}
             for wl, st in (("decode_128k", 20), ("decode_cfg3", 20), ("vllm_fog_decode", 20), ("page_ops", 50),
-                           ("prefill", 10), ("index_query", 50)):
+                           ("prefill", 10), ("index_query", 50), ("tiered_cache", 20)):
                 r = measure_aux(wl, st)
                 r.pop("workload", None)
                 sec[wl] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}
@@ -471,7 +471,8 @@ def run_cp_decode(args):
             line["secondary_note"] = ("other north_star configs, same process, CUDA-event timed: decode_128k/cfg3 = "
                                       "config 3 (GB/s vs hbm peak), vllm_fog_decode = config 3 through the vLLM "
                                       "attention mirror with the fog bias, page_ops = config 2, prefill = config 4 "
-                                      "(TFLOP/s), index_query = conversation-index top-5 (GB/s vs hbm peak)")
+                                      "(TFLOP/s), index_query = conversation-index top-5 (GB/s vs hbm peak), "
+                                      "tiered_cache = HF tiered-cache decode step over 32 layers (GB/s vs hbm peak)")
         print(json.dumps(line), flush=True)
     if world > 1:
         dec.close()                       # collective: barrier, then unmap / free the exchange buffers
@@ -699,6 +700,115 @@ def measure_aux(workload, steps, warmup=3):
                                       "launch pair (query + merge); warm = back-to-back calls, index resident in L2 (n78125 only fits); "
                                       "search_e2e = VectorIndex.search wall time per call (host query in, host "
                                       "results out)")
+    elif args.workload == "tiered_cache":
+        # HF tiered KV cache (KeSSieCache): a decode step = update() of all 32
+        # layers, [1, 8, S, 128] bf16, window 4096, fog 0.5 / 0.5, S from 6144
+        # (between one and two windows).  Algorithmic bytes per layer update:
+        # the live V read + the fogged V written (2 x S x H x D x 2) + the new
+        # token's K and V read and written.  Device time: a device-side sleep
+        # lets the host enqueue every step before the first event.  Beside it,
+        # the reference's update as its own torch ops (cat, fp32 fog mask,
+        # v.float() * fog, .to) on the same shapes.  Then one eviction of
+        # 4,097 tokens x 32 layers and its recall, wall time.
+        import time
+        from kessie_b200.kessie_cache import KeSSieCache
+        L, Bq, Hk, Dh, W, S0 = 32, 1, 8, 128, 4096, 6143
+        cache = KeSSieCache(window_size=W, fog_alpha=0.5, fog_start=0.5)
+        kp = torch.randn(Bq, Hk, S0, Dh, device=dev, dtype=torch.bfloat16)
+        vp = torch.randn_like(kp)
+        for l in range(L):
+            cache.update(kp, vp, l)
+        k1, v1 = torch.randn(Bq, Hk, 1, Dh, device=dev, dtype=torch.bfloat16), torch.randn(Bq, Hk, 1, Dh, device=dev, dtype=torch.bfloat16)
+        K = args.steps
+
+        def step():
+            for l in range(L):
+                cache.update(k1, v1, l)
+
+        def dev_time(fn, reps, host_us):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(int(reps * host_us * 2000))
+            a.record()
+            for _ in range(reps):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / reps
+
+        s_first = cache.get_seq_length() + 3 + 1
+        ms = dev_time(step, K, L * 60)
+        s_mid = s_first + K // 2
+        byts = L * (2 * s_mid * Bq * Hk * Dh * 2 + 4 * Bq * Hk * Dh * 2)
+        # the reference's update on the same shapes, as its torch ops
+        kc = [kp.clone() for _ in range(L)]
+        vc = [vp.clone() for _ in range(L)]
+
+        def ref_step():
+            for l in range(L):
+                kc[l] = torch.cat([kc[l], k1], dim=-2)
+                vc[l] = torch.cat([vc[l], v1], dim=-2)
+                n = vc[l].shape[-2]
+                cc = max(1, int(n * 0.5))
+                fc = n - cc
+                pos = torch.arange(fc, dtype=torch.float32, device=dev)
+                fw = (pos / max(fc - 1, 1)).pow(0.5).clamp(min=0.01)
+                fog = torch.cat([fw, torch.ones(cc, dtype=torch.float32, device=dev)]).view(1, 1, n, 1)
+                _ = (vc[l].float() * fog).to(kc[l].dtype)
+
+        ms_ref = dev_time(ref_step, K, L * 150)
+        del kc, vc
+        # one eviction (S = 8193 -> 4096 kept) and its recall, wall time
+        grow = 2 * W + 1 - cache.get_seq_length()
+        kg = torch.randn(Bq, Hk, grow, Dh, device=dev, dtype=torch.bfloat16)
+        for l in range(L):
+            cache.update(kg, kg, l)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        cache.evict_if_needed()
+        t_ev = time.perf_counter() - t0
+        start, end = cache.cpu_kv_store[-1][:2]
+        ev_bytes = L * 2 * Bq * Hk * (end - start) * Dh * 2
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ok = cache.recall_from_cpu(start, dev)
+        torch.cuda.synchronize()
+        t_rc = time.perf_counter() - t0
+        # a second eviction of the same size (the recalled chunk's pinned block is free again)
+        for l in range(L):
+            cache.update(kg[:, :, :end - start], kg[:, :, :end - start], l)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        cache.evict_if_needed()
+        t_ev2 = time.perf_counter() - t0
+        # the reference's eviction as its own torch ops on the same shapes: per
+        # layer .to("cpu") of the evicted range, then .contiguous() of the rest
+        del cache, kg
+        torch.cuda.empty_cache()
+        S_ev = 2 * W + 1
+        ev = S_ev - W
+        kc = [torch.randn(Bq, Hk, S_ev, Dh, device=dev, dtype=torch.bfloat16) for _ in range(L)]
+        vc = [torch.randn(Bq, Hk, S_ev, Dh, device=dev, dtype=torch.bfloat16) for _ in range(L)]
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        cpu_layers = []
+        for l in range(L):
+            cpu_layers.append((kc[l][:, :, :ev, :].to("cpu", non_blocking=True),
+                               vc[l][:, :, :ev, :].to("cpu", non_blocking=True)))
+            kc[l] = kc[l][:, :, ev:, :].contiguous()
+            vc[l] = vc[l][:, :, ev:, :].contiguous()
+        torch.cuda.synchronize()
+        t_ref_ev = time.perf_counter() - t0
+        del kc, vc, cpu_layers
+        res.update(step_ms=ms, step_bytes=byts, GBs=byts / ms / 1e6, frac_of_hbm=byts / ms / 1e6 / hbm,
+                   evict2_ms=t_ev2 * 1e3, evict2_GBs=ev_bytes / t_ev2 / 1e9, reference_torch_ops_evict_ms=t_ref_ev * 1e3,
+                   reference_torch_ops_step_ms=ms_ref, speedup_vs_reference_ops=ms_ref / ms,
+                   evict_ms=t_ev * 1e3, evict_tokens=end - start, evict_GBs=ev_bytes / t_ev / 1e9,
+                   recall_ms=t_rc * 1e3, recall_ok=bool(ok), recall_GBs=ev_bytes / t_rc / 1e9,
+                   note="32-layer decode step, [1, 8, S, 128] bf16, S ~ %d; device time (CUDA events, host "
+                        "enqueue ahead); evict / recall wall time incl. the host-memory copy" % s_mid)
     elif args.workload in ("prefill", "prefill_small"):
         Hq, Hkv, D, ps, T, Nk = 32, 8, 128, 16, 8192, 262144
         if args.workload == "prefill_small":        # profiling size: 256 MB of KV

@@ -62,76 +62,104 @@ struct TieredUpdateArgs {
     char* v_fog;                  // nullptr: fog off
     long long cap, lo, hi;        // tokens
     long long nsb, nsh, nst;      // new-token strides (bytes) for b, h, t
-    int B, H, T, chunks;          // chunks = row bytes / 16
-    long long S;                  // live tokens after the append
+    int H, T, S, chunks;          // S = live tokens after the append; chunks = row bytes / 16
     int fc, alpha_mode;
     float den, alpha;
 };
 
-template <typename T>
+constexpr int kItems = 4;                                  // 16-byte items in flight per thread
+
+// grid (x over the rows of one (b, h), y = b * H + h): rows [0, S) are the
+// fogged V (or [0, T) the V append when the fog is off), then T K-append rows.
+template <typename T, int CH>
 __global__ void __launch_bounds__(256) tiered_update_kernel(TieredUpdateArgs a) {
-    const long long row_bytes = (long long)a.chunks * 16;
-    const long long BH = (long long)a.B * a.H;
-    const long long s_old = a.hi - a.lo;
-    const long long v_rows = a.v_fog ? BH * a.S : BH * a.T;
-    const long long total = (v_rows + BH * a.T) * a.chunks;
-    for (long long it = blockIdx.x * (long long)blockDim.x + threadIdx.x; it < total;
-         it += (long long)gridDim.x * blockDim.x) {
-        const long long row = it / a.chunks;
-        const int c = (int)(it - row * a.chunks);
-        if (row < v_rows) {
-            if (a.v_fog) {                                   // fogged V of the live range (+ V append)
-                const long long bh = row / a.S, s = row - bh * a.S;
-                const float w = tiered_fog_weight(s, a.fc, a.den, a.alpha, a.alpha_mode);
-                uint4 raw;
-                if (s < s_old) {
-                    raw = ldg_stream(a.v_store + ((bh * a.cap + a.lo + s) * row_bytes + c * 16));
-                } else {
-                    const long long t = s - s_old, b = bh / a.H, h = bh - b * a.H;
-                    raw = ldg_stream(a.v_new + (b * a.nsb + h * a.nsh + t * a.nst + c * 16));
-                    *reinterpret_cast<uint4*>(a.v_store + ((bh * a.cap + a.hi + t) * row_bytes + c * 16)) = raw;
-                }
-                stg_stream(a.v_fog + (row * row_bytes + c * 16), scale16<T>(raw, w));
-            } else {                                         // V append only
-                const long long bh = row / a.T, t = row - bh * a.T, b = bh / a.H, h = bh - b * a.H;
-                const uint4 raw = ldg_stream(a.v_new + (b * a.nsb + h * a.nsh + t * a.nst + c * 16));
-                *reinterpret_cast<uint4*>(a.v_store + ((bh * a.cap + a.hi + t) * row_bytes + c * 16)) = raw;
+    const int chunks = CH > 0 ? CH : a.chunks;
+    const long long rb = (long long)chunks * 16;
+    const int bh = blockIdx.y, b = bh / a.H, h = bh - b * a.H;
+    const int s_old = (int)(a.hi - a.lo);
+    const int vrows = a.v_fog ? a.S : a.T;
+    const int items = (vrows + a.T) * chunks;
+    char* vst = a.v_store + (long long)bh * a.cap * rb;
+    char* kst = a.k_store + (long long)bh * a.cap * rb;
+    const char* vnew = a.v_new + b * a.nsb + h * a.nsh;
+    const char* knew = a.k_new + b * a.nsb + h * a.nsh;
+    char* vfog = a.v_fog ? a.v_fog + (long long)bh * a.S * rb : nullptr;
+    for (int base = blockIdx.x * 256 * kItems + threadIdx.x; base < items; base += gridDim.x * 256 * kItems) {
+        uint4 raw[kItems];
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) {
+            const int i = base + u * 256;
+            if (i >= items) break;
+            const int r = i / chunks, c = i - r * chunks;
+            const char* src;
+            if (r < vrows) {
+                if (vfog && r < s_old) src = vst + (a.lo + r) * rb;
+                else src = vnew + (long long)(vfog ? r - s_old : r) * a.nst;
+            } else {
+                src = knew + (long long)(r - vrows) * a.nst;
             }
-        } else {                                             // K append
-            const long long r = row - v_rows;
-            const long long bh = r / a.T, t = r - bh * a.T, b = bh / a.H, h = bh - b * a.H;
-            const uint4 raw = ldg_stream(a.k_new + (b * a.nsb + h * a.nsh + t * a.nst + c * 16));
-            *reinterpret_cast<uint4*>(a.k_store + ((bh * a.cap + a.hi + t) * row_bytes + c * 16)) = raw;
+            raw[u] = ldg_stream(src + c * 16);
+        }
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) {
+            const int i = base + u * 256;
+            if (i >= items) break;
+            const int r = i / chunks, c = i - r * chunks;
+            if (r < vrows) {
+                if (vfog) {
+                    const float w = tiered_fog_weight(r, a.fc, a.den, a.alpha, a.alpha_mode);
+                    stg_stream(vfog + r * rb + c * 16, scale16<T>(raw[u], w));
+                    if (r >= s_old)
+                        *reinterpret_cast<uint4*>(vst + (a.hi + r - s_old) * rb + c * 16) = raw[u];
+                } else {
+                    *reinterpret_cast<uint4*>(vst + (a.hi + r) * rb + c * 16) = raw[u];
+                }
+            } else {
+                *reinterpret_cast<uint4*>(kst + (a.hi + r - vrows) * rb + c * 16) = raw[u];
+            }
         }
     }
 }
 
-// Pack (unpack = 0) or unpack (1) tokens [t0, t0 + n) of M strided stores.
+// Pack (unpack = 0) or unpack (1): grid (x over one store row's tokens,
+// y = store * BH + row); row y of the staging is contiguous.
+template <int CH>
 __global__ void __launch_bounds__(256) strided_pack_kernel(const unsigned long long* __restrict__ bases,
-                                                           const long long* __restrict__ pitches, int M, long long BH,
-                                                           long long n, int chunks, char* __restrict__ staging,
-                                                           int unpack) {
-    const long long row_bytes = (long long)chunks * 16;
-    const long long total = (long long)M * BH * n * chunks;
-    for (long long it = blockIdx.x * (long long)blockDim.x + threadIdx.x; it < total;
-         it += (long long)gridDim.x * blockDim.x) {
-        const long long row = it / chunks;
-        const int c = (int)(it - row * chunks);
-        const long long t = row % n, mb = row / n;
-        const long long bh = mb % BH;
-        const int m = (int)(mb / BH);
-        char* store = reinterpret_cast<char*>(bases[m]) + bh * pitches[m] + t * row_bytes + c * 16;
-        char* stage = staging + row * row_bytes + c * 16;
-        if (unpack) *reinterpret_cast<uint4*>(store) = ldg_stream(stage);
-        else stg_stream(stage, *reinterpret_cast<const uint4*>(store));
+                                                           const long long* __restrict__ pitches, int BH, int n,
+                                                           int chunks_rt, char* __restrict__ staging, int unpack) {
+    const int chunks = CH > 0 ? CH : chunks_rt;
+    const long long rb = (long long)chunks * 16;
+    const int m = blockIdx.y / BH, bh = blockIdx.y - m * BH;
+    char* store = reinterpret_cast<char*>(bases[m]) + bh * pitches[m];
+    char* stage = staging + (long long)blockIdx.y * n * rb;
+    const int items = n * chunks;                          // one store row = n tokens x rb bytes, contiguous
+    for (int base = blockIdx.x * 256 * kItems + threadIdx.x; base < items; base += gridDim.x * 256 * kItems) {
+        uint4 v[kItems];
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) {
+            const int i = base + u * 256;
+            if (i >= items) break;
+            v[u] = ldg_stream((unpack ? stage : store) + (long long)i * 16);
+        }
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) {
+            const int i = base + u * 256;
+            if (i >= items) break;
+            char* dst = (unpack ? store : stage) + (long long)i * 16;
+            if (unpack) *reinterpret_cast<uint4*>(dst) = v[u];
+            else stg_stream(dst, v[u]);
+        }
     }
 }
 
-int copy_grid(long long items) {
-    const long long per = 256LL * 8;                       // 8 items per thread before the stride
-    long long g = (items + per - 1) / per;
-    const long long cap = (long long)sm_count() * 8;
-    return (int)(g < 1 ? 1 : (g > cap ? cap : g));
+// x blocks for `items` per y row: enough CTAs in total for the SMs, at most
+// one item batch per thread when that fits.
+int grid_x(long long items, long long rows_y) {
+    const long long per = 256LL * kItems;
+    long long gx = (items + per - 1) / per;
+    const long long cap = ((long long)sm_count() * 16 + rows_y - 1) / rows_y;
+    if (gx > cap) gx = cap;
+    return (int)(gx < 1 ? 1 : gx);
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -163,6 +191,8 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
         fc = (int)(S - cc);
     }
     if (fc <= 0) v_fog = nullptr;
+    if ((long long)B * H > 65535 || S > (1LL << 30) / (D * es / 16 + 1))
+        return set_error(KESSIE_ERR_ARG, "tiered_update_v2: B * H <= 65535 and S * row chunks < 2^30");
     TieredUpdateArgs a;
     a.k_store = static_cast<char*>(k_store);
     a.v_store = static_cast<char*>(v_store);
@@ -171,20 +201,29 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
     a.v_fog = static_cast<char*>(v_fog);
     a.cap = cap; a.lo = lo; a.hi = hi;
     a.nsb = new_stride_b * es; a.nsh = new_stride_h * es; a.nst = new_stride_t * es;
-    a.B = B; a.H = H; a.T = T; a.chunks = D * es / 16;
-    a.S = S;
+    a.H = H; a.T = T; a.S = (int)S; a.chunks = D * es / 16;
     a.fc = fc;
     a.den = (float)(fc - 1 > 1 ? fc - 1 : 1);
     a.alpha = fog_alpha;
     a.alpha_mode = fog_alpha == 0.5f ? 1 : fog_alpha == 1.f ? 2 : fog_alpha == 2.f ? 3 : fog_alpha == 3.f ? 4 : 0;
-    const long long BH = (long long)B * H;
-    const long long items = ((v_fog ? BH * S : BH * T) + BH * T) * a.chunks;
-    if (items == 0) { clear_error(); return 0; }
+    const long long rows = (v_fog ? S : T) + T;
+    if (rows == 0) { clear_error(); return 0; }
     cudaStream_t st = as_stream(stream);
-    const int grid = copy_grid(items);
-    if (dtype == KESSIE_DTYPE_BF16) tiered_update_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
-    else if (dtype == KESSIE_DTYPE_F16) tiered_update_kernel<__half><<<grid, 256, 0, st>>>(a);
-    else tiered_update_kernel<float><<<grid, 256, 0, st>>>(a);
+    const dim3 grid(grid_x(rows * a.chunks, (long long)B * H), B * H);
+    auto launch = [&](auto kern) { kern<<<grid, 256, 0, st>>>(a); };
+    if (dtype == KESSIE_DTYPE_BF16) {
+        if (a.chunks == 16) launch(tiered_update_kernel<__nv_bfloat16, 16>);
+        else if (a.chunks == 8) launch(tiered_update_kernel<__nv_bfloat16, 8>);
+        else launch(tiered_update_kernel<__nv_bfloat16, 0>);
+    } else if (dtype == KESSIE_DTYPE_F16) {
+        if (a.chunks == 16) launch(tiered_update_kernel<__half, 16>);
+        else if (a.chunks == 8) launch(tiered_update_kernel<__half, 8>);
+        else launch(tiered_update_kernel<__half, 0>);
+    } else {
+        if (a.chunks == 32) launch(tiered_update_kernel<float, 32>);
+        else if (a.chunks == 16) launch(tiered_update_kernel<float, 16>);
+        else launch(tiered_update_kernel<float, 0>);
+    }
     return check_launch("tiered_update");
 }
 
@@ -194,10 +233,17 @@ extern "C" int kessie_strided_pack_v2(const unsigned long long* store_bases, con
     if (!store_bases || !store_pitch_bytes || !staging || num_stores <= 0 || rows_per_store <= 0 || tokens < 0 ||
         row_bytes <= 0 || row_bytes % 16 || !al16(staging))
         return set_error(KESSIE_ERR_ARG, "strided_pack_v2: bad arguments (row_bytes % 16 == 0, aligned staging)");
-    const long long items = (long long)num_stores * rows_per_store * tokens * (row_bytes / 16);
-    if (items == 0) { clear_error(); return 0; }
-    strided_pack_kernel<<<copy_grid(items), 256, 0, as_stream(stream)>>>(
-        store_bases, store_pitch_bytes, num_stores, rows_per_store, tokens, row_bytes / 16,
-        static_cast<char*>(staging), unpack ? 1 : 0);
+    if ((long long)num_stores * rows_per_store > 65535 || tokens * (row_bytes / 16) > (1LL << 30))
+        return set_error(KESSIE_ERR_ARG, "strided_pack_v2: stores * rows <= 65535, tokens * row chunks < 2^30");
+    if (tokens == 0) { clear_error(); return 0; }
+    const int ch = row_bytes / 16, ys = num_stores * rows_per_store;
+    const dim3 grid(grid_x(tokens * ch, ys), ys);
+    cudaStream_t st = as_stream(stream);
+    if (ch == 16)
+        strided_pack_kernel<16><<<grid, 256, 0, st>>>(store_bases, store_pitch_bytes, rows_per_store, (int)tokens, ch,
+                                                       static_cast<char*>(staging), unpack ? 1 : 0);
+    else
+        strided_pack_kernel<0><<<grid, 256, 0, st>>>(store_bases, store_pitch_bytes, rows_per_store, (int)tokens, ch,
+                                                      static_cast<char*>(staging), unpack ? 1 : 0);
     return check_launch("strided_pack");
 }

@@ -16,7 +16,7 @@ range.  So:
   the next ``update`` of the same layer.
 * ``evict_if_needed`` (:452-486) packs the evicted range of every layer with
   ONE ``kessie_strided_pack_v2`` launch, moves it with ONE device-to-host copy
-  into pinned memory (the CPU chunk's per-layer tensors are views of it) and
+  into pinned host memory (the CPU chunk's per-layer tensors are views of it) and
   trims by moving ``lo`` -- no ``.contiguous()`` re-copy of the window.
 * ``recall_from_cpu`` (:488-533) brings a chunk back with ONE host-to-device
   copy (for chunks this class evicted) and ONE unpack launch into the room in
@@ -86,8 +86,8 @@ class _Store:
 
 
 class KeSSieCache:
-    """Tiered KV cache: the hot window in HBM, fogged/evicted KV in pinned
-    host memory, recalled on a hit (kessie_exp3.py:342-351)."""
+    """Tiered KV cache: the hot window in HBM, fogged/evicted KV in host
+    memory, recalled on a hit (kessie_exp3.py:342-351)."""
 
     def __init__(self, window_size=4096, index_granularity=128, fog_alpha=0.5, fog_start=0.5,
                  kv_cache_dtype=None, max_conversation_tokens=10_000_000):
@@ -226,7 +226,7 @@ class KeSSieCache:
 
     def evict_if_needed(self):
         """Above twice the window, move all but the last window tokens of every
-        layer to pinned host memory (kessie_exp3.py:452-486)."""
+        layer to host memory (kessie_exp3.py:452-486)."""
         if not self.key_cache or not self._valid(self.key_cache[0]):
             return
         cl = self.key_cache[0].shape[-2]
@@ -246,7 +246,9 @@ class KeSSieCache:
             dev = st0.k.device
             nel = len(grp) * 2 * B * H * ev * D
             staging = torch.empty(nel, dtype=st0.k.dtype, device=dev)
-            host = torch.empty(nel, dtype=st0.k.dtype).pin_memory()
+            # pinned, from torch's caching host allocator: a recalled chunk's block
+            # returns there and the next eviction of that size reuses it
+            host = torch.empty(nel, dtype=st0.k.dtype, pin_memory=True)
             bases, pitch = self._bases([self._stores[i] for i in grp], [self._stores[i].lo for i in grp], dev)
             ops.strided_pack(bases, pitch, B * H, ev, D * st0.k.element_size(), staging, unpack=False)
             host.copy_(staging, non_blocking=True)
@@ -316,7 +318,10 @@ class KeSSieCache:
                 src, grp = fast[li]
             else:
                 grp = [li]
-                src = torch.cat([cpu_layers[li][0].reshape(-1), cpu_layers[li][1].reshape(-1)]).pin_memory()
+                kr, vr = cpu_layers[li]
+                src = torch.empty(kr.numel() + vr.numel(), dtype=kr.dtype)
+                src[:kr.numel()].copy_(kr.reshape(-1))
+                src[kr.numel():].copy_(vr.reshape(-1))
             st0 = self._stores[grp[0]]
             B, H, _, D = st0.k.shape
             n = cpu_layers[grp[0]][0].shape[-2]
