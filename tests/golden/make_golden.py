@@ -327,6 +327,38 @@ def gen_tiered_cache():
     save("tiered_cache.npz", **out)
 
 
+def gen_tiered_bookkeeping():
+    """KeSSieCache's host bookkeeping (kessie_exp3.py:535-608): conversation
+    overflow with index / turn shifting, turn lookups, token distances, the
+    seeded projection and the stats of a cache without KV."""
+    import json
+    import kessie_exp3 as E
+    c = E.KeSSieCache(window_size=64, fog_alpha=0.5, fog_start=0.25, max_conversation_tokens=50)
+    out = {"steps": []}
+    plan = [(list(range(0, 20)), "user"), (list(range(20, 45)), "assistant"), (list(range(45, 70)), "user"),
+            (list(range(70, 72)), "assistant"), (list(range(72, 140)), "user")]
+    for i, (tids, role) in enumerate(plan):
+        if i == 1:
+            c.index_embeddings = [np.full(4, k, np.float32) for k in range(3)]
+            c.index_positions = [5, 30, 44]
+        c.append_conversation(tids, role)
+        out["steps"].append({
+            "conversation_tokens": list(c.conversation_tokens),
+            "index_positions": list(c.index_positions),
+            "index_embeddings": [float(e[0]) for e in c.index_embeddings],
+            "turn_boundaries": [list(t) for t in c.turn_boundaries],
+            "turns": {str(p): list(c.get_turn_for_position(p)) for p in (-1, 0, 4, 5, 24, 25, 30, 49, 100)},
+            "distance": {str(p): c.get_token_distance(p) for p in (0, 10, 49)},
+            "stats": c.get_stats()})
+    proj = c._get_projection(64, 16)
+    out["projection_64_16"] = proj.astype(np.float64).round(7).tolist()
+    c.full_reset()
+    out["after_full_reset"] = c.get_stats()
+    with open(os.path.join(HERE, "tiered_bookkeeping.json"), "w") as f:
+        json.dump(out, f)
+    print("wrote tiered_bookkeeping.json")
+
+
 if __name__ == "__main__":
     gen_fog()
     gen_rope()
@@ -337,3 +369,4 @@ if __name__ == "__main__":
     gen_fog_bias()
     gen_index_query()
     gen_tiered_cache()
+    gen_tiered_bookkeeping()

@@ -229,3 +229,32 @@ def test_gpu_cache_kv_dtype_cast_and_strided_input():
         assert ck.dtype == torch.bfloat16
         np.testing.assert_array_equal(_np(ck), mk)
         np.testing.assert_array_equal(_np(cv), mv)
+
+
+def test_host_bookkeeping_matches_reference(golden_dir):
+    """append_conversation overflow (index positions and turn boundaries shift
+    or drop; a turn longer than the cap keeps all its tokens, as the
+    reference does), get_turn_for_position, get_token_distance, the seeded
+    projection and get_stats of a cache holding no KV (kessie_exp3.py:535-608)
+    against the reference class's recorded values."""
+    from kessie_b200.kessie_cache import KeSSieCache
+    with open(os.path.join(golden_dir, "tiered_bookkeeping.json")) as f:
+        g = json.load(f)
+    c = KeSSieCache(window_size=64, fog_alpha=0.5, fog_start=0.25, max_conversation_tokens=50)
+    plan = [(list(range(0, 20)), "user"), (list(range(20, 45)), "assistant"), (list(range(45, 70)), "user"),
+            (list(range(70, 72)), "assistant"), (list(range(72, 140)), "user")]
+    for i, ((tids, role), want) in enumerate(zip(plan, g["steps"])):
+        if i == 1:
+            c.index_embeddings = [np.full(4, k, np.float32) for k in range(3)]
+            c.index_positions = [5, 30, 44]
+        c.append_conversation(tids, role)
+        assert c.conversation_tokens == want["conversation_tokens"]
+        assert c.index_positions == want["index_positions"]
+        assert [float(e[0]) for e in c.index_embeddings] == want["index_embeddings"]
+        assert [list(t) for t in c.turn_boundaries] == want["turn_boundaries"]
+        assert {str(p): list(c.get_turn_for_position(p)) for p in (-1, 0, 4, 5, 24, 25, 30, 49, 100)} == want["turns"]
+        assert {str(p): c.get_token_distance(p) for p in (0, 10, 49)} == want["distance"]
+        assert c.get_stats() == want["stats"]
+    np.testing.assert_allclose(c._get_projection(64, 16), np.array(g["projection_64_16"]), rtol=0, atol=1e-7)
+    c.full_reset()
+    assert c.get_stats() == g["after_full_reset"]
