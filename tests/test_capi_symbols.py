@@ -55,3 +55,36 @@ def test_argument_errors_are_reported_without_gpu():
                                         0.5, None, 0, 0.1, 1, 8, 2, 96, 128, 1, None, None, None, 0, None)
     assert rc == 2  # head_dim 96 unsupported
     assert lib.kessie_page_evict_workspace_size(8192) >= 8192
+
+
+def test_index_query_and_tiered_cache_argument_errors_without_gpu():
+    """The index-query, tiered-update and strided-pack entry points reject bad
+    arguments (with a message) before any CUDA call; the fog-start argument of
+    the tiered update is a double, as the reference's int(S * fog_start) is."""
+    from kessie_b200 import _lib
+    lib = _lib.load()
+    ERR_ARG = 1                                   # KESSIE_ERR_ARG
+    # dim not a multiple of 4
+    assert lib.kessie_index_query_v2(16, 16, 100, 6, 1, None, 5, 16, 16, None, 0, None) == ERR_ARG
+    assert "dim" in _lib.last_error()[1]
+    # top_k above 32
+    assert lib.kessie_index_query_v2(16, 16, 100, 8, 1, None, 33, 16, 16, None, 0, None) == ERR_ARG
+    # misaligned index
+    assert lib.kessie_index_query_v2(16, 20, 100, 8, 1, 16, 0, None, None, None, 0, None) == ERR_ARG
+    assert "aligned" in _lib.last_error()[1]
+    # nothing requested
+    assert lib.kessie_index_query_v2(16, 16, 100, 8, 1, None, 0, None, None, None, 0, None) == ERR_ARG
+    # tiered update: hi + T beyond the store
+    assert lib.kessie_tiered_update_v2(16, 16, 100, 0, 99, 16, 16, 0, 0, 128, 1, 8, 2, 128, 1, None, 0.5, 0.5,
+                                       None) == ERR_ARG
+    assert "cap" in _lib.last_error()[1]
+    # head_dim * element size not a multiple of 16
+    assert lib.kessie_tiered_update_v2(16, 16, 100, 0, 10, 16, 16, 0, 0, 12, 1, 8, 1, 12, 0, None, 0.5, 0.5,
+                                       None) == ERR_ARG
+    # unaligned store
+    assert lib.kessie_tiered_update_v2(24, 16, 100, 0, 10, 16, 16, 0, 0, 128, 1, 8, 1, 128, 1, None, 0.5, 0.5,
+                                       None) == ERR_ARG
+    assert _lib.SIGNATURES["kessie_tiered_update_v2"][1][17] is ctypes.c_double
+    # strided pack: row bytes not a multiple of 16
+    assert lib.kessie_strided_pack_v2(16, 16, 2, 8, 10, 24, 16, 0, None) == ERR_ARG
+    assert lib.kessie_strided_pack_v2(None, 16, 2, 8, 10, 32, 16, 0, None) == ERR_ARG

@@ -258,3 +258,29 @@ def test_host_bookkeeping_matches_reference(golden_dir):
     np.testing.assert_allclose(c._get_projection(64, 16), np.array(g["projection_64_16"]), rtol=0, atol=1e-7)
     c.full_reset()
     assert c.get_stats() == g["after_full_reset"]
+
+
+def test_host_guards_without_gpu():
+    """The product path refuses CPU tensors instead of computing on the CPU;
+    an empty cache behaves as the reference's (length 0, eviction no-op,
+    recall miss); the ops wrappers check their buffers before launching."""
+    from kessie_b200 import ops
+    from kessie_b200.kessie_cache import KeSSieCache
+    from kessie_b200.vector_index import VectorIndex
+    c = KeSSieCache(window_size=8)
+    assert c.get_seq_length() == 0 and len(c) == 0
+    c.evict_if_needed()
+    assert c.recall_from_cpu(3, "cpu") is False
+    k = torch.zeros(1, 2, 4, 32, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        c.update(k, k, 0)
+    with pytest.raises(ValueError):
+        ops.tiered_update(k, k, 0, 0, k, k, None, 0.5, 0.5)
+    with pytest.raises(ValueError):
+        ops.index_query(torch.zeros(8), torch.zeros(4, 8))
+    vi = VectorIndex(dim=8)
+    assert vi.search(np.ones(8, np.float32)) == [] and vi.count == 0
+    vi.rebuild([], [])
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError):
+            vi.rebuild([np.ones(8, np.float32)], [1])
