@@ -74,7 +74,7 @@ def build(force: bool = False, jobs: int = 8, verbose: bool = False) -> str:
                     print(msg, file=sys.stderr)
     if todo or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
         tmp = LIB + ".tmp"
-        cmd = [NVCC] + ARCH + ["-shared", "-o", tmp] + objs + ["-lpthread"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", tmp] + objs + ["-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

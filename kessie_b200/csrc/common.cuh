@@ -9,6 +9,8 @@
 
 #include "../../include/kessie_capi.h"
 
+#include <nvtx3/nvToolsExt.h>
+
 namespace kessie {
 
 // ---------------------------------------------------------------- host errors
@@ -25,6 +27,18 @@ int* device_status_ptr();
 int sm_count();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Scoped NVTX range around a C-ABI entry point, so host-side timelines
+// (Nsight Systems, or any NVTX tool) show which library call launched what.
+// Header-only NVTX: without an attached tool each push / pop is one test of a
+// function pointer.
+class NvtxRange {
+  public:
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

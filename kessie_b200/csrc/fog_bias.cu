@@ -41,6 +41,7 @@ using namespace kessie;
 
 extern "C" int kessie_build_fog_bias_v2(void* out, int out_dtype, int kv_len, const kessie_fog_bias* bias,
                                         void* stream) {
+    NvtxRange nvtx_range("kessie_build_fog_bias_v2");
     if (!out || kv_len < 0) return set_error(KESSIE_ERR_ARG, "build_fog_bias_v2: bad arguments");
     if (!dtype_ok(out_dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "build_fog_bias_v2: dtype %d", out_dtype);
     FogBias f;

@@ -978,6 +978,7 @@ int decode_entry(const void* q, int64_t q_stride_b, int64_t q_stride_h, const vo
                  const float* fog_weights, int window_size, float sm_scale, int batch, int num_q_heads,
                  int num_kv_heads, int head_dim, int max_seq_len, int dtype, const kessie_fog_bias* bias, void* out,
                  float* out_partial, void* workspace, size_t workspace_bytes, int phases, void* stream) {
+    NvtxRange nvtx_range("kessie_paged_fog_decode");
     if (phases < 1 || phases > 3) return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: phases %d", phases);
     DecodeParams p;
     Plan pl;
@@ -1054,6 +1055,7 @@ namespace {
 int cp_combine(void* const* exchange_buffers, int rank, int world, uint32_t epoch, int64_t wait_timeout_ns, int batch,
                int num_q_heads, int num_kv_heads, int head_dim, int dtype, void* out, float* out_partial, void* stream,
                bool follows_decode) {
+    NvtxRange nvtx_range("kessie_cp_combine");
     if (world < 1 || world > kCpMaxRanks || rank < 0 || rank >= world || !exchange_buffers || !exchange_buffers[rank])
         return set_error(KESSIE_ERR_ARG, "cp_combine_v2: rank %d / world %d / buffers", rank, world);
     if (epoch == 0 || wait_timeout_ns <= 0) return set_error(KESSIE_ERR_ARG, "cp_combine_v2: epoch / timeout");
@@ -1135,6 +1137,7 @@ extern "C" int kessie_paged_fog_decode_cp_v2(
 
 extern "C" int kessie_lse_combine_v2(const float* partials, int num_splits, int64_t split_stride, int rows,
                                      int head_dim, void* out, int out_dtype, float* out_partial, void* stream) {
+    NvtxRange nvtx_range("kessie_lse_combine_v2");
     if (!partials || num_splits <= 0 || rows <= 0 || head_dim <= 0 || head_dim > 1024 || (!out && !out_partial))
         return set_error(KESSIE_ERR_ARG, "lse_combine_v2: bad arguments");
     if (!dtype_ok(out_dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "lse_combine_v2: dtype %d", out_dtype);
@@ -1204,6 +1207,7 @@ extern "C" int kessie_paged_fog_decode_noalloc_v2(
     const int32_t* q_positions, const int32_t* clear_start, float fog_alpha, const float* fog_weights,
     int window_size, float sm_scale, int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_seq_len,
     int dtype, void* out, float* out_partial, void* stream) {
+    NvtxRange nvtx_range("kessie_paged_fog_decode_noalloc_v2");
     if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_seq_len < 0)
         return set_error(KESSIE_ERR_ARG, "noalloc decode: bad sizes");
     const size_t need = kessie_paged_fog_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim,

@@ -440,6 +440,7 @@ extern "C" int kessie_fog_attention_v2(const void* q, const void* k, const void*
                                        const float* fog_weights, float sm_scale, int batch, int num_q_heads,
                                        int num_kv_heads, int seq_len, int head_dim, int window_size, int is_causal,
                                        void* stream) {
+    NvtxRange nvtx_range("kessie_fog_attention_v2");
     if (dtype != KESSIE_DTYPE_BF16 && dtype != KESSIE_DTYPE_F16)
         return set_error(KESSIE_ERR_UNSUPPORTED, "fog_attention_v2: dtype %d (f16/bf16 only)", dtype);
     if (head_dim != 64 && head_dim != 128)
@@ -475,6 +476,7 @@ int prefill_entry(
     int window_size, int is_causal, float sm_scale, int batch, int num_q_tokens, int num_q_heads, int num_kv_heads,
     int head_dim, int dtype, const kessie_fog_bias* bias, void* out, int64_t o_stride_b, int64_t o_stride_t,
     int64_t o_stride_h, int max_kv_len, void* workspace, size_t workspace_bytes, void* stream) {
+    NvtxRange nvtx_range("kessie_paged_fog_prefill");
     if (dtype != KESSIE_DTYPE_BF16 && dtype != KESSIE_DTYPE_F16)
         return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_prefill_v2: dtype %d (f16/bf16 only)", dtype);
     if (head_dim != 64 && head_dim != 128)

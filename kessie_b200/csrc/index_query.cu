@@ -270,6 +270,7 @@ extern "C" size_t kessie_index_query_workspace_size(int num_rows, int top_k) {
 extern "C" int kessie_index_query_v2(const float* query, const float* index, int num_rows, int dim,
                                      int normalize_rows, float* sims, int top_k, int32_t* top_idx, float* top_scores,
                                      void* workspace, size_t workspace_bytes, void* stream) {
+    NvtxRange nvtx_range("kessie_index_query_v2");
     if (!query || !index || num_rows <= 0 || dim <= 0 || dim % 4 || dim > (1 << 24) || top_k < 0 || top_k > kIqMaxK)
         return set_error(KESSIE_ERR_ARG, "index_query_v2: bad arguments (0 < dim <= 2^24, dim %% 4 == 0, 0 <= top_k <= %d)", kIqMaxK);
     if ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(index)) & 15)

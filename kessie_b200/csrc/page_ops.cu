@@ -940,6 +940,7 @@ void launch_kessie_rope_remap(void* k_data, const void* orig_positions, const vo
 int kessie_rope_remap_v2(void* k_data, int dtype, int num_tokens, int num_heads, int head_dim,
                          int64_t token_stride, int64_t head_stride, const int32_t* orig_positions,
                          const int32_t* target_positions, float rope_theta, void* stream) {
+    NvtxRange nvtx_range("kessie_rope_remap_v2");
     if (!dtype_ok(dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "rope_remap_v2: dtype %d", dtype);
     if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0 || (head_dim & 1) || head_dim / 2 > kMaxHalf)
         return set_error(KESSIE_ERR_ARG, "rope_remap_v2: bad shape T=%d H=%d D=%d", num_tokens, num_heads, head_dim);
@@ -972,12 +973,14 @@ size_t kessie_page_evict_workspace_size(int num_pages) { return num_pages > 0 ? 
 int kessie_page_evict_v2(int8_t* page_valid, const int32_t* page_positions, int8_t* page_allocated,
                          int num_pages, int evict_before_pos, int32_t* freed_count, int32_t* freed_ids,
                          void* workspace, size_t workspace_bytes, void* stream) {
+    NvtxRange nvtx_range("kessie_page_evict_v2");
     return run_compaction(page_valid, page_positions, page_allocated, num_pages, evict_before_pos, 0,
                           freed_count, freed_ids, workspace, workspace_bytes, as_stream(stream));
 }
 
 int kessie_page_list_valid_v2(const int8_t* page_valid, int num_pages, int32_t* count, int32_t* ids,
                               void* workspace, size_t workspace_bytes, void* stream) {
+    NvtxRange nvtx_range("kessie_page_list_valid_v2");
     return run_compaction(const_cast<int8_t*>(page_valid), nullptr, nullptr, num_pages, 0, 1, count, ids,
                           workspace, workspace_bytes, as_stream(stream));
 }
@@ -1009,6 +1012,7 @@ int kessie_page_insert_v2(void* kv_cache, int dtype, int64_t page_stride, int64_
                           int num_heads, int head_dim, const int32_t* target_page_ids, int8_t* page_valid,
                           int32_t* page_positions, int conv_pos, const int32_t* orig_positions,
                           const int32_t* target_positions, float rope_theta, void* stream) {
+    NvtxRange nvtx_range("kessie_page_insert_v2");
     if (!dtype_ok(dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "page_insert_v2: dtype %d", dtype);
     if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0 || page_size <= 0 || max_pages <= 0)
         return set_error(KESSIE_ERR_ARG, "page_insert_v2: bad shape");
@@ -1029,6 +1033,7 @@ int kessie_page_gather_v2(const void* kv_cache, int dtype, int64_t page_stride, 
                           int64_t kv_stride, int64_t head_stride, int max_pages, int page_size,
                           const int32_t* page_ids, int num_gather, int num_heads, int head_dim, void* out_keys,
                           void* out_values, void* stream) {
+    NvtxRange nvtx_range("kessie_page_gather_v2");
     if (!dtype_ok(dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "page_gather_v2: dtype %d", dtype);
     if (num_gather < 0 || num_heads <= 0 || head_dim <= 0 || page_size <= 0 || max_pages <= 0)
         return set_error(KESSIE_ERR_ARG, "page_gather_v2: bad shape");
@@ -1044,6 +1049,7 @@ int kessie_page_gather_v2(const void* kv_cache, int dtype, int64_t page_stride, 
 }
 
 int kessie_build_fog_weights_v2(float* out, int seq_len, int clear_start, float fog_alpha, void* stream) {
+    NvtxRange nvtx_range("kessie_build_fog_weights_v2");
     if (seq_len < 0 || (seq_len > 0 && !out)) return set_error(KESSIE_ERR_ARG, "build_fog_weights_v2: bad arguments");
     if (seq_len == 0) { clear_error(); return 0; }
     fog_weights_kernel<<<(seq_len + 255) / 256, 256, 0, as_stream(stream)>>>(out, seq_len, clear_start, fog_alpha);

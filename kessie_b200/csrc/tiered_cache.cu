@@ -173,6 +173,7 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
                                        const void* k_new, const void* v_new, long long new_stride_b,
                                        long long new_stride_h, long long new_stride_t, int B, int H, int T, int D,
                                        int dtype, void* v_fog, float fog_alpha, double fog_start, void* stream) {
+    NvtxRange nvtx_range("kessie_tiered_update_v2");
     if (!k_store || !v_store || !k_new || !v_new || B <= 0 || H <= 0 || T < 0 || D <= 0 || !dtype_ok(dtype) ||
         lo < 0 || hi < lo || cap < hi + T)
         return set_error(KESSIE_ERR_ARG, "tiered_update_v2: bad arguments (0 <= lo <= hi, hi + T <= cap)");
@@ -230,6 +231,7 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
 extern "C" int kessie_strided_pack_v2(const unsigned long long* store_bases, const long long* store_pitch_bytes,
                                       int num_stores, int rows_per_store, long long tokens, int row_bytes,
                                       void* staging, int unpack, void* stream) {
+    NvtxRange nvtx_range("kessie_strided_pack_v2");
     if (!store_bases || !store_pitch_bytes || !staging || num_stores <= 0 || rows_per_store <= 0 || tokens < 0 ||
         row_bytes <= 0 || row_bytes % 16 || !al16(staging))
         return set_error(KESSIE_ERR_ARG, "strided_pack_v2: bad arguments (row_bytes % 16 == 0, aligned staging)");
