@@ -260,3 +260,140 @@ def kessie_index_query(query_embed: torch.Tensor, index_embeds: torch.Tensor, to
     ids, scores, sims = ops.index_query(query_embed.float(), index_embeds.float(), top_k=max(top_k, 1),
                                         normalize_rows=True, return_sims=True)
     return (sims, ids, scores) if top_k > 0 else sims
+
+
+# ---------------------------------------------------------------------------
+# Self-test suite (kessie_hip_kernels.py:613-747): the same test names,
+# configurations and pass thresholds, run on this library's kernels against
+# the *_ref functions above.  Without a CUDA device every test logs SKIP and
+# passes, as the reference's does without Triton.
+# ---------------------------------------------------------------------------
+class KeSSieKernelTests:
+    WINDOWED_CONFIGS = [(1, 4, 128, 64, 0, True), (1, 4, 128, 64, 64, True),
+                        (1, 8, 256, 128, 128, True), (2, 8, 512, 128, 256, True)]
+
+    def __init__(self, device="cuda"):
+        self.device = torch.device(device) if torch.cuda.is_available() else torch.device("cpu")
+        if self.device.type == "cuda":
+            logger.info(f"GPU: {torch.cuda.get_device_name(self.device)}")
+
+    def _gpu(self) -> bool:
+        return self.device.type == "cuda"
+
+    def _rand(self, *shape):
+        return torch.randn(*shape, device=self.device, dtype=torch.float16)
+
+    def test_windowed_attention_correctness(self) -> bool:
+        logger.info("TEST: windowed attention vs kessie_windowed_attention_ref (max-abs < 0.05, fp16)")
+        ok = True
+        for Z, H, N, D, W, causal in self.WINDOWED_CONFIGS:
+            if not self._gpu():
+                logger.info(f"  Z={Z} H={H} N={N} D={D} W={W} | SKIP")
+                continue
+            q, k, v = self._rand(Z, H, N, D), self._rand(Z, H, N, D), self._rand(Z, H, N, D)
+            ref = kessie_windowed_attention_ref(q.float(), k.float(), v.float(), W, causal).half()
+            md = (ref - kessie_windowed_attention(q, k, v, W, causal)).abs().max().item()
+            passed = md < 0.05
+            ok &= passed
+            logger.info(f"  Z={Z} H={H} N={N} D={D} W={W} | max_diff={md:.6f} [{'PASS' if passed else 'FAIL'}]")
+        return ok
+
+    def test_fused_fog_attention(self) -> bool:
+        logger.info("TEST: fused fog attention vs kessie_fused_fog_attention_ref (max-abs < 0.1, fp16)")
+        if not self._gpu():
+            logger.info("  SKIP")
+            return True
+        Z, H, N, D = 1, 8, 512, 128
+        q, k, v = self._rand(Z, H, N, D), self._rand(Z, H, N, D), self._rand(Z, H, N, D)
+        fog = kessie_build_fog_weights(N, 0.5, 0.5, self.device)
+        ref = kessie_fused_fog_attention_ref(q.float(), k.float(), v.float(), fog).half()
+        md = (ref - kessie_fused_fog_attention(q, k, v, fog)).abs().max().item()
+        logger.info(f"  N={N} fog_alpha=0.5 | max_diff={md:.6f} [{'PASS' if md < 0.1 else 'FAIL'}]")
+        return md < 0.1
+
+    def test_rope_remap(self) -> bool:
+        logger.info("TEST: RoPE remap round trip 100 -> 5000 -> 100 (< 0.05) and identity (< 1e-5)")
+        if not self._gpu():
+            logger.info("  SKIP")
+            return True
+        L, H, D = 64, 8, 128
+        k = self._rand(L, H, D)
+        k0 = k.clone()
+        orig = torch.arange(100, 100 + L, dtype=torch.int32, device=self.device)
+        tgt = torch.arange(5000, 5000 + L, dtype=torch.int32, device=self.device)
+        kessie_rope_remap(k, orig, tgt)
+        kessie_rope_remap(k, tgt, orig)
+        md = (k0.float() - k.float()).abs().max().item()
+        k2 = self._rand(L, H, D)
+        k2o = k2.clone()
+        kessie_rope_remap(k2, orig, orig)
+        md2 = (k2o.float() - k2.float()).abs().max().item()
+        logger.info(f"  round trip max_diff={md:.6f} [{'PASS' if md < 0.05 else 'FAIL'}]  "
+                    f"identity max_diff={md2:.6f} [{'PASS' if md2 < 1e-5 else 'FAIL'}]")
+        return md < 0.05 and md2 < 1e-5
+
+    def test_paged_kv_cache(self) -> bool:
+        logger.info("TEST: paged KV cache insert 512 at position 0, evict before 5000")
+        if not self._gpu():
+            logger.info("  SKIP")
+            return True
+        cache = KeSSiePagedKVCache(64, 128, 2, 8, 64, self.device)
+        keys, vals = self._rand(512, 8, 64), self._rand(512, 8, 64)
+        ok = cache.insert_probe_kv(0, keys, vals, 0)
+        logger.info(f"  insert: {'OK' if ok else 'FAIL'}, active={cache.active_pages}")
+        freed = cache.evict_before(5000)
+        logger.info(f"  evict <5000: {freed} freed, active={cache.active_pages}")
+        return True
+
+    def bench_fused_vs_separate(self, seq_len=4096):
+        """Fog folded into V then windowed attention, against the fused kernel
+        (CUDA-event timings, 20 runs after 3 warm-ups)."""
+        logger.info(f"BENCH: fused vs separate fog (N={seq_len})")
+        if not self._gpu():
+            logger.info("  SKIP")
+            return None
+        Z, H, D = 1, 8, 128
+        q, k, v = self._rand(Z, H, seq_len, D), self._rand(Z, H, seq_len, D), self._rand(Z, H, seq_len, D)
+        fog = kessie_build_fog_weights(seq_len, 0.5, 0.5, self.device)
+
+        def timed(fn):
+            for _ in range(3):
+                fn()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(20):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / 20
+
+        t_sep = timed(lambda: kessie_windowed_attention(q, k, v * fog[None, None, :, None].to(v.dtype)))
+        t_fused = timed(lambda: kessie_fused_fog_attention(q, k, v, fog))
+        logger.info(f"  separate: {t_sep:.3f} ms | fused: {t_fused:.3f} ms | speedup: {t_sep / t_fused:.2f}x")
+        return t_sep, t_fused
+
+    def run_all(self) -> bool:
+        logger.info(f"KeSSie B200 kernel test suite (device {self.device})")
+        ok = self.test_windowed_attention_correctness()
+        ok &= self.test_fused_fog_attention()
+        ok &= self.test_rope_remap()
+        ok &= self.test_paged_kv_cache()
+        if self._gpu():
+            self.bench_fused_vs_separate()
+        logger.info("done")
+        return ok
+
+
+if __name__ == "__main__":
+    import argparse
+    logging.basicConfig(level=logging.INFO, format="%(message)s")
+    ap = argparse.ArgumentParser(description="KeSSie B200 kernel tests")
+    ap.add_argument("--device", default="cuda", choices=["cuda", "cpu"])
+    ap.add_argument("--test", default="all",
+                    choices=["all", "correctness", "fused-fog", "rope-remap", "bench-fog", "bench-paged"])
+    ap.add_argument("--seq-len", type=int, default=4096)
+    a = ap.parse_args()
+    t = KeSSieKernelTests(device=a.device)
+    {"all": t.run_all, "correctness": t.test_windowed_attention_correctness,
+     "fused-fog": t.test_fused_fog_attention, "rope-remap": t.test_rope_remap,
+     "bench-fog": lambda: t.bench_fused_vs_separate(a.seq_len), "bench-paged": t.test_paged_kv_cache}[a.test]()
