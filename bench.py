@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kessie|reference] [--workload NAME]
 
-Default workload (every N): BASELINE config 5, the 1M-token context-parallel
+Default workload (every N): benchmark config 5, the 1M-token context-parallel
 fog decode at the 70B attention shape -- batch 4, 64 query / 8 KV heads,
 head_dim 128, bf16 paged KV (page 16) of 1,048,576 tokens per sequence,
 window 8192 (clear_start = N - 8192, fog alpha 0.5).  The KV sequence is

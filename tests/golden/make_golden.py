@@ -137,7 +137,7 @@ def gen_attention():
 
 
 def gen_config1():
-    """B1 Hq8/Hkv2 D128 N4096 W512 fp32, RoPE theta 1e4 at
+    """Benchmark config 1: B1 Hq8/Hkv2 D128 N4096 W512 fp32, RoPE theta 1e4 at
     positions 0..4095, decode query = position 4095.  GQA by repeat_interleave.
     Two fog mappings: (a) causal + clear_start = N-W; (b) reference-literal
     window_size=W mask plus the same fog weights."""

@@ -8,7 +8,7 @@ from oracle import fog_oracle as O
 TORCH_DT = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 ROUND = {"bf16": O.round_bf16, "fp16": O.round_f16, "fp32": lambda x: np.asarray(x, np.float32)}
 
-# the bf16 / fp16 / fp32 parity bars stated in BASELINE.json's north_star
+# the bf16 / fp16 / fp32 parity bars of the target path (1e-4 fp32; 2e-2 abs / 1e-2 rel bf16, fp16)
 TOL = {"bf16": dict(atol=2e-2, rtol=1e-2), "fp16": dict(atol=2e-2, rtol=1e-2), "fp32": dict(atol=1e-4, rtol=0)}
 
 

@@ -148,7 +148,7 @@ def test_decode_context_parallel_shards_merge():
 
 
 def test_config1_golden_decode(golden_dir):
-    """BASELINE config 1 (fp32 in the reference) through the bf16/fp16 kernel:
+    """Benchmark config 1 (fp32 in the reference) through the bf16/fp16 kernel:
     the inputs are rounded to fp16 and compared with the stated fp16 bar; the
     oracle at the same rounded inputs is checked at the tighter 5e-3."""
     from kessie_b200 import ops
