@@ -197,8 +197,9 @@ __global__ void __launch_bounds__(kPThreads, 1) fog_prefill_kernel(const __grid_
 
     for (int it = 0; it < n_tiles; ++it) {
         const int s = it % kPST;
-        if (!ptx::mbar_wait(&full[s], (uint32_t)(it / kPST) & 1u)) {
-            record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+        // warp-uniform: the ldmatrix / mma.sync below are warp-collective
+        if (!__all_sync(0xffffffffu, ptx::mbar_wait(&full[s], (uint32_t)(it / kPST) & 1u))) {
+            if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
             break;
         }
         const int j0 = (tile_lo + it) * kBN;

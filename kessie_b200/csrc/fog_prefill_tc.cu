@@ -231,7 +231,9 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         const uint32_t idS = ptx::umma_idesc_f16(BF16, false, 128);
         const uint32_t idPV = ptx::umma_idesc_f16(BF16, true, 128);
         const uint32_t qa = ptx::smem_u32(smem + L::kQ);
-        bool ok = n_tiles > 0 && ptx::mbar_wait(q_full, 0);
+        // every wait result below is made warp-uniform (__all_sync) before it
+        // steers control flow: the issue lambdas end in __syncwarp
+        bool ok = n_tiles > 0 && __all_sync(0xffffffffu, ptx::mbar_wait(q_full, 0));
         ptx::tc_fence_after();
         auto issue_s = [&](int t, int x) {
             const uint32_t kb = ptx::smem_u32(smem + L::kK + (t % kNK) * L::kTile);
@@ -264,13 +266,13 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
             __syncwarp();
         };
         if (ok) {
-            ok = ptx::mbar_wait(&k_full[0], 0);
+            ok = __all_sync(0xffffffffu, ptx::mbar_wait(&k_full[0], 0));
             ptx::tc_fence_after();
             if (ok) { issue_s(0, 0); issue_s(0, 1); }
         }
         for (int t = 0; ok && t < n_tiles; ++t) {
             const bool more = t + 1 < n_tiles;
-            if (!ptx::mbar_wait(&v_full[t % kNV], (uint32_t)(t / kNV) & 1u)) { ok = false; break; }
+            if (!__all_sync(0xffffffffu, ptx::mbar_wait(&v_full[t % kNV], (uint32_t)(t / kNV) & 1u))) { ok = false; break; }
             if (!a.dense && (tile_lo + t) * 128 + 128 > kv_len) {
                 // stale slots past kv_len in the last page: zero their V rows so
                 // 0 * (stale NaN) cannot reach O
@@ -283,9 +285,12 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 ptx::fence_proxy_async_smem();
                 __syncwarp();
             }
-            if (more && !ptx::mbar_wait(&k_full[(t + 1) % kNK], (uint32_t)((t + 1) / kNK) & 1u)) { ok = false; break; }
+            if (more && !__all_sync(0xffffffffu, ptx::mbar_wait(&k_full[(t + 1) % kNK], (uint32_t)((t + 1) / kNK) & 1u))) {
+                ok = false;
+                break;
+            }
             for (int x = 0; x < 2; ++x) {
-                if (!ptx::mbar_wait(&p_full[x], (uint32_t)t & 1u)) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, ptx::mbar_wait(&p_full[x], (uint32_t)t & 1u))) { ok = false; break; }
                 ptx::tc_fence_after();
                 issue_pv(t, x);
                 if (more) issue_s(t + 1, x);
@@ -352,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 reinterpret_cast<float4*>(bbuf)[lane] = b4v;
             }
             __syncwarp();
-            if (!ptx::mbar_wait(&s_full[x], (uint32_t)j & 1u)) { ok = false; break; }
+            // warp-uniform: the tcgen05.ld / st below are warp-collective
+            if (!__all_sync(0xffffffffu, ptx::mbar_wait(&s_full[x], (uint32_t)j & 1u))) { ok = false; break; }
             ptx::tc_fence_after();
             uint32_t sv[4][32];
 #pragma unroll
@@ -438,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
         // ---- epilogue: O / l -> global
         bool have = n_tiles > 0 && ok;
         if (have) {
-            have = ptx::mbar_wait(&o_bar[x], (uint32_t)(n_tiles - 1) & 1u);
+            have = __all_sync(0xffffffffu, ptx::mbar_wait(&o_bar[x], (uint32_t)(n_tiles - 1) & 1u));
             ptx::tc_fence_after();
         }
         if (!ok || (n_tiles > 0 && !have)) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
