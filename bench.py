@@ -694,7 +694,24 @@ def measure_aux(workload, steps, warmup=3):
                 for _ in range(args.steps):
                     vi.search(qh, top_k=5)
                 res[tag + "_search_e2e_us"] = (time.perf_counter() - t0) / args.steps * 1e6
-                del vi, xh
+                # CPU baseline: the reference's own numpy search (fp32 matvec over
+                # the normalised rows + full argsort) on the host cores, ~1 s
+                from oracle import fog_oracle as O
+                rows = O.vector_index_rows(xh)
+                reps, t0 = 0, time.perf_counter()
+                while time.perf_counter() - t0 < 1.0:
+                    O.vector_index_search_fp32(rows, qh, 5)
+                    reps += 1
+                cpu_us = (time.perf_counter() - t0) / reps * 1e6
+                try:
+                    from threadpoolctl import threadpool_info
+                    cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+                except Exception:
+                    cores = os.cpu_count() or 1
+                res["cpu_baseline"] = {"value": cpu_us, "unit": "us per query", "cores": cores, "kind": "port",
+                                       "sample": "VectorIndex.search numpy path (kessie_exp3.py:89-103), 78,125 x "
+                                                 f"256 fp32 rows, top-5, {reps} queries"}
+                del vi, xh, rows
             del x
         res.update(hbm_peak=hbm, note="top-5 over fp32 rows, normalize_rows=1; cold = 256 MB read (L2 flush) before each "
                                       "launch pair (query + merge); warm = back-to-back calls, index resident in L2 (n78125 only fits); "

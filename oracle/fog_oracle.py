@@ -508,3 +508,20 @@ def index_query(query: np.ndarray, index: np.ndarray, normalize_rows: bool = Tru
     sims = x @ qn
     order = np.lexsort((np.arange(len(sims)), -sims))[:top_k]
     return sims, order, sims[order]
+
+
+def vector_index_search_fp32(rows: np.ndarray, query: np.ndarray, top_k: int = 5):
+    """VectorIndex.search's numpy path (kessie_exp3.py:89-103) in float32, as
+    the reference runs it: the query divided by its norm (empty result below
+    1e-8), sims = rows @ q over the stored normalised rows, the k = min(top_k,
+    rows) largest by a full argsort, best first.  The timed CPU baseline of the
+    index query; returns (ids, scores)."""
+    q = np.asarray(query, dtype=np.float32).reshape(1, -1)
+    qn = np.linalg.norm(q)
+    if qn < 1e-8 or len(rows) == 0:
+        return np.zeros(0, np.int64), np.zeros(0, np.float32)
+    q = q / qn
+    sims = (rows @ q.T).ravel()
+    k = min(top_k, len(sims))
+    idx = np.argsort(sims)[-k:][::-1]
+    return idx, sims[idx]

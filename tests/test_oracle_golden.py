@@ -227,3 +227,19 @@ def test_index_query_matches_vector_index(golden_dir):
         np.testing.assert_array_equal(ids, d[f"q{qi}_ids"])
         np.testing.assert_allclose(scores, d[f"q{qi}_scores"], rtol=1e-5, atol=1e-6)
     assert int(d["tiny_query_result_len"]) == 0      # VectorIndex returns nothing for a ~zero query
+
+
+def test_vector_index_search_fp32_reproduces_reference(golden_dir):
+    """The timed CPU baseline of the index query is the reference's own numpy
+    search: same ids and scores as the recorded VectorIndex.search results."""
+    d = np.load(os.path.join(golden_dir, "index_query.npz"))
+    n, dim, seed = (int(v) for v in d["cfg"])
+    mat = np.random.default_rng(seed).standard_normal((n, dim), dtype=np.float32)
+    mat[7] = 0.0
+    rows = O.vector_index_rows(mat)
+    for qi in range(3):
+        q = np.random.default_rng(seed + 1 + qi).standard_normal((dim,), dtype=np.float32)
+        ids, scores = O.vector_index_search_fp32(rows, q, 10)
+        np.testing.assert_array_equal(ids, d[f"q{qi}_ids"])
+        np.testing.assert_allclose(scores, d[f"q{qi}_scores"], rtol=1e-6)
+    assert len(O.vector_index_search_fp32(rows, np.full(dim, 1e-12, np.float32), 10)[0]) == int(d["tiny_query_result_len"])
