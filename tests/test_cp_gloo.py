@@ -2,7 +2,7 @@
 shard-partial -> all-gather -> log-sum-exp merge decomposition that
 kessie_b200.context_parallel runs on NCCL, and failure handling when a rank
 dies before the exchange.  No GPU is used: per-rank partials come from the
-oracle, the exchange is a real 2-rank gloo all-gather."""
+oracle, the exchange is a real 2- or 4-rank gloo all-gather."""
 
 import os
 import socket
@@ -59,7 +59,11 @@ def _rank_main(rank, world, port, q, k, v, cs, out_q):
     dist.destroy_process_group()
 
 
-def test_two_rank_gloo_merge_equals_unsplit():
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_merge_equals_unsplit(world):
+    """world ranks each attend over their page-aligned shard of 1000 keys
+    (uneven at 4 ranks), all-gather the (m, l, o) partials and merge them;
+    every rank gets the unsplit attention."""
     rng = np.random.default_rng(0)
     Hq, Hkv, D, N = 8, 2, 64, 1000
     q = rng.standard_normal((Hq, 1, D)); k = rng.standard_normal((Hkv, N, D)); v = rng.standard_normal((Hkv, N, D))
@@ -68,14 +72,14 @@ def test_two_rank_gloo_merge_equals_unsplit():
     ctx = mp.get_context("spawn")
     out_q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, k, v, cs, out_q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, k, v, cs, out_q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(out_q.get(timeout=120) for _ in range(2))
+    res = dict(out_q.get(timeout=120) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for r in range(2):
+    for r in range(world):
         np.testing.assert_allclose(res[r], want, atol=1e-6)
 
 
