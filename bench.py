@@ -231,6 +231,23 @@ def cpu_decode_sample(seconds=10.0, tokens=131072, max_seconds=30.0, seed=0):
                       f"(oracle.fog_decode_group_fp32), {reps} reps in {el:.1f} s; GB/s of bf16-equivalent KV")
 
 
+def _cpu_rate(fn, seconds=1.0):
+    """Mean wall time of fn on the host over about `seconds`, and the BLAS
+    thread count it ran with."""
+    fn()
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        fn()
+        reps += 1
+    per = (time.perf_counter() - t0) / reps
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:
+        cores = os.cpu_count() or 1
+    return per, reps, cores
+
+
 def reference_arm(args):
     rank, world, _ = env_rank()
     if rank != 0:
@@ -661,6 +678,20 @@ def measure_aux(workload, steps, warmup=3):
         ms_e = timeit(ev_step, args.steps)
         res.update(l2="one-launch timings: 256 MB read (L2 flush) before each; b2b: 8 layer caches back to back",
                    evicted=n, evict_plus_refill_us=ms_e * 1e3, hbm_peak=hbm, layers=L)
+        # CPU baseline: the oracle port of the same ops on the host (bounded samples)
+        from oracle import fog_oracle as O
+        rng = np.random.default_rng(5)
+        pages = rng.integers(0, 65535, size=(2048, ps, 2, H, D), dtype=np.uint16)   # raw bf16 storage
+        order = rng.permutation(2048)
+        t_g, r_g, cores = _cpu_rate(lambda: O.page_gather(pages, order))
+        kk = rng.standard_normal((4096, H, D), dtype=np.float32)
+        p0 = np.arange(4096, dtype=np.int64)
+        t_r, r_r, _ = _cpu_rate(lambda: O.rope_remap(kk, p0, p0 + 131072, 500000.0))
+        res["cpu_baseline"] = {"gather_GBs": 2 * pages.nbytes / t_g / 1e9, "remap_GBs": 4096 * H * D * 4 / t_r / 1e9,
+                               "unit": "GB/s (bf16-equivalent bytes read + written)", "cores": cores, "kind": "port",
+                               "sample": f"oracle.page_gather of 2,048 pages ({r_g} reps), oracle.rope_remap of "
+                                         f"4,096 tokens x {H} heads x {D} ({r_r} reps)"}
+        del pages, kk
     elif args.workload == "index_query":
         # Conversation-index query (fp32 cosine similarity + top-5): the
         # reference index shape (78,125 rows x 256, 80 MB: under L2, so timed
@@ -843,6 +874,20 @@ def measure_aux(workload, steps, warmup=3):
         flops = 4 * D * Hq * (T * (Nk - T) + T * (T + 1) // 2)
         res.update(ms=ms, tflops=flops / ms / 1e9, frac_of_bf16_peak=flops / ms / 1e9 / tf, flops=flops,
                    peak_tflops=tf, peak_source=f"{peak_src} bf16_tflops (burst; one launch per timing)")
+        if args.workload == "prefill":
+            # CPU baseline: the fp32 GEMM port (oracle.fog_decode_group_fp32) on the
+            # dominant work of config 4 -- chunk queries over prefix keys with fog
+            from oracle import fog_oracle as O
+            rng = np.random.default_rng(6)
+            Gs, Ts, Ns = Hq // Hkv, 64, 16384
+            qs = rng.standard_normal((Gs * Ts, D), dtype=np.float32)
+            ks = rng.standard_normal((Ns, D), dtype=np.float32)
+            vs = rng.standard_normal((Ns, D), dtype=np.float32)
+            ws = O.fog_weights_from_clear_start(Ns, Ns - 4096, 0.5)
+            t_c, r_c, cores = _cpu_rate(lambda: O.fog_decode_group_fp32(qs, ks, vs, ws))
+            res["cpu_baseline"] = {"value": 4 * D * Gs * Ts * Ns / t_c / 1e12, "unit": "TFLOP/s", "cores": cores,
+                                   "kind": "port", "sample": f"{Gs * Ts} query rows x {Ns} keys x {D}, fp32 numpy "
+                                                             f"GEMM port with fog ({r_c} reps)"}
     return res
 
 
