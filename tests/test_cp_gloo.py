@@ -40,7 +40,7 @@ def test_shard_ranges_cover_sequence_page_aligned():
 def _rank_main(rank, world, port, q, k, v, cs, out_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     from datetime import timedelta
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     N = k.shape[1]
     a, b = shard_range(N, rank, world, 16)
     w = O.fog_weights_from_clear_start(N, cs, 0.5)
@@ -86,14 +86,17 @@ def test_gloo_merge_equals_unsplit(world):
 def _dying_rank(rank, world, port, out_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     from datetime import timedelta
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=4))
+    # Rendezvous gets a long limit (spawned interpreters start slowly on a busy
+    # host); the step's collectives run in a group with a short one.
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    step_group = dist.new_group(timeout=timedelta(seconds=4))
     if rank == 1:
         os._exit(3)                     # dies between steps, before the exchange
     t0 = time.time()
     try:
         x = torch.zeros(4)
         out = torch.empty(8)
-        dist.all_gather_into_tensor(out, x)
+        dist.all_gather_into_tensor(out, x, group=step_group)
         out_q.put(("no-error", time.time() - t0))
     except Exception as e:               # the survivor learns of it through the collective
         out_q.put(("error", time.time() - t0, type(e).__name__))
