@@ -41,6 +41,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_NOTE = "KV working set far above the 126 MB L2; no flush between steps"
+# One metric string for both arms (this library and --impl reference), so the
+# two JSON lines compare directly.
+METRIC = "fog-attn decode HBM GB/s (1M ctx, 70B shape)"
 
 
 def parse():
@@ -273,16 +276,15 @@ def reference_arm(args):
     per = el / args.steps
     gbs = tokens * D * 2 * 2 / per / 1e9
     c = CFG5
-    total_bytes = c["batch"] * c["ctx"] * c["kv_heads"] * c["head_dim"] * 4
-    ms_full = total_bytes / (gbs * 1e9) * 1e3
-    sample = (f"each step: 1 KV-head group (8 q heads) x {tokens} keys of the config-5 decode, fp32 numpy GEMM "
-              f"port of kessie_hip_kernels.py:577-593 (oracle.fog_decode_group_fp32); full-step time extrapolated "
-              f"by bytes")
-    line = {"impl": "reference", "metric": "fog-attn decode HBM GB/s (1M ctx, 70B shape)", "value": round(gbs, 3),
+    sample = (f"one step = 1 KV-head group (8 q heads, GQA) x {tokens} keys of the config-5 decode "
+              f"(fog at clear_start = N - 8192), fp32 numpy GEMM port of kessie_hip_kernels.py:577-593 "
+              f"(oracle.fog_decode_group_fp32); GB/s of bf16-equivalent KV bytes")
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3),
             "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_full, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "cp_decode_1m (BASELINE config 5)", **c, "parallelism": "host cores"},
+            "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded N(0,1) q/k/v)",
+            "config": {"workload": "cp_decode_1m (BASELINE config 5)", **c, "parallelism": "host cores",
+                       "sample_tokens_per_step": tokens, "sample_kv_heads_per_step": 1},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -370,27 +372,37 @@ def run_cp_decode(args):
     time.sleep(0.15)
     if world > 1:
         dist.barrier()
+    # At N = 1 a step is one decode launch, so an event at every step boundary
+    # inside the timed loop gives the kernel's own duration at no cost.  At
+    # N > 1 an event between the decode and its programmatic-dependent combine
+    # would stop their overlap, so the timed loop has none and the decode is
+    # timed alone in a loop of the same step right after it.
+    step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)] if world == 1 else None
     torch.cuda.synchronize()
     t_start.record()
     for i in range(K):
+        if step_ev is not None:
+            step_ev[i].record()
         step()
+    if step_ev is not None:
+        step_ev[K].record()
     t_end.record()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    # decode-kernel duration for the roofline: CUDA events around each decode
-    # launch, same workload, right after the timed region (clocks still sampled)
-    Kk = max(10, K // 2)
-    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
-    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
-    for i in range(Kk):
-        step_split(ev_a, ev_b, i)
-    torch.cuda.synchronize()
-    if world > 1:
+    if step_ev is None:
+        Kk = max(10, K // 2)
+        ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
+        ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
+        for i in range(Kk):
+            step_split(ev_a, ev_b, i)
+        torch.cuda.synchronize()
         dist.barrier()
+        kern_ms = sum(ev_a[i].elapsed_time(ev_b[i]) for i in range(Kk)) / Kk
+    else:
+        kern_ms = sum(step_ev[i].elapsed_time(step_ev[i + 1]) for i in range(K)) / K
     clocks.stop()
     el_ms = t_start.elapsed_time(t_end)
-    kern_ms = sum(ev_a[i].elapsed_time(ev_b[i]) for i in range(Kk)) / Kk
     t = torch.tensor([el_ms, kern_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -450,7 +462,9 @@ def run_cp_decode(args):
                 "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "peak_source": f"{peak_src} hbm_gbs (copy, burst)",
                 "algorithmic_bytes_per_launch": local_bytes, "kernel_ms": round(kern_ms, 4),
-                "kernel_timing": ("CUDA events around each decode launch (max over ranks), in a loop of the same "
+                "kernel_timing": ("CUDA events at every step boundary of the timed loop (N=1: a step is one "
+                                  "decode launch)" if world == 1 else
+                                  "CUDA events around each decode launch (max over ranks), in a loop of the same "
                                   "step right after the timed region"),
                 "traffic": (int(tr * local_bytes) if tr else None)}
         cpu = None
@@ -458,7 +472,7 @@ def run_cp_decode(args):
             gbs, per, sample = cpu_decode_sample()
             cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
                    "sample": sample}
-        line = {"metric": "fog-attn decode HBM GB/s (1M ctx, 70B shape; per-step us in ms_per_step)",
+        line = {"metric": METRIC,
                 "value": round(total_bytes / (ms_step / 1e3) / 1e9, 3), "unit": "GB/s", "n_gpus": world,
                 "steps": K, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4),
                 "us_per_step": round(ms_step * 1e3, 1), "higher_is_better": True, "scaling": "strong",
@@ -484,18 +498,61 @@ def run_cp_decode(args):
                 r.pop("workload", None)
                 sec[wl] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}
                 torch.cuda.empty_cache()
-            line["secondary"] = sec
-            line["secondary_note"] = ("other north_star configs, same process, CUDA-event timed: decode_128k/cfg3 = "
-                                      "config 3 (GB/s vs hbm peak), vllm_fog_decode = config 3 through the vLLM "
-                                      "attention mirror with the fog bias, page_ops = config 2, prefill = config 4 "
-                                      "(TFLOP/s), index_query = conversation-index top-5 (GB/s vs hbm peak), "
-                                      "tiered_cache = HF tiered-cache decode step over 32 layers (GB/s vs hbm peak)")
+            # full figures on stderr (logs); a compact summary closes the stdout line
+            print(json.dumps({"secondary_full": sec}), file=sys.stderr, flush=True)
+            line["secondary"] = compact_secondary(sec)
         print(json.dumps(line), flush=True)
     if world > 1:
         dec.close()                       # collective: barrier, then unmap / free the exchange buffers
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def _sig(x, n=3):
+    """x rounded to n significant figures, or to an integer when it has more
+    integer digits than that."""
+    if x is None or isinstance(x, (bool, int, str)):
+        return x
+    if x == 0 or not math.isfinite(x):
+        return x
+    nd = n - 1 - int(math.floor(math.log10(abs(x))))
+    return int(round(x)) if nd <= 0 else round(x, nd)
+
+
+def compact_secondary(sec):
+    """The other benchmark configs in a few hundred characters, so that the
+    whole summary survives a reader that keeps only the end of stdout:
+    decode configs first (us per step, GB/s, fraction of the HBM peak), then
+    page ops (back-to-back fraction of the HBM peak), prefill (ms, TFLOP/s,
+    fraction of the bf16 peak), the index query and the tiered cache, then
+    the CPU-port baselines."""
+    out = {}
+    for k in ("decode_128k", "decode_cfg3", "vllm_fog_decode", "decode_f32_cfg1"):
+        r = sec.get(k)
+        if r:
+            out[k] = {"us": _sig(r.get("us_per_step")), "GBs": _sig(r.get("GBs")), "frac": _sig(r.get("frac_of_hbm"))}
+    r = sec.get("page_ops")
+    if r:
+        out["page_ops_b2b_frac"] = {n: _sig(r.get(n + "_b2b_frac")) for n in ("gather", "remap", "insert_remap")}
+    r = sec.get("prefill")
+    if r:
+        out["prefill"] = {"ms": _sig(r.get("ms")), "TFs": _sig(r.get("tflops")), "frac": _sig(r.get("frac_of_bf16_peak"))}
+    r = sec.get("index_query")
+    if r:
+        out["index_query"] = {"1M_frac": _sig(r.get("n1000000_topk_frac")), "78k_us": _sig(r.get("n78125_topk_us"))}
+    r = sec.get("tiered_cache")
+    if r:
+        out["tiered_cache"] = {"step_ms": _sig(r.get("step_ms")), "frac": _sig(r.get("frac_of_hbm")),
+                               "x_ref_ops": _sig(r.get("speedup_vs_reference_ops"))}
+    cpu = {}
+    for k, f in (("page_ops", "gather_GBs"), ("page_ops", "remap_GBs"), ("prefill", "value"), ("index_query", "value")):
+        cb = (sec.get(k) or {}).get("cpu_baseline") or {}
+        if f in cb:
+            cpu[k + ("_" + f if k == "page_ops" else "")] = _sig(cb[f])
+    if cpu:
+        out["cpu_port"] = cpu
+    return out
 
 
 def run_aux_workload(args):

@@ -26,7 +26,7 @@ OUT = os.path.join(HERE, "build")
 LIB = os.path.join(OUT, "libkessie_cuda.so")
 LEGACY = os.path.join(OUT, "libkessie_hip.so")
 
-SOURCES = ["status.cu", "page_ops.cu", "fog_decode.cu", "cp_exchange.cu", "fog_bias.cu", "index_query.cu", "tiered_cache.cu", "fog_prefill.cu", "fog_prefill_tc.cu"]
+SOURCES = ["status.cu", "page_ops.cu", "fog_decode.cu", "fog_decode_f32.cu", "cp_exchange.cu", "fog_bias.cu", "index_query.cu", "tiered_cache.cu", "fog_prefill.cu", "fog_prefill_tc.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "-I" + os.path.join(ROOT, "include"),

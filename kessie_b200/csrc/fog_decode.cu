@@ -49,6 +49,7 @@
 //           per step, no collective library call.
 #include "common.cuh"
 #include "cp_layout.cuh"
+#include "decode_f32.cuh"
 #include "fog_bias.cuh"
 #include "ptx.cuh"
 #include "tma_host.cuh"
@@ -893,8 +894,7 @@ int prepare_decode(DecodeParams& p, Plan& pl, const void* q, int64_t q_stride_b,
                    const float* fog_weights, int window_size, float sm_scale, int batch, int num_q_heads,
                    int num_kv_heads, int head_dim, int max_seq_len, int dtype, void* workspace,
                    size_t workspace_bytes) {
-    if (dtype != KESSIE_DTYPE_BF16 && dtype != KESSIE_DTYPE_F16)
-        return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_v2: dtype %d (f16/bf16 only)", dtype);
+    if (!dtype_ok(dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_v2: dtype %d", dtype);
     if (head_dim != 64 && head_dim != 128)
         return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_v2: head_dim %d (64/128 only)", head_dim);
     if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads)
@@ -907,7 +907,8 @@ int prepare_decode(DecodeParams& p, Plan& pl, const void* q, int64_t q_stride_b,
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: null pointer or bad size");
     if ((q_stride_h & 1) || (q_stride_b & 1) || (reinterpret_cast<uintptr_t>(q) & 3))
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: q rows must be 4-byte aligned");
-    if (((token_stride | head_stride | page_stride) & 7) || (reinterpret_cast<uintptr_t>(k_cache) & 15) ||
+    const int64_t vec = dtype == KESSIE_DTYPE_F32 ? 3 : 7;      // elements per 16 bytes, minus one
+    if (((token_stride | head_stride | page_stride) & vec) || (reinterpret_cast<uintptr_t>(k_cache) & 15) ||
         (reinterpret_cast<uintptr_t>(v_cache) & 15))
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: cache strides/base must be 16-byte multiples");
     pl = make_plan(batch, num_q_heads, num_kv_heads, head_dim, max_seq_len);
@@ -992,7 +993,23 @@ int decode_entry(const void* q, int64_t q_stride_b, int64_t q_stride_h, const vo
     if (!out && !out_partial) return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: no output");
     if ((reinterpret_cast<uintptr_t>(out) & 7) || (reinterpret_cast<uintptr_t>(out_partial) & 7))
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: outputs must be 8-byte aligned");
+    if (dtype == KESSIE_DTYPE_F32 && p.bias.on)
+        return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_v2: the additive fog bias needs f16/bf16");
     if (!(phases & 1)) { clear_error(); return 0; }      // the merge runs inside the decode kernel
+    if (dtype == KESSIE_DTYPE_F32) {
+        DecodeF32Args a{};
+        a.q = static_cast<const float*>(q); a.q_sb = q_stride_b; a.q_sh = q_stride_h;
+        a.k_cache = static_cast<const float*>(k_cache); a.v_cache = static_cast<const float*>(v_cache);
+        a.page_stride = page_stride; a.token_stride = token_stride; a.head_stride = head_stride;
+        a.num_pages = num_pages; a.page_size = page_size;
+        a.block_table = block_table; a.bt_stride = block_table_stride;
+        a.seq_lens = seq_lens; a.kv_off = kv_pos_offset; a.q_pos = q_positions; a.clear_start = clear_start;
+        a.fog_alpha = fog_alpha; a.fog_w = fog_weights; a.window = window_size; a.sm_scale = sm_scale;
+        a.B = batch; a.Hq = num_q_heads; a.Hkv = num_kv_heads; a.D = head_dim; a.max_seq_len = pl.max_units * 16;
+        a.counters = p.counters; a.tag = p.tag; a.part_ml = p.part_ml; a.part_o = p.part_o; a.slots = pl.slots;
+        a.out = static_cast<float*>(out); a.out_part = out_partial; a.status = p.status;
+        return launch_decode_f32(a, as_stream(stream));
+    }
     p.out = out;
     p.out_part = out_partial;
     p.cp.world = 0;
@@ -1109,6 +1126,8 @@ extern "C" int kessie_paged_fog_decode_cp_v2(
         if (!exchange_buffers[r] || (reinterpret_cast<uintptr_t>(exchange_buffers[r]) & 255))
             return set_error(KESSIE_ERR_ARG, "paged_fog_decode_cp_v2: exchange buffer %d null or not 256-byte aligned", r);
     if ((phases & 2) && !out && !out_partial) return set_error(KESSIE_ERR_ARG, "paged_fog_decode_cp_v2: no output");
+    if (dtype == KESSIE_DTYPE_F32)
+        return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode_cp_v2: dtype f32 (f16/bf16 only)");
     DecodeParams p;
     Plan pl;
     int rc = prepare_decode(p, pl, q, q_stride_b, q_stride_h, k_cache, v_cache, page_stride, token_stride, head_stride,

@@ -1,0 +1,495 @@
+// fog_decode_f32.cu -- paged fog-attention decode in fp32 on the CUDA cores.
+//
+// Semantics are those of the bf16/fp16 decode (fog_decode.cu) and of the
+// reference's fp32 path, kessie_fused_fog_attention_ref
+// (kessie_hip_kernels.py:577-593) at one query row per sequence:
+//     O = sum_j p_j w_j v_j / sum_j p_j,  p_j = exp(q.k_j * sm_scale - m),
+// over the visible keys (j <= q_pos; q_pos - j < W when W > 0), with the fog
+// weight w_j = (j / max(cs-1, 1))^alpha for j < cs (kessie_hip_kernels.py:408-412)
+// evaluated with an IEEE divide and powf (sqrtf for alpha 0.5), as the
+// reference's fp32 torch ops do.  Every product and sum is fp32; no tensor
+// core is involved (tf32 would miss the 1e-4 fp32 bar).
+//
+// Design (B200): decode reads 1 KB of K+V per key (D 128) and does 4 FLOP per
+// byte, so it is HBM-bound as long as the FMA work per key stays below the
+// issue budget.
+//   grid  = (S splits, B*Hkv groups); the visible keys of a group are cut into
+//           8-key chunks (a chunk never crosses a page: page_size % 16 == 0)
+//           and split S ways; S is chosen from the SM count, at least two
+//           chunks per warp.
+//   CTA   = 8 warps.  Each warp streams every 8th chunk of the CTA's range
+//           through its own 3-stage ring of 16-byte cp.async copies (8 KB of
+//           K+V per stage at D 128), so two chunks per warp are in flight
+//           while it computes the third.  K lands 16-byte swizzled
+//           (chunk x of row r at x ^ (r & 7)) so the score loop reads it
+//           without bank conflicts; V lands row-major.
+//   QK    = lane (key kk = lane/4, quarter dq = lane%4) dots its quarter row of
+//           K with every query head of the group (q staged once per CTA in
+//           shared memory, pre-scaled by sm_scale*log2e, swizzled so the four
+//           quarters read distinct banks); a two-step transposing shuffle
+//           reduction over the quarters leaves each lane the full scores of
+//           GP/4 heads of its key.
+//   soft  = online softmax per head across the chunk's 8 keys (xor shuffles
+//           over the key lanes), running (m, l) per lane; p*w and the rescale
+//           factors go to a per-warp shared tile.
+//   PV    = lane owns D/32 consecutive dims of O for every head; per visible
+//           key: one V load and GP*D/32 FMAs.
+//   merge = the 8 warps merge through shared memory; with S > 1 each CTA
+//           writes (O/l, m, l) per head into its workspace slot and bumps the
+//           group's tagged arrival counter; the last CTA merges the S slots
+//           and writes out / out_partial (and zeroes the counter).
+#include "decode_f32.cuh"
+
+#include <math.h>
+
+namespace kessie {
+namespace {
+
+constexpr int kW = 8;            // warps per CTA
+constexpr int kT = kW * 32;
+constexpr int kNS = 3;           // cp.async stages per warp
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr unsigned kFull = 0xffffffffu;
+
+template <int D, int GP>
+struct F32Layout {
+    static constexpr int kChunk = 8 * D;                     // floats of one 8-key K (or V) slice
+    static constexpr int kStage = 2 * kChunk;
+    static constexpr int kWarpF = kNS * kStage + 8 * GP + GP;   // stages, P tile [8][GP], alpha [GP]
+    static constexpr int kWarpOff = GP * D;                  // after the staged q [GP][D]
+    static constexpr int kTailOff = kWarpOff + kW * kWarpF;  // merged (M, L) [GP][2], warp scales [kW][GP]
+    static constexpr int kFloats = kTailOff + 2 * GP + kW * GP;
+    static constexpr int kBytes = kFloats * 4;
+    static_assert(kNS * kStage >= 2 * GP + GP * D, "a warp's merge data must fit in its stages");
+    static_assert(kWarpF % 4 == 0 && kWarpOff % 4 == 0, "float4 alignment");
+};
+
+struct SeqF32 {
+    int k_lo, k_hi;   // visible local keys [k_lo, k_hi)
+    int off;          // global position of local key 0
+    int cs;           // clear_start (global), 0: no fog
+};
+
+__device__ __forceinline__ SeqF32 seq_f32(const DecodeF32Args& p, int b) {
+    SeqF32 s;
+    const int cap = ((p.max_seq_len + 15) / 16) * 16;
+    int n = p.seq_lens[b];
+    if (n < 0 || n > cap) {
+        record_status(p.status, KESSIE_DEV_BAD_ARG);
+        n = n < 0 ? 0 : cap;
+    }
+    s.off = p.kv_off ? p.kv_off[b] : 0;
+    const int qp = p.q_pos ? p.q_pos[b] : s.off + n - 1;
+    s.k_hi = min(n, qp - s.off + 1);
+    s.k_lo = p.window > 0 ? max(0, qp - p.window + 1 - s.off) : 0;
+    if (s.k_hi < s.k_lo) s.k_hi = s.k_lo;
+    s.cs = p.clear_start ? p.clear_start[b] : 0;
+    return s;
+}
+
+// Fog weight of the key at global position j (kessie_hip_kernels.py:408-412):
+// the fp32 ratio j / max(cs-1, 1) with an IEEE divide, then pow (sqrt for
+// alpha 0.5, the route torch takes for that exponent).
+__device__ __forceinline__ float fog_weight_f32(const DecodeF32Args& p, int cs, int j) {
+    if (p.fog_w) return __ldg(p.fog_w + j);
+    if (!(p.fog_alpha > 0.f) || cs <= 0 || j >= cs) return 1.f;
+    const float t = __fdiv_rn((float)j, (float)max(cs - 1, 1));
+    return p.fog_alpha == 0.5f ? sqrtf(t) : powf(t, p.fog_alpha);
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory");
+}
+
+// Count one arrival at a group counter; returns the arrivals before this one
+// (a counter holding another launch's tag counts as zero).
+__device__ __forceinline__ unsigned arrive_tagged(unsigned long long* c, uint32_t tag) {
+    const unsigned long long hi = (unsigned long long)tag << 32;
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(c);
+    while (true) {
+        const unsigned long long cur = (old >> 32) == tag ? old : hi;
+        const unsigned long long prev = atomicCAS(c, old, cur + 1ull);
+        if (prev == old) return (unsigned)(cur & 0xffffffffull);
+        old = prev;
+    }
+}
+
+__device__ __forceinline__ void emit_f32(const DecodeF32Args& p, int row, int d, float o, float M, float L) {
+    const int D = p.D;
+    if (p.out) p.out[(int64_t)row * D + d] = o;
+    if (p.out_part) {
+        float* dst = p.out_part + (int64_t)row * (D + 2);
+        dst[d] = o;
+        if (d == 0) {
+            dst[D] = M == -INFINITY ? -INFINITY : M * kLn2;
+            dst[D + 1] = L;
+        }
+    }
+}
+
+template <int D, int GP>
+__global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Args p, const int S) {
+    using Lay = F32Layout<D, GP>;
+    constexpr int E = D / 32;      // PV: consecutive dims of O per lane
+    constexpr int CPL = D / 16;    // QK: 16-byte chunks per lane (a quarter row)
+    constexpr int H4 = GP / 4;     // QK: heads per lane after the reduction
+    constexpr int RC = D / 4;      // 16-byte chunks per row
+    extern __shared__ float4 smem_f4[];
+    float* sm = reinterpret_cast<float*>(smem_f4);
+    float* sq = sm;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* sw = sm + Lay::kWarpOff + warp * Lay::kWarpF;
+    float* sP = sw + kNS * Lay::kStage;
+    float* sA = sP + 8 * GP;
+    float* sML = sm + Lay::kTailOff;       // [GP][2]
+    float* sSC = sML + 2 * GP;             // [kW][GP]
+    __shared__ int s_last;
+
+    const int grp = blockIdx.y, split = blockIdx.x;
+    const int b = grp / p.Hkv, hk = grp - b * p.Hkv;
+    const int G = p.Hq / p.Hkv;
+    const SeqF32 si = seq_f32(p, b);
+
+    // query rows of the group, scaled into log2 units, swizzled by quarter
+    const float qscale = p.sm_scale * kLog2e;
+    for (int i = threadIdx.x; i < GP * RC; i += kT) {
+        const int g = i / RC, x = i - g * RC;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (g < G) {
+            const float* src = p.q + (int64_t)b * p.q_sb + (int64_t)(hk * G + g) * p.q_sh + x * 4;
+            v = make_float4(src[0] * qscale, src[1] * qscale, src[2] * qscale, src[3] * qscale);
+        }
+        const int dq = x / CPL, c = x - dq * CPL;
+        *reinterpret_cast<float4*>(sq + g * D + ((dq * CPL + (c ^ dq)) << 2)) = v;
+    }
+    __syncthreads();
+
+    // this CTA's chunks: [cb, ce) of the group's visible chunks
+    const int c_lo = si.k_lo >> 3;
+    const int nch = si.k_hi > si.k_lo ? ((si.k_hi + 7) >> 3) - c_lo : 0;
+    const int per = (nch + S - 1) / S;
+    const int cb = c_lo + split * per;
+    const int ce = min(c_lo + nch, cb + per);
+    const int nw = ce > cb + warp ? (ce - cb - warp + kW - 1) / kW : 0;
+    const int32_t* bt = p.block_table + (int64_t)b * p.bt_stride;
+
+    // Starts the copies of this warp's chunk i into stage i % kNS; returns
+    // true (and copies nothing) when the chunk's page id is out of range.
+    auto issue = [&](int i) -> bool {
+        const int key0 = (cb + warp + i * kW) * 8;
+        const int pi = key0 / p.page_size, tok = key0 - pi * p.page_size;
+        const int page = __ldg(bt + pi);
+        if (page < 0 || page >= p.num_pages) {
+            if (lane == 0) record_status(p.status, KESSIE_DEV_BAD_PAGE_ID);
+            return true;
+        }
+        float* dK = sw + (i % kNS) * Lay::kStage;
+        float* dV = dK + Lay::kChunk;
+        const int64_t base = (int64_t)page * p.page_stride + (int64_t)tok * p.token_stride + (int64_t)hk * p.head_stride;
+        const float* gK = p.k_cache + base;
+        const float* gV = p.v_cache + base;
+#pragma unroll
+        for (int t = 0; t < 8 * RC / 32; ++t) {
+            const int idx = t * 32 + lane;
+            const int r = idx / RC, x = idx - r * RC;
+            const int64_t src = (int64_t)r * p.token_stride + x * 4;
+            cp_async16(dK + r * D + ((x ^ (r & 7)) << 2), gK + src);
+            cp_async16(dV + r * D + (x << 2), gV + src);
+        }
+        return false;
+    };
+
+    float m[H4], l[H4];
+#pragma unroll
+    for (int h = 0; h < H4; ++h) { m[h] = -INFINITY; l[h] = 0.f; }
+    float acc[GP][E];
+#pragma unroll
+    for (int g = 0; g < GP; ++g)
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[g][e] = 0.f;
+
+    uint32_t badm = 0;   // bit s: the chunk in stage s had a bad page id (warp-uniform)
+#pragma unroll
+    for (int i = 0; i < kNS - 1; ++i) {
+        if (i < nw) {
+            if (issue(i)) badm |= 1u << i; else badm &= ~(1u << i);
+        }
+        cp_async_commit();
+    }
+    const int kk = lane >> 2, dq = lane & 3;
+    for (int i = 0; i < nw; ++i) {
+        cp_async_wait<kNS - 2>();
+        __syncwarp();
+        {
+            const int nx = i + kNS - 1;
+            if (nx < nw) {
+                const int sl = nx % kNS;
+                if (issue(nx)) badm |= 1u << sl; else badm &= ~(1u << sl);
+            }
+            cp_async_commit();
+        }
+        const int sl = i % kNS;
+        const float* sK = sw + sl * Lay::kStage;
+        const float* sV = sK + Lay::kChunk;
+        const bool bad = (badm >> sl) & 1u;
+        const int key0 = (cb + warp + i * kW) * 8;
+
+        // ---- scores: lane (kk, dq) dots its quarter of key kk with every head
+        float s[GP];
+#pragma unroll
+        for (int g = 0; g < GP; ++g) s[g] = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < CPL; ++cc) {
+            const int x = dq * CPL + cc;
+            const float4 kf = *reinterpret_cast<const float4*>(sK + kk * D + ((x ^ (kk & 7)) << 2));
+            const int qx = (dq * CPL + (cc ^ dq)) << 2;
+#pragma unroll
+            for (int g = 0; g < GP; ++g) {
+                const float4 qf = *reinterpret_cast<const float4*>(sq + g * D + qx);
+                s[g] = fmaf(qf.x, kf.x, s[g]);
+                s[g] = fmaf(qf.y, kf.y, s[g]);
+                s[g] = fmaf(qf.z, kf.z, s[g]);
+                s[g] = fmaf(qf.w, kf.w, s[g]);
+            }
+        }
+        // transposing reduction over the quarters: lane keeps heads dq*H4 .. dq*H4+H4-1
+        float t[GP / 2];
+        {
+            const bool up = (lane & 2) != 0;
+#pragma unroll
+            for (int j = 0; j < GP / 2; ++j) {
+                const float send = up ? s[j] : s[j + GP / 2];
+                const float keep = up ? s[j + GP / 2] : s[j];
+                t[j] = keep + __shfl_xor_sync(kFull, send, 2);
+            }
+        }
+        float u[H4];
+        {
+            const bool up = (lane & 1) != 0;
+#pragma unroll
+            for (int j = 0; j < H4; ++j) {
+                const float send = up ? t[j] : t[j + H4];
+                const float keep = up ? t[j + H4] : t[j];
+                u[j] = keep + __shfl_xor_sync(kFull, send, 1);
+            }
+        }
+
+        // ---- online softmax over the chunk's 8 keys
+        const int jl = key0 + kk;
+        const bool valid = !bad && jl >= si.k_lo && jl < si.k_hi;
+        const float w = valid ? fog_weight_f32(p, si.cs, si.off + jl) : 0.f;
+        bool moved = false;
+#pragma unroll
+        for (int h = 0; h < H4; ++h) {
+            const float x = valid ? u[h] : -INFINITY;
+            float cm = x;
+            cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 4));
+            cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 8));
+            cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 16));
+            const float mn = fmaxf(m[h], cm);
+            const float al = mn == -INFINITY ? 1.f : exp2f(m[h] - mn);
+            const float pr = valid ? exp2f(x - mn) : 0.f;
+            float ps = pr;
+            ps += __shfl_xor_sync(kFull, ps, 4);
+            ps += __shfl_xor_sync(kFull, ps, 8);
+            ps += __shfl_xor_sync(kFull, ps, 16);
+            l[h] = l[h] * al + ps;
+            m[h] = mn;
+            moved |= al != 1.f;
+            sP[kk * GP + dq * H4 + h] = pr * w;
+            if (kk == 0) sA[dq * H4 + h] = al;
+        }
+        const bool rescale = __any_sync(kFull, moved);
+        __syncwarp();
+
+        // ---- O += P * V (fog already in P); lane owns dims lane*E .. lane*E+E-1
+        if (rescale) {
+#pragma unroll
+            for (int g4 = 0; g4 < GP / 4; ++g4) {
+                const float4 a = *reinterpret_cast<const float4*>(sA + g4 * 4);
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    acc[g4 * 4 + 0][e] *= a.x;
+                    acc[g4 * 4 + 1][e] *= a.y;
+                    acc[g4 * 4 + 2][e] *= a.z;
+                    acc[g4 * 4 + 3][e] *= a.w;
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int j = key0 + r;
+            if (bad || j < si.k_lo || j >= si.k_hi) continue;     // warp-uniform
+            float v[E];
+            if (E == 4) {
+                const float4 vf = *reinterpret_cast<const float4*>(sV + r * D + lane * 4);
+                v[0] = vf.x; v[1] = vf.y; v[2] = vf.z; v[3] = vf.w;
+            } else {
+                const float2 vf = *reinterpret_cast<const float2*>(sV + r * D + lane * 2);
+                v[0] = vf.x; v[1] = vf.y;
+            }
+#pragma unroll
+            for (int g4 = 0; g4 < GP / 4; ++g4) {
+                const float4 pq = *reinterpret_cast<const float4*>(sP + r * GP + g4 * 4);
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    acc[g4 * 4 + 0][e] = fmaf(pq.x, v[e], acc[g4 * 4 + 0][e]);
+                    acc[g4 * 4 + 1][e] = fmaf(pq.y, v[e], acc[g4 * 4 + 1][e]);
+                    acc[g4 * 4 + 2][e] = fmaf(pq.z, v[e], acc[g4 * 4 + 2][e]);
+                    acc[g4 * 4 + 3][e] = fmaf(pq.w, v[e], acc[g4 * 4 + 3][e]);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- merge the 8 warps (each writes into its own stage area)
+    float* mw = sw;              // [GP][2] (m, l)
+    float* ow = sw + 2 * GP;     // [GP][D]
+    if (kk == 0) {
+#pragma unroll
+        for (int h = 0; h < H4; ++h) {
+            mw[(dq * H4 + h) * 2] = m[h];
+            mw[(dq * H4 + h) * 2 + 1] = l[h];
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+        if (E == 4)
+            *reinterpret_cast<float4*>(ow + g * D + lane * 4) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+        else
+            *reinterpret_cast<float2*>(ow + g * D + lane * 2) = make_float2(acc[g][0], acc[g][1]);
+    }
+    __syncthreads();
+    auto warp_area = [&](int w) { return sm + Lay::kWarpOff + w * Lay::kWarpF; };
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float M = -INFINITY;
+        for (int w2 = 0; w2 < kW; ++w2) M = fmaxf(M, warp_area(w2)[g * 2]);
+        float L = 0.f;
+        for (int w2 = 0; w2 < kW; ++w2) {
+            const float mw2 = warp_area(w2)[g * 2];
+            const float sc = mw2 == -INFINITY ? 0.f : exp2f(mw2 - M);
+            sSC[w2 * GP + g] = sc;
+            L += warp_area(w2)[g * 2 + 1] * sc;
+        }
+        sML[g * 2] = M;
+        sML[g * 2 + 1] = L;
+    }
+    __syncthreads();
+
+    const int row0 = b * p.Hq + hk * G;
+    if (S == 1) {
+        for (int i = threadIdx.x; i < G * D; i += kT) {
+            const int g = i / D, d = i - g * D;
+            const float M = sML[g * 2], L = sML[g * 2 + 1];
+            float o = 0.f;
+            if (L > 0.f) {
+                for (int w2 = 0; w2 < kW; ++w2) o = fmaf(warp_area(w2)[2 * GP + g * D + d], sSC[w2 * GP + g], o);
+                o /= L;
+            }
+            emit_f32(p, row0 + g, d, o, M, L);
+        }
+        return;
+    }
+
+    const int slot = grp * S + split;
+    for (int i = threadIdx.x; i < G * D; i += kT) {
+        const int g = i / D, d = i - g * D;
+        const float M = sML[g * 2], L = sML[g * 2 + 1];
+        float o = 0.f;
+        if (L > 0.f) {
+            for (int w2 = 0; w2 < kW; ++w2) o = fmaf(warp_area(w2)[2 * GP + g * D + d], sSC[w2 * GP + g], o);
+            o /= L;
+        }
+        p.part_o[((size_t)slot * G + g) * D + d] = o;
+        if (d == 0) {
+            p.part_ml[((size_t)slot * G + g) * 2] = M;
+            p.part_ml[((size_t)slot * G + g) * 2 + 1] = L;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = arrive_tagged(p.counters + grp, p.tag) == (unsigned)(S - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    // ---- last CTA of the group: merge the S slots.  Per (slot, head) scale
+    // L_s * 2^(m_s - M) / L into the (now idle) stage area.
+    float* ssc = sm + Lay::kWarpOff;      // [S][GP]
+    for (int g = warp; g < G; g += kW) {
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(p.part_ml + ((size_t)(grp * S + s2) * G + g) * 2));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, o));
+        float L = 0.f;
+        for (int s2 = lane; s2 < S; s2 += 32) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + ((size_t)(grp * S + s2) * G + g) * 2));
+            const float sc = ml.x == -INFINITY ? 0.f : ml.y * exp2f(ml.x - M);
+            ssc[s2 * GP + g] = sc;
+            L += sc;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(kFull, L, o);
+        if (lane == 0) {
+            sML[g * 2] = M;
+            sML[g * 2 + 1] = L;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += kT) {
+        const int g = i / D, d = i - g * D;
+        const float M = sML[g * 2], L = sML[g * 2 + 1];
+        float o = 0.f;
+        if (L > 0.f) {
+            for (int s2 = 0; s2 < S; ++s2) {
+                const float sc = ssc[s2 * GP + g];
+                if (sc != 0.f) o = fmaf(__ldcg(p.part_o + ((size_t)(grp * S + s2) * G + g) * D + d), sc, o);
+            }
+            o /= L;
+        }
+        emit_f32(p, row0 + g, d, o, M, L);
+    }
+    if (threadIdx.x == 0) p.counters[grp] = 0ull;     // graph replays (same tag) start clean
+}
+
+template <int D, int GP>
+int launch_f32_t(const DecodeF32Args& a, int S, cudaStream_t st) {
+    using Lay = F32Layout<D, GP>;
+    auto kern = fog_decode_f32_kernel<D, GP>;
+    // the last CTA's per-slot scales [S][GP] live in the warps' stage areas
+    if (S * GP > kW * Lay::kWarpF) S = kW * Lay::kWarpF / GP;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kBytes) != cudaSuccess)
+        return check_launch("paged_fog_decode (fp32): set smem attribute");
+    dim3 grid(S, a.B * a.Hkv);
+    kern<<<grid, kT, Lay::kBytes, st>>>(a, S);
+    return check_launch("paged_fog_decode (fp32)");
+}
+
+}  // namespace
+
+int launch_decode_f32(const DecodeF32Args& a, cudaStream_t st) {
+    const int G = a.Hq / a.Hkv;
+    const int groups = a.B * a.Hkv;
+    const int max_chunks = (a.max_seq_len + 7) / 8 + 1;
+    // about one CTA per SM in total, at least two chunks per warp, and no
+    // more splits than the workspace has slots for
+    int S = (sm_count() + groups - 1) / groups;
+    S = min(S, max(1, max_chunks / (2 * kW)));
+    S = min(S, a.slots / groups);
+    if (S < 1) S = 1;
+    if (a.D == 128) {
+        if (G <= 4) return launch_f32_t<128, 4>(a, S, st);
+        if (G <= 8) return launch_f32_t<128, 8>(a, S, st);
+        return launch_f32_t<128, 16>(a, S, st);
+    }
+    if (G <= 4) return launch_f32_t<64, 4>(a, S, st);
+    if (G <= 8) return launch_f32_t<64, 8>(a, S, st);
+    return launch_f32_t<64, 16>(a, S, st);
+}
+
+}  // namespace kessie
