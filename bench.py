@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["kessie", "reference"], default="kessie")
     ap.add_argument("--workload", default="cp_decode_1m",
-                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "page_ops", "prefill",
+                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "decode_f32", "page_ops", "prefill",
                              "prefill_small", "vllm_fog_decode", "index_query", "tiered_cache"])
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -492,7 +492,8 @@ def run_cp_decode(args):
             del kv, kc, vc, dec
             torch.cuda.empty_cache()
             sec = {}
-            for wl, st in (("decode_128k", 20), ("decode_cfg3", 20), ("vllm_fog_decode", 20), ("page_ops", 50),
+            for wl, st in (("decode_128k", 20), ("decode_cfg3", 20), ("vllm_fog_decode", 20), ("decode_f32", 20),
+                           ("page_ops", 50),
                            ("prefill", 10), ("index_query", 50), ("tiered_cache", 20)):
                 r = measure_aux(wl, st)
                 r.pop("workload", None)
@@ -528,10 +529,12 @@ def compact_secondary(sec):
     fraction of the bf16 peak), the index query and the tiered cache, then
     the CPU-port baselines."""
     out = {}
-    for k in ("decode_128k", "decode_cfg3", "vllm_fog_decode", "decode_f32_cfg1"):
+    for k in ("decode_128k", "decode_cfg3", "vllm_fog_decode", "decode_f32"):
         r = sec.get(k)
         if r:
             out[k] = {"us": _sig(r.get("us_per_step")), "GBs": _sig(r.get("GBs")), "frac": _sig(r.get("frac_of_hbm"))}
+            if "cfg1_us" in r:
+                out[k]["cfg1_us"] = _sig(r["cfg1_us"])
     r = sec.get("page_ops")
     if r:
         out["page_ops_b2b_frac"] = {n: _sig(r.get(n + "_b2b_frac")) for n in ("gather", "remap", "insert_remap")}
@@ -612,7 +615,42 @@ def measure_aux(workload, steps, warmup=3):
         torch.cuda.synchronize()
         return a.elapsed_time(b) / K
 
-    if args.workload in ("decode_cfg3", "decode_128k", "decode_small"):
+    if args.workload == "decode_f32":
+        # fp32 paged decode (the reference's own precision): config 1 (B1,
+        # Hq8/Hkv2, D128, 4096 keys, W512 -> clear_start 3584; 8 MiB of KV,
+        # timed cold after the L2 flush), and the config-3 attention shape
+        # at a fixed 131,072 keys in fp32 (34.4 GB of KV) for the roofline.
+        flush = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
+        B, Hq, Hkv, D, ps, N = 1, 8, 2, 128, 16, 4096
+        kv = torch.randn(N // ps, ps, 2, Hkv, D, device=dev)
+        bt = torch.randperm(N // ps, device=dev).to(torch.int32)[None]
+        q = torch.randn(B, Hq, D, device=dev)
+        sl = torch.tensor([N], dtype=torch.int32, device=dev)
+        cs = sl - 512
+        out = torch.empty(B, Hq, D, device=dev)
+        ms1 = timeit(lambda: ops.paged_fog_decode(q, kv[:, :, 0], kv[:, :, 1], bt, sl, clear_start=cs, out=out),
+                     args.steps)
+        flush = None
+        del kv
+        c = CFG3
+        B, Hq, Hkv, D, ps, N = c["batch"], c["q_heads"], c["kv_heads"], c["head_dim"], c["page"], 131072
+        P = B * N // ps
+        kv = torch.empty(P, ps, 2, Hkv, D, device=dev)
+        kv.normal_().mul_(1 / math.sqrt(128))
+        bt = torch.randperm(P, device=dev).to(torch.int32).view(B, N // ps)
+        q = torch.randn(B, Hq, D, device=dev) / math.sqrt(128)
+        sl = torch.full((B,), N, dtype=torch.int32, device=dev)
+        cs = sl - c["window"]
+        out = torch.empty(B, Hq, D, device=dev)
+        ms = timeit(lambda: ops.paged_fog_decode(q, kv[:, :, 0], kv[:, :, 1], bt, sl, clear_start=cs, out=out),
+                    args.steps)
+        byts = B * N * Hkv * D * 8
+        res.update(ms_per_step=ms, us_per_step=ms * 1e3, kv_bytes=byts, GBs=byts / ms / 1e6,
+                   frac_of_hbm=byts / ms / 1e6 / hbm, cfg1_us=ms1 * 1e3,
+                   note="fp32 K/V/q/out; us/GBs/frac: batch 32 x 131,072 keys, Hq 32 / Hkv 8; cfg1_us: config 1 "
+                        "(4096 keys) after a 256 MB L2 flush")
+        del kv
+    elif args.workload in ("decode_cfg3", "decode_128k", "decode_small"):
         c = CFG3
         B, Hq, Hkv, D, ps = c["batch"], c["q_heads"], c["kv_heads"], c["head_dim"], c["page"]
         rng = np.random.default_rng(3)

@@ -15,8 +15,8 @@
 // issue budget.
 //   grid  = (S splits, B*Hkv groups); the visible keys of a group are cut into
 //           8-key chunks (a chunk never crosses a page: page_size % 16 == 0)
-//           and split S ways; S is chosen from the SM count, at least two
-//           chunks per warp.
+//           and split S ways; S is chosen from the SM count so the grid's
+//           last wave is nearly full, with at least two chunks per warp.
 //   CTA   = 8 warps.  Each warp streams every 8th chunk of the CTA's range
 //           through its own 3-stage ring of 16-byte cp.async copies (8 KB of
 //           K+V per stage at D 128), so two chunks per warp are in flight
@@ -478,10 +478,18 @@ int launch_decode_f32(const DecodeF32Args& a, cudaStream_t st) {
     const int max_chunks = (a.max_seq_len + 7) / 8 + 1;
     // about one CTA per SM in total, at least two chunks per warp, and no
     // more splits than the workspace has slots for
-    int S = (sm_count() + groups - 1) / groups;
-    S = min(S, max(1, max_chunks / (2 * kW)));
-    S = min(S, a.slots / groups);
-    if (S < 1) S = 1;
+    const int sms = sm_count();
+    const int s_max = max(1, min(max_chunks / (2 * kW), a.slots / groups));
+    int S = min(s_max, max(1, (sms + groups - 1) / groups));
+    // one CTA per SM: among the next few split counts take the one whose
+    // grid fills its last wave best (equal-length groups then finish together)
+    auto fill = [&](int s) {
+        const long long ctas = (long long)s * groups;
+        return (double)ctas / (double)(((ctas + sms - 1) / sms) * sms);
+    };
+    double best = fill(S);
+    for (int s = S + 1; s <= min(s_max, 8 * S) && best < 0.97; ++s)
+        if (fill(s) > best + 1e-9) { best = fill(s); S = s; }
     if (a.D == 128) {
         if (G <= 4) return launch_f32_t<128, 4>(a, S, st);
         if (G <= 8) return launch_f32_t<128, 8>(a, S, st);

@@ -346,6 +346,10 @@ int run_prefill(const PrefillParams& p, const void* kc, const void* vc, int64_t 
 // tcgen05 prefill then streams 128-token TMA boxes from contiguous memory
 // instead of 16-token boxes scattered over pages (a TMA box costs a fixed
 // ~130 SM cycles, so 2 KB boxes cannot feed the tensor cores).
+// The fog weight of each key (kessie_hip_kernels.py:408-412: the fp32 ratio
+// j / max(cs-1, 1), then pow) is folded into the staged V here, once per key:
+// O = sum_j p_j (w_j v_j) / sum_j p_j is the same sum, and the attention
+// kernels then run without per-key weights on their softmax path.
 // grid (ceil(kv_max / page_size), B); threads over (kv, head, 16-byte chunk).
 template <typename T>
 __global__ void __launch_bounds__(256) stage_kv_kernel(const T* __restrict__ kc, const T* __restrict__ vc,
@@ -353,7 +357,10 @@ __global__ void __launch_bounds__(256) stage_kv_kernel(const T* __restrict__ kc,
                                                        int num_pages, int ps, const int32_t* __restrict__ bt,
                                                        int64_t bt_stride, const int32_t* __restrict__ kv_lens,
                                                        int max_kv_len, int kv_max, int Hkv, int D,
+                                                       const int32_t* __restrict__ clear_start, float fog_alpha,
+                                                       const float* __restrict__ fog_w, int64_t fog_w_sb,
                                                        T* __restrict__ sk, T* __restrict__ sv, int* status) {
+    __shared__ float wts[256];
     const int pg = blockIdx.x, b = blockIdx.y;
     int kv_len = kv_lens[b];
     if (kv_len > max_kv_len || kv_len < 0) {          // the block table holds max_kv_len keys at most
@@ -371,6 +378,22 @@ __global__ void __launch_bounds__(256) stage_kv_kernel(const T* __restrict__ kc,
             id = -1;
         }
     }
+    const int cs = (clear_start && fog_alpha > 0.f) ? clear_start[b] : INT_MIN;
+    const bool has_fog = fog_w != nullptr || cs > 0;
+    if (has_fog) {
+        for (int s = threadIdx.x; s < ps; s += blockDim.x) {
+            const int j = t0 + s;
+            float w = 1.f;
+            if (j >= kv_len) w = 0.f;
+            else if (fog_w) w = __ldg(fog_w + b * fog_w_sb + j);
+            else if (j < cs) {
+                const float t = __fdiv_rn((float)j, (float)max(cs - 1, 1));
+                w = fog_alpha == 0.5f ? sqrtf(t) : powf(t, fog_alpha);
+            }
+            wts[s] = w;
+        }
+        __syncthreads();
+    }
     const int chunks = D / 8;
     const int items = 2 * Hkv * chunks;
     for (int it = threadIdx.x; it < items; it += blockDim.x) {
@@ -379,9 +402,16 @@ __global__ void __launch_bounds__(256) stage_kv_kernel(const T* __restrict__ kc,
         const int h = r / chunks, c = r - h * chunks;
         const T* src = (kv ? vc : kc) + (int64_t)(id < 0 ? 0 : id) * page_stride + (int64_t)h * head_stride + c * 8;
         T* dst = (kv ? sv : sk) + (((int64_t)b * Hkv + h) * kv_max + t0) * D + c * 8;
+        const bool scale = kv && has_fog;
         for (int s = 0; s < ps && t0 + s < kv_pad; ++s) {
             uint4 v = make_uint4(0, 0, 0, 0);
             if (id >= 0 && t0 + s < kv_len) v = ldg_stream(src + (int64_t)s * token_stride);
+            if (scale) {
+                const float w = wts[s];
+                T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(to_f32(e[i]) * w);
+            }
             *reinterpret_cast<uint4*>(dst + (int64_t)s * D) = v;
         }
     }
@@ -519,19 +549,22 @@ int prefill_entry(
             stage_kv_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
                 (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache, page_stride, token_stride, head_stride,
                 num_pages, page_size, block_table, block_table_stride, kv_lens, max_kv_len, kv_max, num_kv_heads, head_dim,
-                sk, sk + half, p.status);
+                clear_start, fog_alpha, fog_weights, fog_weights_stride_b, sk, sk + half, p.status);
         } else {
             auto* sk = static_cast<__half*>(workspace);
             stage_kv_kernel<__half><<<grid, 256, 0, st>>>(
                 (const __half*)k_cache, (const __half*)v_cache, page_stride, token_stride, head_stride, num_pages,
-                page_size, block_table, block_table_stride, kv_lens, max_kv_len, kv_max, num_kv_heads, head_dim, sk,
-                sk + half, p.status);
+                page_size, block_table, block_table_stride, kv_lens, max_kv_len, kv_max, num_kv_heads, head_dim,
+                clear_start, fog_alpha, fog_weights, fog_weights_stride_b, sk, sk + half, p.status);
         }
         int rc = check_launch("prefill staging");
         if (rc) return rc;
-        // dense view of the staging buffer: page coordinate = sequence, token = position
+        // dense view of the staging buffer: page coordinate = sequence, token =
+        // position; the fog weights are already in the staged V
         p.block_table = nullptr;
         p.num_pages = batch;
+        p.clear_start = nullptr; p.clear_start_const = 0; p.fog_alpha = 0.f;
+        p.fog_w = nullptr; p.fog_w_sb = 0;
         const char* base = static_cast<const char*>(workspace);
         return run_prefill(p, base, base + half * 2, (int64_t)num_kv_heads * kv_max * head_dim, head_dim,
                            (int64_t)kv_max * head_dim, batch, kv_max, head_dim, bf16, st);

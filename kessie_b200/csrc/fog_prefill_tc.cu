@@ -70,6 +70,63 @@ struct TcArgs {
     int page_size;
 };
 
+// P of one 128-key tile for one row: p = 2^(s*scale - m), P' = p * w (FOG:
+// the fog weights of the tile's keys in wbuf; the staged path carries them in
+// V instead, and then key pairs go through packed fp32 arithmetic -- one fma
+// and one add instruction per pair, the exponentials on the MUFU), packed to
+// 16-bit pairs over the first 64 columns of the row's S region.  Returns the
+// row sum of the unweighted p.  Warp-collective (tcgen05.st).
+template <bool BF16, bool FOG>
+__device__ __forceinline__ float softmax_p_tile(const uint32_t (&sv)[4][32], uint32_t sreg, float scale_log2,
+                                                float nb, const float* wbuf) {
+    float lsum;
+    if (FOG) {
+        // scalar form: the weights' registers leave no room for packed pairs
+        const float4* w4 = reinterpret_cast<const float4*>(wbuf);
+        float lt4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int h4 = 0; h4 < 4; ++h4) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+                const float4 w = w4[(h4 * 32 + 2 * i) >> 2];      // keys h4*32 + 2i .. +3
+                const float p0 = ptx::ex2(fmaf(__uint_as_float(sv[h4][2 * i]), scale_log2, nb));
+                const float p1 = ptx::ex2(fmaf(__uint_as_float(sv[h4][2 * i + 1]), scale_log2, nb));
+                const float p2 = ptx::ex2(fmaf(__uint_as_float(sv[h4][2 * i + 2]), scale_log2, nb));
+                const float p3 = ptx::ex2(fmaf(__uint_as_float(sv[h4][2 * i + 3]), scale_log2, nb));
+                lt4[0] += p0; lt4[1] += p1; lt4[2] += p2; lt4[3] += p3;
+                pk[i] = ptx::pack2<BF16>(p0 * w.x, p1 * w.y);
+                pk[i + 1] = ptx::pack2<BF16>(p2 * w.z, p3 * w.w);
+            }
+            ptx::tmem_st16(sreg + h4 * 16, pk);
+        }
+        lsum = (lt4[0] + lt4[1]) + (lt4[2] + lt4[3]);
+    } else {
+        const uint64_t sc2 = ptx::f2_pack(scale_log2, scale_log2), nb2 = ptx::f2_pack(nb, nb);
+        uint64_t lt2[2] = {0ull, 0ull};
+#pragma unroll
+        for (int h4 = 0; h4 < 4; ++h4) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const uint64_t s2 = ptx::f2_pack(__uint_as_float(sv[h4][2 * i]), __uint_as_float(sv[h4][2 * i + 1]));
+                float e0, e1;
+                ptx::f2_unpack(ptx::ffma2(s2, sc2, nb2), e0, e1);
+                const float p0 = ptx::ex2(e0), p1 = ptx::ex2(e1);
+                lt2[i & 1] = ptx::fadd2(lt2[i & 1], ptx::f2_pack(p0, p1));
+                pk[i] = ptx::pack2<BF16>(p0, p1);
+            }
+            ptx::tmem_st16(sreg + h4 * 16, pk);
+        }
+        float a0, a1, b0, b1;
+        ptx::f2_unpack(lt2[0], a0, a1);
+        ptx::f2_unpack(lt2[1], b0, b1);
+        lsum = (a0 + a1) + (b0 + b1);
+    }
+    ptx::tmem_st_wait();
+    return lsum;
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                                       const __grid_constant__ CUtensorMap tmK,
@@ -372,7 +429,9 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[c][i]));
+                    for (int i = 0; i < 32; i += 2)
+                        mx4[(i >> 1) & 3] = ptx::max3(mx4[(i >> 1) & 3], __uint_as_float(sv[c][i]),
+                                                      __uint_as_float(sv[c][i + 1]));
             } else {
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
@@ -395,8 +454,12 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 l *= factor;
                 m_used = m_new;
             }
-            // O rescale in TMEM (warp-collective, rare).  PV(j-1) is complete:
-            // the commit that published S(j) was issued after it.
+            const float nb = m_used == -INFINITY ? 0.f : -m_used;
+            l += has_fog ? softmax_p_tile<BF16, true>(sv, sreg, p.scale_log2, nb, wbuf)
+                         : softmax_p_tile<BF16, false>(sv, sreg, p.scale_log2, nb, wbuf);
+            // O rescale in TMEM (warp-collective, rare), after P so the scores'
+            // registers are free.  PV(j-1) is complete (the commit that
+            // published S(j) was issued after it) and PV(j) waits for p_full.
             if (__any_sync(0xffffffffu, need && factor != 0.f && j > 0)) {
                 const float f = (need && factor != 0.f) ? factor : 1.f;
 #pragma unroll 1
@@ -410,33 +473,6 @@ __global__ void __launch_bounds__(kThreads, 1) fog_prefill_tc_kernel(const __gri
                 }
                 ptx::tmem_st_wait();
             }
-            const float4* w4 = reinterpret_cast<const float4*>(wbuf);
-            const float nb = m_used == -INFINITY ? 0.f : -m_used;
-            float lt4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int h4 = 0; h4 < 4; ++h4) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 16; i += 2) {
-                    const int c0 = h4 * 32 + 2 * i;          // key column (4 keys per step)
-                    const float4 w = has_fog ? w4[c0 >> 2] : make_float4(1.f, 1.f, 1.f, 1.f);
-                    const float s0 = __uint_as_float(sv[h4][2 * i]);
-                    const float s1 = __uint_as_float(sv[h4][2 * i + 1]);
-                    const float s2 = __uint_as_float(sv[h4][2 * i + 2]);
-                    const float s3 = __uint_as_float(sv[h4][2 * i + 3]);
-                    const float p0 = ptx::ex2(fmaf(s0, p.scale_log2, nb));
-                    const float p1 = ptx::ex2(fmaf(s1, p.scale_log2, nb));
-                    const float p2 = ptx::ex2(fmaf(s2, p.scale_log2, nb));
-                    const float p3 = ptx::ex2(fmaf(s3, p.scale_log2, nb));
-                    lt4[0] += p0; lt4[1] += p1; lt4[2] += p2; lt4[3] += p3;
-                    pk[i] = ptx::pack2<BF16>(p0 * w.x, p1 * w.y);
-                    pk[i + 1] = ptx::pack2<BF16>(p2 * w.z, p3 * w.w);
-                }
-                // P (bf16 pairs) over the first 64 columns of this tile's S region
-                ptx::tmem_st16(sreg + h4 * 16, pk);
-            }
-            ptx::tmem_st_wait();
-            l += (lt4[0] + lt4[1]) + (lt4[2] + lt4[3]);
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&p_full[x]);

@@ -53,7 +53,7 @@ def test_compact_secondary_is_short():
     sys.path.insert(0, ROOT)
     import bench
     dec = {"us_per_step": 2514.2345, "GBs": 6833.33, "frac_of_hbm": 1.04231}
-    sec = {"decode_128k": dec, "decode_cfg3": dec, "vllm_fog_decode": dec, "decode_f32_cfg1": dec,
+    sec = {"decode_128k": dec, "decode_cfg3": dec, "vllm_fog_decode": dec, "decode_f32": dict(dec, cfg1_us=31.23),
            "page_ops": {"gather_b2b_frac": 0.86341, "remap_b2b_frac": 0.7601, "insert_remap_b2b_frac": 0.7891,
                         "cpu_baseline": {"gather_GBs": 3.981, "remap_GBs": 0.9312}},
            "prefill": {"ms": 40.931, "tflops": 846.21, "frac_of_bf16_peak": 0.51101, "cpu_baseline": {"value": 0.2461}},
