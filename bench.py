@@ -754,6 +754,9 @@ def measure_aux(workload, steps, warmup=3):
             torch.cuda.synchronize()
             reps = max(3, args.steps // L)
             e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+            # a device-side sleep ahead of the first event lets the host enqueue
+            # every launch, so host-side wrapper time is not in the events
+            torch.cuda._sleep(int(reps * L * 1e5))
             e0.record()
             for _ in range(reps):
                 for l in range(L):

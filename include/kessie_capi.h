@@ -27,6 +27,9 @@
  *     library's device status word and returns; kessie_read_device_status()
  *     reads and clears it.
  *   - Strides are in ELEMENTS; head_dim is always the contiguous dimension.
+ *   - The library caches, per device, the addresses of its own device
+ *     variables (the status word, the allocation-free decode's scratch): do
+ *     not use it on a device after cudaDeviceReset of that device.
  *   - Positions are int32; page tables are int32; page_valid is int8.
  */
 #ifndef KESSIE_CAPI_H
@@ -286,6 +289,8 @@ int kessie_paged_fog_decode_ex_v2(const void* q, int64_t q_stride_b, int64_t q_s
  *     the array are rejected with KESSIE_ERR_WORKSPACE and a message.
  *   - The first call on each device looks the array's address up
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *     The address is cached for the life of the process: do not call this
+ *     entry point on a device after cudaDeviceReset of that device.
  *   - Every call uses the same array: calls that can overlap on the GPU race
  *     and must be ordered by the caller.  Leftover contents from a previous
  *     call are never read. */

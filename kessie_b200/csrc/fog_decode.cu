@@ -1185,7 +1185,10 @@ extern "C" int kessie_lse_combine_v2(const float* partials, int num_splits, int6
 // exits.  Its name is only a host-side handle: host code must never pass it
 // to a kernel.  Its device address is looked up with cudaGetSymbolAddress
 // once per device, on the first call made with that device current, and
-// cached; make that first call before any stream capture.  All calls share
+// cached; make that first call before any stream capture.  The cache is never
+// refreshed: after cudaDeviceReset (or anything else that tears down the
+// device's primary context) the cached address is stale, so a process that
+// resets a device must not call this entry point on it again.  All calls share
 // the one array, so two calls whose work overlaps on the GPU (different
 // streams, or different threads using one device) race on it; callers must
 // order them.  The array keeps whatever the previous call left: the decode's
@@ -1209,8 +1212,10 @@ int noalloc_scratch(void** out) {
     if (!g_noalloc_ptr[dev]) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();       // consume the error so a later call's launch check does not see it
             return set_error(KESSIE_ERR_CUDA, "noalloc decode: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        }
         g_noalloc_ptr[dev] = p;
     }
     *out = g_noalloc_ptr[dev];

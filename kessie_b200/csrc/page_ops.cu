@@ -12,6 +12,7 @@
 // Semantics follow kessie_kernels_v2.hip:393-456,670-707 and
 // kessie_hip_kernels.py:520-564,596-606 (see each kernel).
 #include "common.cuh"
+#include "ptx.cuh"
 
 #include <math.h>
 #include <stdio.h>
@@ -107,6 +108,157 @@ __device__ __forceinline__ void rotate_pair(uint4& lo, uint4& hi, const float* c
     lo = VecOps<T>::pack(ra);
     hi = VecOps<T>::pack(rb);
 }
+
+// ------------------------------------------------------------------ bulk-copy page gather
+// Persistent, warp-specialised CTAs (one per SM) gather pages with the
+// bulk-copy (TMA) engine instead of through registers.  A unit is one
+// gathered page: its K rows and V rows (a row = all heads of one token, H*D
+// contiguous elements; 2 x 16 x 2 KB = 64 KB at config 2).  A ring of
+// shared-memory stages carries the units:
+//   warp 0 (producer): one global->shared bulk load per row of unit k into
+//           stage k % ns once the stage is released (empty[s]); completion on
+//           full[s];
+//   warp 1 (storer): waits for full[s], issues one shared->global bulk store
+//           per output row (row-sized copies measured faster than one 32 KB
+//           copy per block), and releases a stage once the
+//           stores that read it are done (bulk-group read wait, one unit
+//           behind).
+// Sources and destinations are this GPU's memory; no multicast.  Every wait
+// is bounded; a wait that runs out flags KESSIE_DEV_WAIT_TIMEOUT, stops both
+// roles, and the CTA lets its issued copies finish before exiting.
+constexpr int kBulkMaxStages = 8;
+constexpr int kBulkStoreLag = 1;       // store groups left in flight before a stage is released
+constexpr int kBulkHeader = 256;       // barriers and the abort flag
+
+struct BulkArgs {
+    const char* cache;              // source pages
+    int64_t page_b, token_b, kv_b;  // byte strides of the cache
+    int max_pages, ps;
+    const int32_t* ids;             // page of unit i
+    char* rk;                       // dense K output rows [n*ps][H][D] (nullable)
+    char* rv;                       // dense V output rows (nullable)
+    int R;                          // bytes of one row (H*D elements), a multiple of 16
+    int units;
+    int ns, stage_b;                // ring stages, bytes per stage
+    int* status;
+};
+
+__global__ void __launch_bounds__(64, 1) page_gather_bulk_kernel(const BulkArgs a) {
+    extern __shared__ __align__(128) uint8_t bsm[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(bsm);                 // [ns]
+    uint64_t* empty = full + kBulkMaxStages;                           // [ns]
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bsm + 2 * kBulkMaxStages * 8);
+    uint8_t* stages = bsm + kBulkHeader;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int my_units = a.units > (int)blockIdx.x ? (a.units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    auto unit_of = [&](int k) { return (int)blockIdx.x + k * (int)gridDim.x; };
+    auto page_of = [&](int u) -> int {
+        const int pg = a.ids[u];
+        return (pg < 0 || pg >= a.max_pages) ? -1 : pg;
+    };
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.ns; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        *abort_flag = 0;
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    const uint32_t R = (uint32_t)a.R;
+    const uint32_t blk = (uint32_t)a.ps * R;          // one K (or V) block of a page
+    auto fail = [&]() {
+        record_status(a.status, KESSIE_DEV_WAIT_TIMEOUT);
+        *abort_flag = 1;
+    };
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        int issued = 0;
+        if (lane == 0) {
+            for (int k = 0; k < my_units && !*abort_flag; ++k) {
+                const int s = k % a.ns;
+                if (k >= a.ns && !ptx::mbar_wait(&empty[s], (uint32_t)(k / a.ns - 1) & 1u)) { fail(); break; }
+                const int pg = page_of(unit_of(k));
+                uint8_t* st = stages + (size_t)s * a.stage_b;
+                const int nb = pg < 0 ? 0 : (a.rk ? 1 : 0) + (a.rv ? 1 : 0);
+                ptx::mbar_arrive_expect_tx(&full[s], (uint32_t)nb * blk);
+                if (pg >= 0) {
+                    const char* page = a.cache + (int64_t)pg * a.page_b;
+                    for (int b = 0; b < 2; ++b) {
+                        if (!(b ? a.rv : a.rk)) continue;
+                        for (int t = 0; t < a.ps; ++t)
+                            ptx::bulk_g2s(st + b * blk + t * R, page + t * a.token_b + b * a.kv_b, R, &full[s]);
+                    }
+                }
+                issued = k + 1;
+            }
+        }
+        __syncwarp();
+        // the CTA exits only after every issued load has landed (bounded)
+        if (lane == 0)
+            for (int k = max(0, issued - a.ns); k < issued; ++k)
+                if (!ptx::mbar_wait(&full[k % a.ns], (uint32_t)(k / a.ns) & 1u)) { fail(); break; }
+    } else {
+        // ------------------------------------------------------------ storer
+        for (int k = 0; k < my_units; ++k) {
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            const int s = k % a.ns;
+            if (!__all_sync(0xffffffffu, ptx::mbar_wait(&full[s], (uint32_t)(k / a.ns) & 1u))) {
+                if (lane == 0) fail();
+                break;
+            }
+            const int u = unit_of(k);
+            const int pg = page_of(u);
+            const uint8_t* st = stages + (size_t)s * a.stage_b;
+            const int64_t off = (int64_t)u * blk;     // dense output rows of this page
+            if (pg < 0) {
+                // a bad page id gathers zeros
+                if (lane == 0) record_status(a.status, KESSIE_DEV_BAD_PAGE_ID);
+                for (int b = 0; b < 2; ++b) {
+                    char* out = b ? a.rv : a.rk;
+                    if (!out) continue;
+                    for (uint32_t i = lane * 16; i < blk; i += 32 * 16)
+                        *reinterpret_cast<uint4*>(out + off + i) = make_uint4(0, 0, 0, 0);
+                }
+            } else if (lane == 0) {
+                for (int b = 0; b < 2; ++b) {
+                    char* out = b ? a.rv : a.rk;
+                    if (!out) continue;
+                    for (int t = 0; t < a.ps; ++t) ptx::bulk_s2g(out + off + t * R, st + b * blk + t * R, R);
+                }
+            }
+            if (lane == 0) {
+                ptx::bulk_commit();
+                ptx::bulk_wait_read<kBulkStoreLag>();
+                if (k >= kBulkStoreLag) ptx::mbar_arrive(&empty[(k - kBulkStoreLag) % a.ns]);
+            }
+            __syncwarp();
+        }
+        if (lane == 0) ptx::bulk_wait<0>();
+    }
+    __syncthreads();
+}
+
+// Bulk gather set-up: rows of H*D contiguous elements (head stride ==
+// head_dim), 16-byte aligned bases and strides, dense outputs, and a ring of
+// >= 3 stages in shared memory.  Returns 0 when the shape is outside it.
+int launch_gather_bulk(BulkArgs a, cudaStream_t st) {
+    const int budget = 227 * 1024;
+    a.stage_b = (int)align_up((size_t)2 * a.ps * a.R, 128);
+    a.ns = std::min(kBulkMaxStages, (budget - kBulkHeader) / a.stage_b);
+    if (a.ns < kBulkStoreLag + 2) return 0;
+    const int smem = kBulkHeader + a.ns * a.stage_b;
+    if (cudaFuncSetAttribute(page_gather_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    const int grid = std::min(a.units, sm_count());
+    page_gather_bulk_kernel<<<grid, 64, smem, st>>>(a);
+    return 1;
+}
+
+bool bulk_ok(int64_t bytes) { return bytes % 16 == 0; }
 
 // ------------------------------------------------------------------ RoPE remap
 // CTA = `tpb` tokens.  Stage 1: cos/sin of (tgt-orig)*f_d for the CTA's tokens
@@ -330,6 +482,7 @@ __global__ void __launch_bounds__(256, 6) rope_tokens_kernel(
     T* ksm = reinterpret_cast<T*>(tab + tpb * (half / 2));   // [tpb][H][D] K rows
     T* vsm = ksm + tpb * rowe;                               // [tpb][H][D] V rows (insert)
     long long* rowoff = reinterpret_cast<long long*>(vsm + (INSERT ? tpb * rowe : 0));  // [tpb] insert dst offsets
+    float* fqs = reinterpret_cast<float*>(rowoff + (INSERT ? tpb : 0));                // [half] frequencies
     const int t0 = blockIdx.x * tpb;
     const int nt = min(tpb, num_tokens - t0);
     const int kitems = nt * hg * hc;                // <= blockDim by construction of tpb
@@ -366,7 +519,11 @@ __global__ void __launch_bounds__(256, 6) rope_tokens_kernel(
         }
     }
     cp_async_commit();
-    // ---- 2. angle table (one float4 = two consecutive d)
+    // ---- 2. angle table (one float4 = two consecutive d).  The frequencies
+    // go through shared memory first: a kernel parameter read at a per-thread
+    // index is serialised by the constant cache.
+    for (int i = threadIdx.x; i < half; i += blockDim.x) fqs[i] = ft.f[i];
+    __syncthreads();
     const int hp = half / 2;
     for (int i = threadIdx.x; i < nt * hp; i += blockDim.x) {
         const int tl = i / hp, dp = i - tl * hp;
@@ -374,8 +531,8 @@ __global__ void __launch_bounds__(256, 6) rope_tokens_kernel(
         const int target = tgt ? tgt[t] : conv_pos + t;
         const float dlt = (float)(target - orig[t]);
         float4 cs;
-        rope_sincos(dlt * ft.f[2 * dp], &cs.y, &cs.x);
-        rope_sincos(dlt * ft.f[2 * dp + 1], &cs.w, &cs.z);
+        rope_sincos(dlt * fqs[2 * dp], &cs.y, &cs.x);
+        rope_sincos(dlt * fqs[2 * dp + 1], &cs.w, &cs.z);
         tab[i] = cs;
     }
     if (INSERT) {
@@ -455,10 +612,11 @@ int tokens_per_block(int H, int half, int N, int hpt, int elem_bytes, bool inser
     int tpb = 256 / per_token;
     // angle table + staged K (and V) rows within the default 48 KB of shared memory
     const int per_tok_smem = (half / 2) * 16 + H * 2 * half * elem_bytes * (insert ? 2 : 1) + (insert ? 8 : 0);
-    return std::min(tpb, (48 * 1024) / per_tok_smem);
+    return std::min(tpb, (48 * 1024 - half * 4) / per_tok_smem);
 }
 size_t rope_tokens_smem(int tpb, int H, int half, int elem_bytes, bool insert) {
-    return (size_t)tpb * ((half / 2) * 16 + (size_t)H * 2 * half * elem_bytes * (insert ? 2 : 1) + (insert ? 8 : 0));
+    return (size_t)tpb * ((half / 2) * 16 + (size_t)H * 2 * half * elem_bytes * (insert ? 2 : 1) + (insert ? 8 : 0)) +
+           (size_t)half * 4;
 }
 
 template <typename T>
@@ -838,6 +996,7 @@ __global__ void fog_weights_kernel(float* __restrict__ w, int n, int cs, float a
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+
 template <typename T>
 int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv, int64_t sts, int64_t shs,
                   int T_, const int32_t* ids, int8_t* valid, int32_t* positions, int conv_pos,
@@ -906,6 +1065,15 @@ int launch_gather(const void* cache, const PageGeom& g, const int32_t* ids, int 
     bool vec = g.head_dim % N == 0 && aligned16(cache) && (!ok || aligned16(ok)) && (!ov || aligned16(ov)) &&
                (g.page_stride * es) % 16 == 0 && (g.token_stride * es) % 16 == 0 &&
                (g.kv_stride * es) % 16 == 0 && (g.head_stride * es) % 16 == 0;
+    const int64_t R = (int64_t)g.num_heads * g.head_dim * es;
+    if (vec && g.head_stride == g.head_dim && bulk_ok(R)) {
+        BulkArgs a{};
+        a.cache = static_cast<const char*>(cache);
+        a.page_b = g.page_stride * es; a.token_b = g.token_stride * es; a.kv_b = g.kv_stride * es;
+        a.max_pages = g.max_pages; a.ps = g.page_size; a.ids = ids;
+        a.rk = (char*)ok; a.rv = (char*)ov; a.R = (int)R; a.units = n; a.status = status;
+        if (launch_gather_bulk(a, st)) return check_launch("page_gather (bulk)");
+    }
     if (vec) {
         page_gather_kernel<T><<<n, 256, 0, st>>>((const T*)cache, g, ids, (T*)ok, (T*)ov, status);
     } else {

@@ -1,6 +1,6 @@
 // ptx.cuh -- inline-PTX building blocks for sm_100a kernels:
-// mbarriers with bounded waits, TMA tensor loads (no multicast), ldmatrix,
-// movmatrix, mma.sync, tcgen05 helpers.
+// mbarriers with bounded waits, TMA tensor loads and bulk copies (no
+// multicast), ldmatrix, movmatrix, mma.sync, tcgen05 helpers.
 #pragma once
 
 #include <cuda.h>
@@ -75,6 +75,28 @@ __device__ __forceinline__ void tma_load_5d_hint(void* dst, const CUtensorMap* m
            "r"(c4), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// ------------------------------------------------------------------ bulk (non-tensor) async copies, no multicast
+// global -> shared, completing on an mbarrier's transaction count.  Both
+// addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+// shared -> global, tracked in the issuing thread's bulk groups.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 :: "l"(dst), "r"(smem_u32(src)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's bulk groups still read shared memory.
+template <int N> __device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory");
+}
+// Wait until at most N of this thread's bulk groups are incomplete.
+template <int N> __device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" :: "n"(N) : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -45,6 +45,9 @@ int check_launch(const char* what) {
     return KESSIE_OK;
 }
 
+// Device address of the status word on the current device, looked up once per
+// device and cached for the life of the process (a cudaDeviceReset of the
+// device would leave it stale; the library is not used across one).
 int* device_status_ptr() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;

@@ -22,6 +22,7 @@
 // pack + one device-to-host copy and a recall one host-to-device copy + one
 // unpack.
 #include "common.cuh"
+#include "ptx.cuh"
 
 #include <math.h>
 
@@ -71,8 +72,15 @@ constexpr int kItems = 4;                                  // 16-byte items in f
 
 // grid (x over the rows of one (b, h), y = b * H + h): rows [0, S) are the
 // fogged V (or [0, T) the V append when the fog is off), then T K-append rows.
+// Launched as a programmatic dependent of whatever precedes it on the stream
+// (the previous layer's update in a decode step): every CTA lets the next
+// launch start right away, then waits for the preceding grid to complete
+// before touching memory, so the next launch's scheduling and start-up
+// overlap this one's tail instead of following it.
 template <typename T, int CH>
 __global__ void __launch_bounds__(256) tiered_update_kernel(TieredUpdateArgs a) {
+    ptx::launch_dependents();
+    ptx::grid_dependency_wait();
     const int chunks = CH > 0 ? CH : a.chunks;
     const long long rb = (long long)chunks * 16;
     const int bh = blockIdx.y, b = bh / a.H, h = bh - b * a.H;
@@ -211,7 +219,18 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
     if (rows == 0) { clear_error(); return 0; }
     cudaStream_t st = as_stream(stream);
     const dim3 grid(grid_x(rows * a.chunks, (long long)B * H), B * H);
-    auto launch = [&](auto kern) { kern<<<grid, 256, 0, st>>>(a); };
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t lerr = cudaSuccess;
+    auto launch = [&](auto kern) { lerr = cudaLaunchKernelEx(&cfg, kern, a); };
     if (dtype == KESSIE_DTYPE_BF16) {
         if (a.chunks == 16) launch(tiered_update_kernel<__nv_bfloat16, 16>);
         else if (a.chunks == 8) launch(tiered_update_kernel<__nv_bfloat16, 8>);
@@ -224,6 +243,10 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
         if (a.chunks == 32) launch(tiered_update_kernel<float, 32>);
         else if (a.chunks == 16) launch(tiered_update_kernel<float, 16>);
         else launch(tiered_update_kernel<float, 0>);
+    }
+    if (lerr != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(KESSIE_ERR_CUDA, "tiered_update: %s", cudaGetErrorString(lerr));
     }
     return check_launch("tiered_update");
 }

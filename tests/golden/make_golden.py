@@ -7,11 +7,11 @@ seeded numpy inputs and stores their outputs.  Inputs are not stored when
 they can be regenerated from the recorded seed (numpy PCG64 standard_normal
 is stable across numpy versions); the oracle tests regenerate them.
 
-Needs the reference source tree (default /root/reference, or $KESSIE_REF);
-it is run once in the build container and its outputs are committed.  Nothing
-on the GPU box runs this script.
+Needs the reference source tree, named by $KESSIE_REF; it is run once where
+that tree exists and its outputs are committed.  Nothing on the GPU box runs
+this script.
 
-    python tests/golden/make_golden.py
+    KESSIE_REF=<reference tree> python tests/golden/make_golden.py
 """
 
 import os
@@ -20,7 +20,9 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("KESSIE_REF", "/root/reference")
+REF = os.environ.get("KESSIE_REF")
+if not REF or not os.path.exists(os.path.join(REF, "kessie_hip_kernels.py")):
+    sys.exit("make_golden.py: set KESSIE_REF to the reference source tree (kessie_hip_kernels.py not found)")
 sys.dont_write_bytecode = True
 sys.path.insert(0, REF)
 

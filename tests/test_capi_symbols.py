@@ -88,3 +88,47 @@ def test_index_query_and_tiered_cache_argument_errors_without_gpu():
     # strided pack: row bytes not a multiple of 16
     assert lib.kessie_strided_pack_v2(16, 16, 2, 8, 10, 24, 16, 0, None) == ERR_ARG
     assert lib.kessie_strided_pack_v2(None, 16, 2, 8, 10, 32, 16, 0, None) == ERR_ARG
+
+
+LEGACY = ["launch_kessie_windowed_attn", "launch_kessie_fused_fog_attn", "launch_kessie_page_evict",
+          "launch_kessie_page_insert", "launch_kessie_rope_remap"]
+
+
+def header_param_ctypes(name):
+    """ctypes types of a legacy launcher's parameters as include/kessie_capi.h
+    declares them (pointer -> c_void_p, float -> c_float, int -> c_int)."""
+    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    m = re.search(r"void\s+" + name + r"\s*\(([^)]*)\)", src)
+    assert m, name
+    out = []
+    for p in m.group(1).split(","):
+        p = p.strip()
+        out.append(ctypes.c_void_p if "*" in p else ctypes.c_float if p.startswith("float") else ctypes.c_int)
+    return out
+
+
+def test_reference_ctypes_class_binds_this_library():
+    """The reference's own, unmodified KeSSieKernels (kessie_hip_ctypes.py:42-114)
+    loads this library under the name it searches for and binds all five
+    launchers; the argument types it sets are the ones the header declares.
+    Needs the reference tree: set KESSIE_REF to its directory."""
+    import importlib.util
+    import sys
+    ref = os.environ.get("KESSIE_REF")
+    if not ref or not os.path.exists(os.path.join(ref, "kessie_hip_ctypes.py")):
+        pytest.skip("KESSIE_REF (the reference source tree) is not set")
+    lib_path = os.path.join(ROOT, "kessie_b200", "build", "libkessie_hip.so")
+    old = sys.dont_write_bytecode
+    sys.dont_write_bytecode = True            # the reference tree is read-only
+    try:
+        spec = importlib.util.spec_from_file_location("kessie_ref_hip_ctypes",
+                                                      os.path.join(ref, "kessie_hip_ctypes.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        sys.dont_write_bytecode = old
+    kernels = mod.KeSSieKernels(lib_path=lib_path)
+    for name in LEGACY:
+        fn = getattr(kernels.lib, name)
+        assert fn.restype is None, name
+        assert list(fn.argtypes) == header_param_ctypes(name), name
