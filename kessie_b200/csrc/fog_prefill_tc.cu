@@ -4,24 +4,32 @@
 // Semantics are those of fog_prefill.cu (kessie_hip_kernels.py:577-593 with a
 // query offset, GQA, paged or dense KV): O_i = sum_j p_ij w_j v_j / sum_j p_ij.
 //
-// CTA = 128 query rows of one KV head (rows are (token, head-in-group) pairs,
-// so the Hq/Hkv heads sharing a KV head share every K/V tile), 6 warps:
-//   warp 0     TMA producer: Q once; per 128-key tile the K and V boxes
-//              (16..128 tokens each, one per d-half) into 3- / 2-stage rings.
-//   warp 1     TMEM owner and MMA issuer (one thread):
-//                S_j  = Q K_j^T           tcgen05.mma  SS, M128 N128 K16 x 8  -> TMEM S[j%2]
-//                O   += P_{j-1} V_{j-1}   tcgen05.mma  TS (P in TMEM), V MN-major -> TMEM O
-//              S_j is issued before PV_{j-1}, so the tensor core computes the
-//              next scores while the softmax warps work on the current ones.
-//   warps 2-5  softmax, one row per thread (TMEM lane = row): tcgen05.ld S,
-//              mask (boundary tiles only), online max, p = 2^(s*scale - m),
-//              row sum of p (unweighted), P' = p * w_j (fog), tcgen05.st P'.
-//              The running max is only moved (and O rescaled in TMEM) when it
-//              grows by more than 2^8, so p <= 256 and the rescale is rare;
-//              the final O / l is exact either way.
-// TMEM: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512) columns.
-// Every mbarrier wait is bounded; on a timeout all warps still reach the final
-// barrier and the TMEM is freed.
+// CTA = two 128-row Q tiles (A, B) of one KV head -- rows are (token,
+// head-in-group) pairs, so the Hq/Hkv heads sharing a KV head share every K/V
+// tile -- and 12 warps:
+//   warps 0-3 / 4-7  softmax warpgroups, one per Q tile, one row per thread
+//              (TMEM lane = row): tcgen05.ld S, mask (boundary tiles only),
+//              online max, p = 2^(s*scale - m) with packed fp32 pairs, row sum
+//              of p, P = p (or p * w when the fog is applied in-kernel: the
+//              staged path folds the fog weights into V), tcgen05.st P.  The
+//              running max moves (and O is rescaled in TMEM, after P) only
+//              when it grows by more than 2^8.
+//   warp 8     Q loader, then the K producer: 128-key K tiles (one TMA box per
+//              d-half) into a 2-stage ring.
+//   warp 9     TMEM owner (512 columns) and MMA issuer (one thread), per KV
+//              tile t:  PV_A(t) S_A(t+1) PV_B(t) S_B(t+1), where
+//                S_X  = Q_X K^T     tcgen05.mma SS, M128 N128 K16 x 8
+//                O_X += P_X V       tcgen05.mma TS (P in TMEM), V MN-major
+//              so the tensor core computes one tile's scores while the other
+//              tile's softmax runs.
+//   warp 10    V producer: 128-key V tiles into a 2-stage ring.
+//   warp 11    idle (keeps the producer warpgroup whole for setmaxnreg).
+// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_X
+// (16-bit pairs) overwrites the first 64 columns of S_X.
+// setmaxnreg: the producer warpgroup drops to 64 registers, the softmax
+// warpgroups rise to 216 (launch 168; the host checks the launch pool).
+// Every mbarrier wait is bounded; on a timeout all warps still reach the
+// final barrier and the TMEM is freed.
 #include "common.cuh"
 #include "ptx.cuh"
 #include "tma_host.cuh"

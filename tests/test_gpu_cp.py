@@ -1,8 +1,8 @@
 """Multi-GPU parity of the context-parallel decode, both exchanges (NVLink
 peer stores from the decode kernel + bounded-wait combine; NCCL all-gather +
-LSE merge kernel): two ranks, each holding a contiguous position shard of every
+LSE merge kernel): 2, 4 or 8 ranks, each holding a contiguous position shard of every
 sequence, must reproduce the single-GPU decode over the whole cache.
-Skipped with fewer than two GPUs."""
+Skipped with fewer GPUs than ranks."""
 
 import os
 import queue
@@ -69,13 +69,14 @@ def _rank(rank, world, port, out_q):
     dist.destroy_process_group()
 
 
-def test_context_parallel_two_gpus_matches_single_gpu():
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_context_parallel_gpus_match_single_gpu(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     out_q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, out_q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, out_q)) for r in range(world)]
     for p in procs:
         p.start()
     deadline = time.time() + 300
