@@ -209,7 +209,10 @@ int kessie_build_fog_weights_v2(float* out, int seq_len, int clear_start, float 
  *   out [B, Hq, D] (dtype) and/or out_partial fp32 [B, Hq, D+2] holding
  *   (O/l, m, l) with m in natural-log units of the scaled scores -- the
  *   triple merged across context-parallel shards by kessie_lse_combine_v2.
- *   D in {64, 128}; dtype f16 or bf16; Hq % Hkv == 0; Hq/Hkv <= 16.
+ *   D in {64, 128}; dtype f16, bf16 or f32; Hq % Hkv == 0; Hq/Hkv <= 16.
+ *   f32 (q, caches and out all fp32) runs every product in fp32 on the CUDA
+ *   cores, for the reference's fp32 path at its 1e-4 bar; the additive-bias
+ *   and context-parallel forms below take f16 / bf16 only.
  * workspace: kessie_paged_fog_decode_workspace_size(...) bytes. */
 size_t kessie_paged_fog_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
                                               int head_dim, int max_seq_len, int page_size);
