@@ -235,19 +235,23 @@ def kessie_fused_fog_attention_ref(q, k, v, fog_weights, window_size=0, causal=T
 
 
 def _rope_remap_ref(k_tensor, orig_positions, target_positions, rope_theta=10000.0):
-    """Rotate-half re-rotation in fp32 from the loaded pair (the HIP kernel's
-    arithmetic, kessie_kernels_v2.hip:697-706).  The reference's torch version
-    reads the first half back after overwriting it when K is fp32
-    (``.float()`` is a view there); this one always rotates from copies."""
+    """In-place rotate-half re-rotation by torch ops, computing exactly what
+    the reference's checker computes (kessie_hip_kernels.py:596-606), so code
+    that uses it as its checker gets the same numbers.  For an fp32 K the
+    ``.float()`` of the low half is a view of K itself: the high half is then
+    rotated from the already-rotated low half.  The library's kernels follow
+    the HIP rule instead (kessie_kernels_v2.hip:697-706: both halves from the
+    loaded pair); for fp16 / bf16 K the two agree."""
     num_tokens, num_heads, head_dim = k_tensor.shape
     half_dim = head_dim // 2
-    freqs = 1.0 / (rope_theta ** (torch.arange(half_dim, dtype=torch.float32, device=k_tensor.device) / half_dim))
+    exponents = torch.arange(half_dim, dtype=torch.float32, device=k_tensor.device) / half_dim
+    freqs = 1.0 / (rope_theta ** exponents)
     delta = torch.outer((target_positions - orig_positions).float(), freqs)
     cos_d, sin_d = delta.cos()[:, None, :], delta.sin()[:, None, :]
-    k1 = k_tensor[:, :, :half_dim].float().clone()
-    k2 = k_tensor[:, :, half_dim:].float().clone()
-    k_tensor[:, :, :half_dim] = (k1 * cos_d - k2 * sin_d).to(k_tensor.dtype)
-    k_tensor[:, :, half_dim:] = (k1 * sin_d + k2 * cos_d).to(k_tensor.dtype)
+    low = k_tensor[:, :, :half_dim].float()        # a view of k_tensor when K is fp32
+    high = k_tensor[:, :, half_dim:].float()
+    k_tensor[:, :, :half_dim] = (low * cos_d - high * sin_d).to(k_tensor.dtype)
+    k_tensor[:, :, half_dim:] = (low * sin_d + high * cos_d).to(k_tensor.dtype)
     return k_tensor
 
 

@@ -243,3 +243,21 @@ def test_vector_index_search_fp32_reproduces_reference(golden_dir):
         np.testing.assert_array_equal(ids, d[f"q{qi}_ids"])
         np.testing.assert_allclose(scores, d[f"q{qi}_scores"], rtol=1e-6)
     assert len(O.vector_index_search_fp32(rows, np.full(dim, 1e-12, np.float32), 10)[0]) == int(d["tiny_query_result_len"])
+
+
+def test_mirror_rope_remap_ref_equals_the_reference_checker(golden_dir):
+    """The mirror module's _rope_remap_ref gives the reference checker's own
+    numbers (kessie_hip_kernels.py:596-606), fp32 view behaviour included:
+    checked against the golden outputs the reference produced."""
+    import torch
+    from kessie_b200 import kessie_hip_kernels as K
+    d = load(golden_dir, "rope_remap.npz")
+    for i in range(5):
+        dt = str(d[f"case{i}_dtype"])
+        theta = float(d[f"case{i}_meta"][4])
+        kin = d[f"case{i}_kin"]
+        tdt = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}[dt]
+        k = torch.from_numpy(np.ascontiguousarray(kin, dtype=np.float32)).to(tdt)
+        out = K._rope_remap_ref(k, torch.from_numpy(d[f"case{i}_orig"].astype(np.int32)),
+                                torch.from_numpy(d[f"case{i}_tgt"].astype(np.int32)), theta)
+        np.testing.assert_array_equal(out.float().numpy(), d[f"case{i}_kout"], err_msg=f"case {i} ({dt})")
