@@ -98,11 +98,6 @@ __device__ __forceinline__ float fog_weight_f32(const DecodeF32Args& p, int cs, 
     return p.fog_alpha == 0.5f ? sqrtf(t) : powf(t, p.fog_alpha);
 }
 
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory");
-}
-
 // Count one arrival at a group counter; returns the arrivals before this one
 // (a counter holding another launch's tag counts as zero).
 __device__ __forceinline__ unsigned arrive_tagged(unsigned long long* c, uint32_t tag) {
@@ -220,7 +215,7 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
     }
     const int kk = lane >> 2, dq = lane & 3;
     for (int i = 0; i < nw; ++i) {
-        cp_async_wait<kNS - 2>();
+        cp_async_wait_group<kNS - 2>();
         __syncwarp();
         {
             const int nx = i + kNS - 1;
@@ -343,7 +338,7 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
             }
         }
     }
-    cp_async_wait<0>();
+    cp_async_wait_group<0>();
     __syncthreads();
 
     // ---- merge the 8 warps (each writes into its own stage area)

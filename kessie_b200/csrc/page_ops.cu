@@ -466,14 +466,16 @@ void launch_rows(int kt, dim3 grid, int threads, size_t smem, cudaStream_t st, T
 // sin d+1); then wait, barrier, rotate out of shared memory and store.
 // INSERT: destination row of token t is page page_ids[t / ps], slot t % ps
 // (first token of a page sets page_valid / page_positions); the V rows are
-// copied alongside.
+// copied alongside.  With bulk_st (destination rows of H*D contiguous
+// elements) the insert writes its rotated K rows back into shared memory and
+// every K and V row leaves as one shared->global bulk copy.
 template <typename T, bool INSERT, int HPT>
 __global__ void __launch_bounds__(256, 6) rope_tokens_kernel(
     T* __restrict__ dst, const T* __restrict__ srck, const T* __restrict__ srcv, int num_tokens, int num_heads,
     int half, int64_t sts, int64_t shs, int64_t dts, int64_t dhs, int64_t dkv, int64_t page_stride, int ps,
     const int32_t* __restrict__ page_ids, int max_pages, int8_t* __restrict__ valid, int32_t* __restrict__ positions,
     int conv_pos, const int32_t* __restrict__ orig, const int32_t* __restrict__ tgt, FreqTable ft, int tpb,
-    int* status) {
+    int* status, int bulk_st) {
     extern __shared__ float4 tab[];                 // [tpb][half/2] of (cos d, sin d, cos d+1, sin d+1)
     constexpr int N = VecOps<T>::N;
     const int hc = half / N;                        // 16-byte chunks per half row
@@ -579,6 +581,13 @@ __global__ void __launch_bounds__(256, 6) rope_tokens_kernel(
                 ra[2 * q + 1] = a[2 * q + 1] * cs[q].z - bb[2 * q + 1] * cs[q].w;
                 rb[2 * q + 1] = a[2 * q + 1] * cs[q].w + bb[2 * q + 1] * cs[q].z;
             }
+            if (INSERT && bulk_st) {
+                // rotated in place; the rows leave through the bulk-copy engine below
+                T* wrow = ksm + ktl * rowe + (g + j * hg) * 2 * half;
+                *reinterpret_cast<uint4*>(wrow + kc * N) = VecOps<T>::pack(ra);
+                *reinterpret_cast<uint4*>(wrow + half + kc * N) = VecOps<T>::pack(rb);
+                continue;
+            }
             bool ok;
             T* row = dst_row(ktl, g + j * hg, ok);
             if (ok) {
@@ -586,6 +595,26 @@ __global__ void __launch_bounds__(256, 6) rope_tokens_kernel(
                 *reinterpret_cast<uint4*>(row + half + kc * N) = VecOps<T>::pack(rb);
             }
         }
+    }
+    if (INSERT && bulk_st) {
+        // every destination row is one contiguous run of H*D elements: one
+        // shared->global bulk copy per K and V row, issued by one thread,
+        // which waits until they have read shared memory before the CTA exits
+        ptx::fence_proxy_async_smem();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const uint32_t rb = (uint32_t)(rowe * sizeof(T));
+            for (int tl = 0; tl < nt; ++tl) {
+                bool ok;
+                T* row = dst_row(tl, 0, ok);
+                if (!ok) continue;
+                ptx::bulk_s2g(row, ksm + tl * rowe, rb);
+                ptx::bulk_s2g(row + dkv, vsm + tl * rowe, rb);
+            }
+            ptx::bulk_commit();
+            ptx::bulk_wait_read<0>();
+        }
+        return;
     }
     if (INSERT) {
 #pragma unroll
@@ -638,7 +667,7 @@ int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int
         auto kern = hpt == 2 ? rope_tokens_kernel<T, false, 2> : rope_tokens_kernel<T, false, 1>;
         kern<<<(T_ + tpb_t - 1) / tpb_t, 256, smem, st>>>(
             (T*)k, (const T*)k, nullptr, T_, H, half, ts, hs, ts, hs, 0, 0, 1, nullptr, 0, nullptr, nullptr, 0, orig, tgt,
-            ft, tpb_t, nullptr);
+            ft, tpb_t, nullptr, 0);
     } else if (vec && rows_shape<T>(H, D, tt, threads, cpr, kt)) {
         size_t smem = (size_t)2 * tt * half * sizeof(float);
         launch_rows<T, 0>(kt, dim3((T_ + tt - 1) / tt), threads, smem, st, (T*)k, (const T*)k, nullptr, T_, H, half,
@@ -1017,10 +1046,12 @@ int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv
         FreqTable ft = make_freqs(theta, g.head_dim / 2);
         size_t smem = rope_tokens_smem(tpb_i, g.num_heads, g.head_dim / 2, es, true);
         auto kern = hpt == 2 ? rope_tokens_kernel<T, true, 2> : rope_tokens_kernel<T, true, 1>;
+        // destination rows of all heads contiguous: K and V rows leave as bulk copies
+        const int bulk_st = (g.head_stride == g.head_dim && ((int64_t)g.num_heads * g.head_dim * es) % 16 == 0) ? 1 : 0;
         kern<<<(T_ + tpb_i - 1) / tpb_i, 256, smem, st>>>(
             (T*)cache, (const T*)nk, (const T*)nv, T_, g.num_heads, g.head_dim / 2, sts, shs, g.token_stride,
             g.head_stride, g.kv_stride, g.page_stride, g.page_size, ids, g.max_pages, valid, positions, conv_pos, orig,
-            tgt, ft, tpb_i, status);
+            tgt, ft, tpb_i, status, bulk_st);
     } else if (orig && vec && g.page_size <= 256 && rows_shape<T>(g.num_heads, g.head_dim, g.page_size, threads, cpr, kt)) {
         FreqTable ft = make_freqs(theta, g.head_dim / 2);
         size_t smem = (size_t)2 * g.page_size * (g.head_dim / 2) * sizeof(float);
