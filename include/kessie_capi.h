@@ -229,7 +229,8 @@ int kessie_paged_fog_decode_v2(const void* q, int64_t q_stride_b, int64_t q_stri
                                void* workspace, size_t workspace_bytes, void* stream);
 
 /* Dense fog attention, any GQA ratio: q/out [B, Hq, N, D], k/v [B, Hkv, N, D]
- * contiguous (f16 or bf16), optional fog_weights fp32 [N].  The _v2 form of
+ * contiguous (f16, bf16 or f32; f32 runs the fp32 CUDA-core decode once per
+ * query row), optional fog_weights fp32 [N].  The _v2 form of
  * launch_kessie_fused_fog_attn / launch_kessie_windowed_attn
  * (kessie_hip_kernels.py:367-440, semantics :577-593). */
 int kessie_fog_attention_v2(const void* q, const void* k, const void* v, void* out, int dtype,

@@ -32,9 +32,18 @@ struct DecodeF32Args {
     float* part_ml;               // [slots][G][2]
     float* part_o;                // [slots][G][D]
     int slots;
-    float* out;                   // [B][Hq][D] or null
+    float* out;                   // rows at out + b * out_sb + h * out_sh, or null
+    int64_t out_sb, out_sh;       // element strides of out per sequence and per query head
     float* out_part;              // [B][Hq][D+2] or null
     int* status;
+    // Dense square attention (square_n > 0): "sequence" r of the launch is query
+    // row square_row0 + r of an N = square_n token sequence -- N keys, query
+    // position square_row0 + r (N - 1 when neither causal nor windowed),
+    // offset 0; seq_lens, kv_off and q_pos are not read.  block_table ==
+    // nullptr: page id = page index.
+    int square_n;
+    int square_row0;              // query row of "sequence" 0 of the launch
+    int causal;
 };
 
 // Launches the fp32 decode (argument checks done by the caller).

@@ -1007,7 +1007,8 @@ int decode_entry(const void* q, int64_t q_stride_b, int64_t q_stride_h, const vo
         a.fog_alpha = fog_alpha; a.fog_w = fog_weights; a.window = window_size; a.sm_scale = sm_scale;
         a.B = batch; a.Hq = num_q_heads; a.Hkv = num_kv_heads; a.D = head_dim; a.max_seq_len = pl.max_units * 16;
         a.counters = p.counters; a.tag = p.tag; a.part_ml = p.part_ml; a.part_o = p.part_o; a.slots = pl.slots;
-        a.out = static_cast<float*>(out); a.out_part = out_partial; a.status = p.status;
+        a.out = static_cast<float*>(out); a.out_sb = (int64_t)num_q_heads * head_dim; a.out_sh = head_dim;
+        a.out_part = out_partial; a.status = p.status;
         return launch_decode_f32(a, as_stream(stream));
     }
     p.out = out;

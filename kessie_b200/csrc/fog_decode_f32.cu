@@ -73,6 +73,15 @@ struct SeqF32 {
 
 __device__ __forceinline__ SeqF32 seq_f32(const DecodeF32Args& p, int b) {
     SeqF32 s;
+    if (p.square_n > 0) {
+        const int qp = (p.causal || p.window > 0) ? p.square_row0 + b : p.square_n - 1;
+        s.off = 0;
+        s.k_hi = min(p.square_n, qp + 1);
+        s.k_lo = p.window > 0 ? max(0, qp - p.window + 1) : 0;
+        if (s.k_hi < s.k_lo) s.k_hi = s.k_lo;
+        s.cs = 0;
+        return s;
+    }
     const int cap = ((p.max_seq_len + 15) / 16) * 16;
     int n = p.seq_lens[b];
     if (n < 0 || n > cap) {
@@ -111,11 +120,11 @@ __device__ __forceinline__ unsigned arrive_tagged(unsigned long long* c, uint32_
     }
 }
 
-__device__ __forceinline__ void emit_f32(const DecodeF32Args& p, int row, int d, float o, float M, float L) {
+__device__ __forceinline__ void emit_f32(const DecodeF32Args& p, int b, int h, int d, float o, float M, float L) {
     const int D = p.D;
-    if (p.out) p.out[(int64_t)row * D + d] = o;
+    if (p.out) p.out[(int64_t)b * p.out_sb + (int64_t)h * p.out_sh + d] = o;
     if (p.out_part) {
-        float* dst = p.out_part + (int64_t)row * (D + 2);
+        float* dst = p.out_part + ((int64_t)b * p.Hq + h) * (D + 2);
         dst[d] = o;
         if (d == 0) {
             dst[D] = M == -INFINITY ? -INFINITY : M * kLn2;
@@ -168,14 +177,14 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
     const int cb = c_lo + split * per;
     const int ce = min(c_lo + nch, cb + per);
     const int nw = ce > cb + warp ? (ce - cb - warp + kW - 1) / kW : 0;
-    const int32_t* bt = p.block_table + (int64_t)b * p.bt_stride;
+    const int32_t* bt = p.block_table ? p.block_table + (int64_t)b * p.bt_stride : nullptr;
 
     // Starts the copies of this warp's chunk i into stage i % kNS; returns
     // true (and copies nothing) when the chunk's page id is out of range.
     auto issue = [&](int i) -> bool {
         const int key0 = (cb + warp + i * kW) * 8;
         const int pi = key0 / p.page_size, tok = key0 - pi * p.page_size;
-        const int page = __ldg(bt + pi);
+        const int page = p.block_table ? __ldg(bt + pi) : pi;
         if (page < 0 || page >= p.num_pages) {
             if (lane == 0) record_status(p.status, KESSIE_DEV_BAD_PAGE_ID);
             return true;
@@ -185,10 +194,14 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
         const int64_t base = (int64_t)page * p.page_stride + (int64_t)tok * p.token_stride + (int64_t)hk * p.head_stride;
         const float* gK = p.k_cache + base;
         const float* gV = p.v_cache + base;
+        // rows at or past the visible end are never read (they are masked
+        // anyway): a dense cache may end inside the chunk
+        const int rows = min(8, si.k_hi - key0);
 #pragma unroll
         for (int t = 0; t < 8 * RC / 32; ++t) {
             const int idx = t * 32 + lane;
             const int r = idx / RC, x = idx - r * RC;
+            if (r >= rows) continue;
             const int64_t src = (int64_t)r * p.token_stride + x * 4;
             cp_async16(dK + r * D + ((x ^ (r & 7)) << 2), gK + src);
             cp_async16(dV + r * D + (x << 2), gV + src);
@@ -376,7 +389,6 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
     }
     __syncthreads();
 
-    const int row0 = b * p.Hq + hk * G;
     if (S == 1) {
         for (int i = threadIdx.x; i < G * D; i += kT) {
             const int g = i / D, d = i - g * D;
@@ -386,7 +398,7 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
                 for (int w2 = 0; w2 < kW; ++w2) o = fmaf(warp_area(w2)[2 * GP + g * D + d], sSC[w2 * GP + g], o);
                 o /= L;
             }
-            emit_f32(p, row0 + g, d, o, M, L);
+            emit_f32(p, b, hk * G + g, d, o, M, L);
         }
         return;
     }
@@ -447,7 +459,7 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
             }
             o /= L;
         }
-        emit_f32(p, row0 + g, d, o, M, L);
+        emit_f32(p, b, hk * G + g, d, o, M, L);
     }
     if (threadIdx.x == 0) p.counters[grp] = 0ull;     // graph replays (same tag) start clean
 }
@@ -470,6 +482,8 @@ int launch_f32_t(const DecodeF32Args& a, int S, cudaStream_t st) {
 int launch_decode_f32(const DecodeF32Args& a, cudaStream_t st) {
     const int G = a.Hq / a.Hkv;
     const int groups = a.B * a.Hkv;
+    if (groups > 65535)
+        return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode (fp32): B * Hkv = %d above 65535", groups);
     const int max_chunks = (a.max_seq_len + 7) / 8 + 1;
     // about one CTA per SM in total, at least two chunks per warp, and no
     // more splits than the workspace has slots for

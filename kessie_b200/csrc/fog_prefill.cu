@@ -19,11 +19,14 @@
 //   S = Q K^T (mma.sync m16n8k16), mask, online softmax (quad shuffles),
 //   P' = P * w_j, O += P' V (ldmatrix.trans of V).
 #include "common.cuh"
+#include "decode_f32.cuh"
 #include "ptx.cuh"
 #include "tma_host.cuh"
 #include "prefill_common.cuh"
 
 #include <math.h>
+
+#include <algorithm>
 
 namespace kessie {
 namespace {
@@ -472,13 +475,47 @@ extern "C" int kessie_fog_attention_v2(const void* q, const void* k, const void*
                                        int num_kv_heads, int seq_len, int head_dim, int window_size, int is_causal,
                                        void* stream) {
     NvtxRange nvtx_range("kessie_fog_attention_v2");
-    if (dtype != KESSIE_DTYPE_BF16 && dtype != KESSIE_DTYPE_F16)
-        return set_error(KESSIE_ERR_UNSUPPORTED, "fog_attention_v2: dtype %d (f16/bf16 only)", dtype);
+    if (!dtype_ok(dtype)) return set_error(KESSIE_ERR_UNSUPPORTED, "fog_attention_v2: dtype %d", dtype);
     if (head_dim != 64 && head_dim != 128)
         return set_error(KESSIE_ERR_UNSUPPORTED, "fog_attention_v2: head_dim %d", head_dim);
     if (!q || !k || !v || !out || batch <= 0 || seq_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 ||
         num_q_heads % num_kv_heads)
         return set_error(KESSIE_ERR_ARG, "fog_attention_v2: bad arguments");
+    if (dtype == KESSIE_DTYPE_F32) {
+        // fp32 (the reference's own precision): every query row is one
+        // "sequence" of the fp32 paged decode over this batch's K/V viewed as
+        // 16-token pages (page p = tokens [16p, 16p + 16), head stride N*D);
+        // one launch per batch, no workspace (a single split per row).
+        if (num_q_heads / num_kv_heads > 16)
+            return set_error(KESSIE_ERR_UNSUPPORTED, "fog_attention_v2: Hq/Hkv > 16 in fp32");
+        if (((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15))
+            return set_error(KESSIE_ERR_ARG, "fog_attention_v2: k/v must be 16-byte aligned");
+        const int64_t sq = (int64_t)num_q_heads * seq_len * head_dim, skv = (int64_t)num_kv_heads * seq_len * head_dim;
+        const int rows_per_launch = 65535 / num_kv_heads;        // grid y = rows x KV heads
+        cudaStream_t st = as_stream(stream);
+        for (int b = 0; b < batch; ++b)
+        for (int r0 = 0; r0 < seq_len; r0 += rows_per_launch) {
+            DecodeF32Args a{};
+            a.q = static_cast<const float*>(q) + b * sq + (int64_t)r0 * head_dim;
+            a.q_sb = head_dim; a.q_sh = (int64_t)seq_len * head_dim;
+            a.k_cache = static_cast<const float*>(k) + b * skv;
+            a.v_cache = static_cast<const float*>(v) + b * skv;
+            a.page_stride = 16 * (int64_t)head_dim; a.token_stride = head_dim;
+            a.head_stride = (int64_t)seq_len * head_dim;
+            a.num_pages = (seq_len + 15) / 16; a.page_size = 16;
+            a.fog_w = fog_weights; a.window = window_size > 0 ? window_size : 0; a.sm_scale = sm_scale;
+            a.B = std::min(rows_per_launch, seq_len - r0); a.Hq = num_q_heads; a.Hkv = num_kv_heads; a.D = head_dim;
+            a.max_seq_len = (seq_len + 15) / 16 * 16;
+            a.slots = 0;                                   // one split per row: no workspace
+            a.out = static_cast<float*>(out) + b * sq + (int64_t)r0 * head_dim;
+            a.out_sb = head_dim; a.out_sh = (int64_t)seq_len * head_dim;
+            a.status = device_status_ptr();
+            a.square_n = seq_len; a.square_row0 = r0; a.causal = is_causal ? 1 : 0;
+            const int rc = launch_decode_f32(a, st);
+            if (rc) return rc;
+        }
+        return 0;
+    }
     PrefillParams p{};
     const int64_t qsb = (int64_t)num_q_heads * seq_len * head_dim, ksb = (int64_t)num_kv_heads * seq_len * head_dim;
     const int64_t sh = (int64_t)seq_len * head_dim;

@@ -54,7 +54,7 @@ def kessie_fused_fog_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor
                                sm_scale: Optional[float] = None) -> torch.Tensor:
     """Flash attention with fused fog decay on V (kessie_hip_kernels.py:367-400).
 
-    q: [Z, Hq, N, D]; k, v: [Z, Hkv, N, D] (fp16 or bf16); fog_weights: [N]
+    q: [Z, Hq, N, D]; k, v: [Z, Hkv, N, D] (fp16, bf16 or fp32); fog_weights: [N]
     float32, 1.0 = clear, < 1.0 = fogged."""
     Z, H, N, D = q.shape
     assert fog_weights.shape == (N,)

@@ -446,7 +446,7 @@ def lse_combine(partials: torch.Tensor, out: Optional[torch.Tensor] = None, out_
 def fog_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, fog_weights: Optional[torch.Tensor] = None,
                   window_size: int = 0, causal: bool = True, sm_scale: Optional[float] = None,
                   out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
-    """Dense fog attention: q [B, Hq, N, D], k/v [B, Hkv, N, D] (f16/bf16,
+    """Dense fog attention: q [B, Hq, N, D], k/v [B, Hkv, N, D] (f16/bf16/f32,
     contiguous), fog_weights fp32 [N] or None (kessie_hip_kernels.py:367-440)."""
     _need_cuda(q, k, v, fog_weights)
     if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):

@@ -194,3 +194,70 @@ def test_decode_fp32_rejects_the_additive_bias():
         ops.paged_fog_decode(to_dev(rnd(92, (1, 8, 128)), "fp32"), kv[:, :, 0], kv[:, :, 1], bt,
                              torch.tensor([64], dtype=torch.int32, device="cuda"),
                              bias=ops.FogBias(0.5, 0.5, dtype=torch.float32))
+
+
+# ---------------------------------------------------------------- dense fp32 attention
+def _dense(q, k, v, fog, W, causal):
+    from kessie_b200 import kessie_hip_kernels as K
+    qd, kd, vd = (to_dev(x, "fp32") for x in (q, k, v))
+    if fog is None:
+        out = K.kessie_windowed_attention(qd, kd, vd, W, causal)
+    else:
+        out = K.kessie_fused_fog_attention(qd, kd, vd, torch.from_numpy(np.asarray(fog, np.float32)).cuda(), W,
+                                           causal)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32
+    return to_np(out)
+
+
+def test_dense_fp32_reference_test_configs(golden_dir):
+    """The reference's own attention test configurations
+    (kessie_hip_kernels.py:623-626, :647-652) in fp32 through the dense entry
+    points, against the outputs the reference's fp32 torch path recorded."""
+    d = np.load(os.path.join(golden_dir, "attention.npz"))
+    for i in range(int(d["nwin"])):
+        Z, H, N, D, W, causal, seed = (int(x) for x in d[f"win{i}_cfg"])
+        q, k, v = (rnd(seed + j, (Z, H, N, D)) for j in range(3))
+        got = _dense(q, k, v, None, W, bool(causal))
+        np.testing.assert_allclose(got[:, :, d[f"win{i}_rows"]], d[f"win{i}_out"], **TOL["fp32"],
+                                   err_msg=f"windowed config {i}")
+    for i in range(int(d["nfog"])):
+        Z, H, N, D, W, causal, seed = (int(x) for x in d[f"fog{i}_cfg"])
+        a, fs = d[f"fog{i}_fog"]
+        q, k, v = (rnd(seed + j, (Z, H, N, D)) for j in range(3))
+        got = _dense(q, k, v, O.build_fog_weights(N, a, fs), W, bool(causal))
+        np.testing.assert_allclose(got[:, :, d[f"fog{i}_rows"]], d[f"fog{i}_out"], **TOL["fp32"],
+                                   err_msg=f"fog config {i}")
+
+
+def test_dense_fp32_config1_full_square(golden_dir):
+    """Config 1 as the reference evaluates it: the whole 4096 x 4096 fp32
+    attention (GQA 8/2, RoPE'd q/k, fog), whose last row the reference
+    recorded for both fog mappings."""
+    d = np.load(os.path.join(golden_dir, "config1_decode.npz"))
+    B, Hq, Hkv, D, N, W, seed = (int(x) for x in d["cfg"])
+    q = rnd(seed, (N, Hq, D)); k = rnd(seed + 1, (N, Hkv, D)); v = rnd(seed + 2, (N, Hkv, D))
+    pos = np.arange(N); zero = np.zeros(N, np.int64)
+    q = O.rope_remap(q, zero, pos, 1e4).astype(np.float32)
+    k = O.rope_remap(k, zero, pos, 1e4).astype(np.float32)
+    qh, kh, vh = (np.ascontiguousarray(np.transpose(x, (1, 0, 2))[None]) for x in (q, k, v))
+    fog = O.build_fog_weights(N, 0.5, W / N)
+    for win, key in ((0, "out_causal_fog"), (W, "out_window_fog")):
+        got = _dense(qh, kh, vh, fog, win, True)
+        np.testing.assert_allclose(got[0, :, -1], d[key], **TOL["fp32"])
+        rows = np.array([0, 1, 511, 512, 2047, N - 2])
+        want = O.fog_attention_rows(qh[0][:, rows], kh[0], vh[0], rows, fog, window_size=win)
+        np.testing.assert_allclose(got[0][:, rows], want, **TOL["fp32"])
+
+
+@pytest.mark.parametrize("W,causal", [(0, True), (0, False), (37, True), (37, False)])
+def test_dense_fp32_ragged_gqa(W, causal):
+    """N not a multiple of 8 (the last key chunk ends inside the tensor),
+    GQA 6/3, head_dim 64, two sequences, every row against the oracle."""
+    B, Hq, Hkv, N, D = 2, 6, 3, 1001, 64
+    q = rnd(71, (B, Hq, N, D)); k = rnd(72, (B, Hkv, N, D)); v = rnd(73, (B, Hkv, N, D))
+    fog = O.fog_weights_from_clear_start(N, N - 300, 0.5)
+    got = _dense(q, k, v, fog, W, causal)
+    for b in range(B):
+        want = O.fog_attention_rows(q[b], k[b], v[b], np.arange(N), fog, window_size=W, causal=causal)
+        np.testing.assert_allclose(got[b], want, **TOL["fp32"], err_msg=f"sequence {b}")

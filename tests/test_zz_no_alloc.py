@@ -5,7 +5,8 @@ memory when they decode (their allocator is fixed or owned by another
 runtime), so it keeps its split-KV scratch in an array built into the
 library.  This file checks, through the C ABI, that two calls in a row give
 the same results as kessie_paged_fog_decode_v2 with a caller-provided
-workspace, and that a shape too large for the built-in array is refused.
+workspace and as the oracle, and that a shape too large for the built-in
+array is refused.
 The file name sorts last so a run that stops at the first failure has
 already run every other test; it also passes on its own in a fresh process.
 """
@@ -71,6 +72,12 @@ def test_noalloc_decode_matches_workspace_decode_twice():
         _lib.check(lib.kessie_paged_fog_decode_noalloc_v2(*args, got.data_ptr(), None, None), "noalloc decode")
         torch.cuda.synchronize()
         np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(), **TOL)
+        # and directly against the oracle restatement of the reference's decode
+        from oracle import fog_oracle as O
+        kvn = kv.float().cpu().numpy()
+        want = O.paged_fog_decode(q.float().cpu().numpy(), kvn[:, :, 0], kvn[:, :, 1], bt.cpu().numpy(),
+                                  sl.cpu().numpy(), cs.cpu().numpy(), 0.5)
+        np.testing.assert_allclose(got.float().cpu().numpy(), want, **TOL)
 
 
 def test_noalloc_decode_rejects_shapes_beyond_its_scratch():
