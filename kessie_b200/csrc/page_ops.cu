@@ -470,7 +470,7 @@ void launch_rows(int kt, dim3 grid, int threads, size_t smem, cudaStream_t st, T
 // elements) the insert writes its rotated K rows back into shared memory and
 // every K and V row leaves as one shared->global bulk copy.
 template <typename T, bool INSERT, int HPT>
-__global__ void __launch_bounds__(256, 6) rope_tokens_kernel(
+__global__ void __launch_bounds__(256, INSERT ? 5 : 6) rope_tokens_kernel(
     T* __restrict__ dst, const T* __restrict__ srck, const T* __restrict__ srcv, int num_tokens, int num_heads,
     int half, int64_t sts, int64_t shs, int64_t dts, int64_t dhs, int64_t dkv, int64_t page_stride, int ps,
     const int32_t* __restrict__ page_ids, int max_pages, int8_t* __restrict__ valid, int32_t* __restrict__ positions,
