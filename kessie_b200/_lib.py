@@ -146,6 +146,34 @@ def load():
         return _lib
 
 
+_binding = None
+
+
+def load_binding():
+    """The torch extension module `kessie_hip` (kessie_b200/build/kessie_hip.so):
+    the reference's pybind11 boundary (kessie_hip_binding.cpp:216-239) over
+    this library.  Loads libkessie_cuda.so globally first, since the module
+    resolves the launchers from it."""
+    global _binding
+    with _lock:
+        if _binding is None:
+            import importlib.machinery
+            import importlib.util
+            import sys
+            import torch  # noqa: F401  (the module links against libtorch)
+            path = os.path.join(HERE, "build", "kessie_hip.so")
+            if not os.path.exists(path):
+                raise KessieLibraryError(f"{path} not found; build it with `python -m kessie_b200.build`")
+            ctypes.CDLL(library_path(), mode=ctypes.RTLD_GLOBAL)
+            loader = importlib.machinery.ExtensionFileLoader("kessie_hip", path)
+            spec = importlib.util.spec_from_loader("kessie_hip", loader)
+            mod = importlib.util.module_from_spec(spec)
+            loader.exec_module(mod)
+            sys.modules.setdefault("kessie_hip", mod)
+            _binding = mod
+        return _binding
+
+
 def missing_symbols():
     lib = load()
     return [n for n in SIGNATURES if not hasattr(lib, n)]

@@ -84,6 +84,31 @@ def build(force: bool = False, jobs: int = 8, verbose: bool = False) -> str:
     return LIB
 
 
+BINDING_SRC = os.path.join(CSRC, "kessie_hip_binding.cpp")
+BINDING = os.path.join(OUT, "kessie_hip.so")
+
+
+def build_binding(force: bool = False, verbose: bool = False) -> str:
+    """The torch extension module `kessie_hip` (the reference's pybind11
+    boundary, over this library's C ABI), built in-tree with torch's
+    extension builder: kessie_b200/build/kessie_hip.so.  Needs
+    libkessie_cuda.so (its launchers are resolved from it at import)."""
+    hdr = os.path.join(ROOT, "include", "kessie_capi.h")
+    if (not force and os.path.exists(BINDING) and os.path.getmtime(BINDING) >= os.path.getmtime(BINDING_SRC)
+            and os.path.getmtime(BINDING) >= os.path.getmtime(hdr)):
+        return BINDING
+    import ctypes
+    from torch.utils.cpp_extension import load
+    ctypes.CDLL(LIB, mode=ctypes.RTLD_GLOBAL)          # the launchers the module links against
+    bdir = os.path.join(OBJ, "binding")
+    os.makedirs(bdir, exist_ok=True)
+    load(name="kessie_hip", sources=[BINDING_SRC], build_directory=bdir, with_cuda=True,
+         extra_cflags=["-O2"], verbose=verbose)
+    shutil.copyfile(os.path.join(bdir, "kessie_hip.so"), BINDING + ".tmp")
+    os.replace(BINDING + ".tmp", BINDING)
+    return BINDING
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -91,3 +116,4 @@ if __name__ == "__main__":
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
     print(build(a.force, a.jobs, a.verbose))
+    print(build_binding(a.force, a.verbose))

@@ -132,3 +132,26 @@ def test_reference_ctypes_class_binds_this_library():
         fn = getattr(kernels.lib, name)
         assert fn.restype is None, name
         assert list(fn.argtypes) == header_param_ctypes(name), name
+
+
+def test_torch_extension_binding_surface():
+    """The torch extension module kessie_hip exposes the reference binding's
+    five functions (kessie_hip_binding.cpp:216-239) with its argument names and
+    defaults; importing it needs no GPU."""
+    from kessie_b200 import _lib
+    m = _lib.load_binding()
+    want = {
+        "windowed_attention": ["Q", "K", "V", "window_size", "causal"],
+        "fused_fog_attention": ["Q", "K", "V", "fog_weights", "window_size", "causal"],
+        "rope_remap": ["k_data", "orig_positions", "target_positions", "rope_theta"],
+        "page_evict": ["page_valid", "page_positions", "evict_before_pos"],
+        "page_insert": ["kv_cache", "new_keys", "new_values", "target_page_ids", "page_valid", "page_positions",
+                        "insert_conv_position"],
+    }
+    for name, args in want.items():
+        sig = getattr(m, name).__doc__.splitlines()[0]
+        got = re.findall(r"(\w+):", sig[sig.index("(") + 1:sig.rindex(")")])
+        assert got == args, (name, sig)
+    assert "window_size: typing.SupportsInt = 0" in m.windowed_attention.__doc__ or \
+        "window_size: int = 0" in m.windowed_attention.__doc__
+    assert "rope_theta" in m.rope_remap.__doc__ and "10000.0" in m.rope_remap.__doc__
