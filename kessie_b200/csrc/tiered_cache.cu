@@ -26,6 +26,10 @@
 
 #include <math.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 namespace kessie {
 namespace {
 
@@ -66,6 +70,7 @@ struct TieredUpdateArgs {
     int H, T, S, chunks;          // S = live tokens after the append; chunks = row bytes / 16
     int fc, alpha_mode;
     float den, alpha;
+    int early;                    // issue the live-V loads before griddepcontrol.wait
 };
 
 constexpr int kItems = 4;                                  // 16-byte items in flight per thread
@@ -73,14 +78,17 @@ constexpr int kItems = 4;                                  // 16-byte items in f
 // grid (x over the rows of one (b, h), y = b * H + h): rows [0, S) are the
 // fogged V (or [0, T) the V append when the fog is off), then T K-append rows.
 // Launched as a programmatic dependent of whatever precedes it on the stream
-// (the previous layer's update in a decode step): every CTA lets the next
-// launch start right away, then waits for the preceding grid to complete
-// before touching memory, so the next launch's scheduling and start-up
-// overlap this one's tail instead of following it.
+// (the previous layer's update in a decode step).  Every CTA waits for the
+// preceding grid to complete (griddepcontrol.wait) and only then lets the next
+// launch start (launch_dependents), so while a grid runs, every grid launched
+// before its predecessor has completed.  With a.early the loads of the live V
+// rows already in the store are issued BEFORE the wait, overlapping the
+// preceding grid's drain: the host sets it only when the last tiered update
+// launched on this stream wrote none of this V store, so the one grid that
+// can still be running writes no byte these loads read.  Loads of the new
+// tokens (written by the caller's producer) and every store follow the wait.
 template <typename T, int CH>
 __global__ void __launch_bounds__(256) tiered_update_kernel(TieredUpdateArgs a) {
-    ptx::launch_dependents();
-    ptx::grid_dependency_wait();
     const int chunks = CH > 0 ? CH : a.chunks;
     const long long rb = (long long)chunks * 16;
     const int bh = blockIdx.y, b = bh / a.H, h = bh - b * a.H;
@@ -92,21 +100,41 @@ __global__ void __launch_bounds__(256) tiered_update_kernel(TieredUpdateArgs a) 
     const char* vnew = a.v_new + b * a.nsb + h * a.nsh;
     const char* knew = a.k_new + b * a.nsb + h * a.nsh;
     char* vfog = a.v_fog ? a.v_fog + (long long)bh * a.S * rb : nullptr;
+    bool waited = !a.early;
+    if (waited) {
+        ptx::grid_dependency_wait();
+        ptx::launch_dependents();
+    }
     for (int base = blockIdx.x * 256 * kItems + threadIdx.x; base < items; base += gridDim.x * 256 * kItems) {
         uint4 raw[kItems];
+        const char* src[kItems];
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
             const int i = base + u * 256;
+            src[u] = nullptr;
             if (i >= items) break;
             const int r = i / chunks, c = i - r * chunks;
-            const char* src;
+            const bool stored = vfog && r < vrows && r < s_old;
             if (r < vrows) {
-                if (vfog && r < s_old) src = vst + (a.lo + r) * rb;
-                else src = vnew + (long long)(vfog ? r - s_old : r) * a.nst;
+                if (stored) src[u] = vst + (a.lo + r) * rb;
+                else src[u] = vnew + (long long)(vfog ? r - s_old : r) * a.nst;
             } else {
-                src = knew + (long long)(r - vrows) * a.nst;
+                src[u] = knew + (long long)(r - vrows) * a.nst;
             }
-            raw[u] = ldg_stream(src + c * 16);
+            src[u] += c * 16;
+            if (stored || waited) raw[u] = ldg_stream(src[u]);
+        }
+        if (!waited) {
+            ptx::grid_dependency_wait();
+            ptx::launch_dependents();
+            waited = true;
+#pragma unroll
+            for (int u = 0; u < kItems; ++u) {
+                const int i = base + u * 256;
+                if (i >= items) break;
+                const int r = i / chunks;
+                if (!(vfog && r < vrows && r < s_old)) raw[u] = ldg_stream(src[u]);
+            }
         }
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
@@ -172,6 +200,30 @@ int grid_x(long long items, long long rows_y) {
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Byte ranges written by the last tiered update launched on each (device,
+// stream) of this process: K store, V store, fogged V.  An update may read its
+// V store early exactly when none of these ranges overlaps it.
+struct ByteRange { uintptr_t lo, hi; };
+struct UpdateWrites { ByteRange r[3]; };
+std::mutex g_last_mu;
+std::map<std::pair<int, uintptr_t>, UpdateWrites> g_last_update;
+
+bool overlaps(const ByteRange& a, const ByteRange& b) { return a.lo < b.hi && b.lo < a.hi; }
+
+// Decides the early flag of an update that reads `v_reads` and writes `w` on
+// (dev, stream), and records `w` as that stream's last update.
+bool claim_early_read(int dev, cudaStream_t stream, const ByteRange& v_reads, const UpdateWrites& w) {
+    std::lock_guard<std::mutex> lock(g_last_mu);
+    const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
+    bool early = true;
+    auto it = g_last_update.find(key);
+    if (it != g_last_update.end())
+        for (const ByteRange& r : it->second.r)
+            if (overlaps(r, v_reads)) early = false;
+    g_last_update[key] = w;
+    return early;
+}
+
 }  // namespace
 }  // namespace kessie
 
@@ -218,6 +270,18 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
     const long long rows = (v_fog ? S : T) + T;
     if (rows == 0) { clear_error(); return 0; }
     cudaStream_t st = as_stream(stream);
+    {
+        const uintptr_t store_bytes = (uintptr_t)((long long)B * H * cap * a.chunks * 16);
+        const uintptr_t kb = reinterpret_cast<uintptr_t>(k_store), vb = reinterpret_cast<uintptr_t>(v_store);
+        const uintptr_t fb = reinterpret_cast<uintptr_t>(v_fog);
+        UpdateWrites w;
+        w.r[0] = {kb, kb + store_bytes};
+        w.r[1] = {vb, vb + store_bytes};
+        w.r[2] = v_fog ? ByteRange{fb, fb + (uintptr_t)((long long)B * H * S * a.chunks * 16)} : ByteRange{0, 0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        a.early = claim_early_read(dev, st, w.r[1], w) && v_fog != nullptr ? 1 : 0;
+    }
     const dim3 grid(grid_x(rows * a.chunks, (long long)B * H), B * H);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

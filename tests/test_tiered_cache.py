@@ -284,3 +284,41 @@ def test_host_guards_without_gpu():
     if not torch.cuda.is_available():
         with pytest.raises(RuntimeError):
             vi.rebuild([np.ones(8, np.float32)], [1])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layers,pattern", [(1, "in_order"), (2, "in_order"), (5, "in_order"), (3, "repeat_first")])
+def test_gpu_back_to_back_updates(layers, pattern):
+    """Decode steps enqueued with no other kernel and no synchronisation in
+    between, as a model's update loop runs: each update may start reading its
+    V store while the previous update drains, which is allowed only when that
+    update wrote another store.  One layer (every update follows one of the
+    same layer), two layers (A B A B: the update before the previous one wrote
+    this store) and a repeated layer in the order all end bit-exact."""
+    from kessie_b200.kessie_cache import KeSSieCache
+    Bq, Hh, Dd, S0, steps = 1, 8, 128, 3000, 12
+    order = list(range(layers)) if pattern == "in_order" else [0, 0] + list(range(1, layers))
+    c = KeSSieCache(window_size=4096, fog_alpha=0.5, fog_start=0.5)
+    m = TieredCacheModel(4096, 0.5, 0.5, "bfloat16")
+    rng = np.random.default_rng(17)
+    rnd = lambda T: FO.round_bf16(rng.standard_normal((Bq, Hh, T, Dd), dtype=np.float32))
+    for l in range(layers):
+        k, v = rnd(S0), rnd(S0)
+        m.update(k, v, l)
+        c.update(_to_dev(k, "bfloat16"), _to_dev(v, "bfloat16"), l)
+    host = [[(rnd(1), rnd(1)) for _ in order] for _ in range(steps)]
+    dev = [[(_to_dev(k, "bfloat16"), _to_dev(v, "bfloat16")) for k, v in row] for row in host]
+    torch.cuda.synchronize()
+    last = {}
+    for row in dev:                                # no host sync and no other kernel in between
+        for l, (k, v) in zip(order, row):
+            last[l] = c.update(k, v, l)
+    want = {}
+    for row in host:
+        for l, (k, v) in zip(order, row):
+            want[l] = m.update(k, v, l)
+    torch.cuda.synchronize()
+    for l in range(layers):
+        np.testing.assert_array_equal(_np(last[l][0]), want[l][0])
+        np.testing.assert_array_equal(_np(last[l][1]), want[l][1])
+        np.testing.assert_array_equal(_np(c.value_cache[l]), m.value_cache[l])
