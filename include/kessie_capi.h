@@ -426,7 +426,13 @@ int kessie_index_query_v2(const float* query, const float* index, int num_rows, 
  *   w(s) = max((s / max(fc - 1, 1)) ^ fog_alpha, 0.01) for s < fc, else 1
  * into v_fog, contiguous [B, H, S, D]; with no mask v_fog is not touched.
  * Needs hi + T <= cap, D * element size a multiple of 16, 16-byte aligned
- * buffers.
+ * buffers.  The update is a programmatic dependent launch: it may start while
+ * the previous kernel on the stream drains.  When the last tiered update
+ * launched on the same (device, stream) by this process wrote none of this V
+ * store, the live-V loads start before that kernel completes; new tokens are
+ * read, and everything is written, only after it completes.  So the stores
+ * belong to this library: a kernel that writes them must not be launched with
+ * a programmatic dependency that triggers before its own writes.
  *
  * kessie_strided_pack_v2 replaces the per-layer slicing copies of
  * evict_if_needed / recall_from_cpu (:452-533): for every store m of
