@@ -53,7 +53,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["kessie", "reference"], default="kessie")
     ap.add_argument("--workload", default="cp_decode_1m",
-                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "decode_f32", "page_ops", "prefill",
+                    choices=["cp_decode_1m", "decode_cfg3", "decode_128k", "decode_small", "decode_f32", "decode_f32_small",
+                             "page_ops", "prefill",
                              "prefill_small", "vllm_fog_decode", "index_query", "tiered_cache"])
     ap.add_argument("--seed", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -615,25 +616,31 @@ def measure_aux(workload, steps, warmup=3):
         torch.cuda.synchronize()
         return a.elapsed_time(b) / K
 
-    if args.workload == "decode_f32":
+    if args.workload in ("decode_f32", "decode_f32_small"):
         # fp32 paged decode (the reference's own precision): config 1 (B1,
         # Hq8/Hkv2, D128, 4096 keys, W512 -> clear_start 3584; 8 MiB of KV,
         # timed cold after the L2 flush), and the config-3 attention shape
         # at a fixed 131,072 keys in fp32 (34.4 GB of KV) for the roofline.
-        flush = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
-        B, Hq, Hkv, D, ps, N = 1, 8, 2, 128, 16, 4096
-        kv = torch.randn(N // ps, ps, 2, Hkv, D, device=dev)
-        bt = torch.randperm(N // ps, device=dev).to(torch.int32)[None]
-        q = torch.randn(B, Hq, D, device=dev)
-        sl = torch.tensor([N], dtype=torch.int32, device=dev)
-        cs = sl - 512
-        out = torch.empty(B, Hq, D, device=dev)
-        ms1 = timeit(lambda: ops.paged_fog_decode(q, kv[:, :, 0], kv[:, :, 1], bt, sl, clear_start=cs, out=out),
-                     args.steps)
-        flush = None
-        del kv
+        # decode_f32_small: the config-3 shape at 2 sequences (2.1 GB, the
+        # profiling size), no config-1 leg.
+        ms1 = None
+        if args.workload == "decode_f32":
+            flush = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
+            B, Hq, Hkv, D, ps, N = 1, 8, 2, 128, 16, 4096
+            kv = torch.randn(N // ps, ps, 2, Hkv, D, device=dev)
+            bt = torch.randperm(N // ps, device=dev).to(torch.int32)[None]
+            q = torch.randn(B, Hq, D, device=dev)
+            sl = torch.tensor([N], dtype=torch.int32, device=dev)
+            cs = sl - 512
+            out = torch.empty(B, Hq, D, device=dev)
+            ms1 = timeit(lambda: ops.paged_fog_decode(q, kv[:, :, 0], kv[:, :, 1], bt, sl, clear_start=cs, out=out),
+                         args.steps)
+            flush = None
+            del kv
         c = CFG3
         B, Hq, Hkv, D, ps, N = c["batch"], c["q_heads"], c["kv_heads"], c["head_dim"], c["page"], 131072
+        if args.workload == "decode_f32_small":
+            B = 2
         P = B * N // ps
         kv = torch.empty(P, ps, 2, Hkv, D, device=dev)
         kv.normal_().mul_(1 / math.sqrt(128))
@@ -646,8 +653,8 @@ def measure_aux(workload, steps, warmup=3):
                     args.steps)
         byts = B * N * Hkv * D * 8
         res.update(ms_per_step=ms, us_per_step=ms * 1e3, kv_bytes=byts, GBs=byts / ms / 1e6,
-                   frac_of_hbm=byts / ms / 1e6 / hbm, cfg1_us=ms1 * 1e3,
-                   note="fp32 K/V/q/out; us/GBs/frac: batch 32 x 131,072 keys, Hq 32 / Hkv 8; cfg1_us: config 1 "
+                   frac_of_hbm=byts / ms / 1e6 / hbm, cfg1_us=ms1 * 1e3 if ms1 is not None else None,
+                   note=f"fp32 K/V/q/out; us/GBs/frac: batch {B} x 131,072 keys, Hq 32 / Hkv 8; cfg1_us: config 1 "
                         "(4096 keys) after a 256 MB L2 flush")
         del kv
     elif args.workload in ("decode_cfg3", "decode_128k", "decode_small"):

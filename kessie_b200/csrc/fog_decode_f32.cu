@@ -18,27 +18,34 @@
 //           and split S ways; S is chosen from the SM count so the grid's
 //           last wave is nearly full, with at least two chunks per warp.
 //   CTA   = 8 warps.  Each warp streams every 8th chunk of the CTA's range
-//           through its own 3-stage ring of 16-byte cp.async copies (8 KB of
-//           K+V per stage at D 128), so two chunks per warp are in flight
-//           while it computes the third.  K lands 16-byte swizzled
-//           (chunk x of row r at x ^ (r & 7)) so the score loop reads it
-//           without bank conflicts; V lands row-major.
+//           through its own 3-stage ring: per chunk two TMA box loads (K, V;
+//           8 keys x D of one head, 4 KB each at D 128) on the stage's
+//           mbarrier, so two chunks per warp are in flight while it computes
+//           the third.  Page ids come from the block table 32 chunks at a
+//           time, a batch ahead, one per lane.  The boxes land 128-byte
+//           swizzled (16-byte chunk c of key t at row (c/8)*8 + t, position
+//           (c%8) ^ t), which both the score and the PV reads take without
+//           bank conflicts.
 //   QK    = lane (key kk = lane/4, quarter dq = lane%4) dots its quarter row of
-//           K with every query head of the group (q staged once per CTA in
-//           shared memory, pre-scaled by sm_scale*log2e, swizzled so the four
-//           quarters read distinct banks); a two-step transposing shuffle
-//           reduction over the quarters leaves each lane the full scores of
-//           GP/4 heads of its key.
+//           K with every query head of the group, two heads per packed fp32
+//           FMA (fma.rn.f32x2; q staged once per CTA by head pairs, pre-scaled
+//           by sm_scale*log2e, swizzled so the four quarters read distinct
+//           banks); a two-step transposing shuffle reduction over the
+//           quarters leaves each lane the full scores of GP/4 heads of its key.
 //   soft  = online softmax per head across the chunk's 8 keys (xor shuffles
 //           over the key lanes), running (m, l) per lane; p*w and the rescale
 //           factors go to a per-warp shared tile.
 //   PV    = lane owns D/32 consecutive dims of O for every head; per visible
-//           key: one V load and GP*D/32 FMAs.
+//           key: one V load and GP*D/64 packed FMAs (two heads each).
+//   The pipeline is bound by bytes in flight: 128 KB of K+V per SM (two of a
+//   warp's three 8 KB stages) against a loaded DRAM latency of a few us.
 //   merge = the 8 warps merge through shared memory; with S > 1 each CTA
 //           writes (O/l, m, l) per head into its workspace slot and bumps the
 //           group's tagged arrival counter; the last CTA merges the S slots
 //           and writes out / out_partial (and zeroes the counter).
 #include "decode_f32.cuh"
+#include "ptx.cuh"
+#include "tma_host.cuh"
 
 #include <math.h>
 
@@ -47,23 +54,36 @@ namespace {
 
 constexpr int kW = 8;            // warps per CTA
 constexpr int kT = kW * 32;
-constexpr int kNS = 3;           // cp.async stages per warp
+constexpr int kNS = 3;           // shared-memory stages per warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr unsigned kFull = 0xffffffffu;
 
+// Shared memory (floats, from a 1024-byte aligned base): the warps' stage
+// rings first (every stage and tile 1024-byte aligned, as the 128-byte
+// swizzle needs), then q, the per-warp P / alpha tiles, the merge tail and the
+// per-warp mbarriers.
 template <int D, int GP>
 struct F32Layout {
-    static constexpr int kChunk = 8 * D;                     // floats of one 8-key K (or V) slice
+    static constexpr int kChunk = 8 * D;                     // floats of one 8-key K (or V) tile
     static constexpr int kStage = 2 * kChunk;
-    static constexpr int kWarpF = kNS * kStage + 8 * GP + GP;   // stages, P tile [8][GP], alpha [GP]
-    static constexpr int kWarpOff = GP * D;                  // after the staged q [GP][D]
+    static constexpr int kRing = kNS * kStage;               // one warp's stages
+    static constexpr int kQOff = kW * kRing;                 // staged q [GP][D]
+    static constexpr int kWarpOff = kQOff + GP * D;          // per warp: P tile [8][GP], alpha [GP]
+    static constexpr int kWarpF = 8 * GP + GP;
     static constexpr int kTailOff = kWarpOff + kW * kWarpF;  // merged (M, L) [GP][2], warp scales [kW][GP]
-    static constexpr int kFloats = kTailOff + 2 * GP + kW * GP;
-    static constexpr int kBytes = kFloats * 4;
-    static_assert(kNS * kStage >= 2 * GP + GP * D, "a warp's merge data must fit in its stages");
+    static constexpr int kBarOff = (kTailOff + 2 * GP + kW * GP + 1) & ~1;   // kW x kNS mbarriers
+    static constexpr int kFloats = kBarOff + 2 * kW * kNS;
+    static constexpr int kBytes = kFloats * 4 + 1024;        // + slack to align the dynamic base
+    static_assert(kRing >= 2 * GP + GP * D, "a warp's merge data must fit in its stages");
+    static_assert((kChunk * 4) % 1024 == 0, "tiles must stay 1024-byte aligned");
     static_assert(kWarpF % 4 == 0 && kWarpOff % 4 == 0, "float4 alignment");
 };
+
+// Offset (floats) of dims [4c, 4c + 4) of key t (0..7) in an 8-key tile: row
+// (c / 8) * 8 + t of 32 floats, 16-byte chunk c % 8 XOR t -- the layout a
+// 128-byte swizzled TMA box {32, 8 tokens, D/32} lands in.
+__device__ __forceinline__ int tile_off(int t, int c) { return ((c >> 3) * 8 + t) * 32 + (((c & 7) ^ t) << 2); }
 
 struct SeqF32 {
     int k_lo, k_hi;   // visible local keys [k_lo, k_hi)
@@ -134,18 +154,20 @@ __device__ __forceinline__ void emit_f32(const DecodeF32Args& p, int b, int h, i
 }
 
 template <int D, int GP>
-__global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Args p, const int S) {
+__global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Args p, const int S,
+                                                               const __grid_constant__ CUtensorMap tmK,
+                                                               const __grid_constant__ CUtensorMap tmV,
+                                                               const int dense) {
     using Lay = F32Layout<D, GP>;
     constexpr int E = D / 32;      // PV: consecutive dims of O per lane
     constexpr int CPL = D / 16;    // QK: 16-byte chunks per lane (a quarter row)
     constexpr int H4 = GP / 4;     // QK: heads per lane after the reduction
-    constexpr int RC = D / 4;      // 16-byte chunks per row
     extern __shared__ float4 smem_f4[];
-    float* sm = reinterpret_cast<float*>(smem_f4);
-    float* sq = sm;
+    float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_f4) + 1023) & ~uintptr_t(1023));
+    float* sq = sm + Lay::kQOff;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* sw = sm + Lay::kWarpOff + warp * Lay::kWarpF;
-    float* sP = sw + kNS * Lay::kStage;
+    float* sw = sm + warp * Lay::kRing;
+    float* sP = sm + Lay::kWarpOff + warp * Lay::kWarpF;
     float* sA = sP + 8 * GP;
     float* sML = sm + Lay::kTailOff;       // [GP][2]
     float* sSC = sML + 2 * GP;             // [kW][GP]
@@ -156,17 +178,18 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
     const int G = p.Hq / p.Hkv;
     const SeqF32 si = seq_f32(p, b);
 
-    // query rows of the group, scaled into log2 units, swizzled by quarter
+    // query rows of the group, scaled into log2 units, stored by head pairs:
+    // 16-byte chunk c of pair gp holds dims 2c, 2c+1 of heads 2gp, 2gp+1
+    // ([q(2gp,2c), q(2gp+1,2c), q(2gp,2c+1), q(2gp+1,2c+1)]), the chunk index
+    // XORed with its quarter so the four quarters read distinct banks
     const float qscale = p.sm_scale * kLog2e;
-    for (int i = threadIdx.x; i < GP * RC; i += kT) {
-        const int g = i / RC, x = i - g * RC;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (g < G) {
-            const float* src = p.q + (int64_t)b * p.q_sb + (int64_t)(hk * G + g) * p.q_sh + x * 4;
-            v = make_float4(src[0] * qscale, src[1] * qscale, src[2] * qscale, src[3] * qscale);
-        }
-        const int dq = x / CPL, c = x - dq * CPL;
-        *reinterpret_cast<float4*>(sq + g * D + ((dq * CPL + (c ^ dq)) << 2)) = v;
+    constexpr int QC = D / 8;                  // chunks per quarter of a head pair's row
+    for (int i = threadIdx.x; i < GP * D; i += kT) {
+        const int g = i / D, d = i - g * D;
+        float v = 0.f;
+        if (g < G) v = p.q[(int64_t)b * p.q_sb + (int64_t)(hk * G + g) * p.q_sh + d] * qscale;
+        const int c = d >> 1, dq = c / QC;
+        sq[((g >> 1) * (D / 2) + (c ^ dq)) * 4 + (d & 1) * 2 + (g & 1)] = v;
     }
     __syncthreads();
 
@@ -179,32 +202,60 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
     const int nw = ce > cb + warp ? (ce - cb - warp + kW - 1) / kW : 0;
     const int32_t* bt = p.block_table ? p.block_table + (int64_t)b * p.bt_stride : nullptr;
 
-    // Starts the copies of this warp's chunk i into stage i % kNS; returns
-    // true (and copies nothing) when the chunk's page id is out of range.
+    // Page ids come from the block table 32 chunks at a time, a batch ahead:
+    // lane j holds the page of this warp's chunk 32 * batch + j, so a copy
+    // never waits on a block-table load.
+    auto page_of = [&](int i) -> int {
+        if (i >= nw) return 0;
+        const int pi = (cb + warp + i * kW) * 8 / p.page_size;
+        return bt ? __ldg(bt + pi) : pi;
+    };
+    int pg_cur = page_of(lane), pg_next = page_of(32 + lane);
+
+    // Per warp one mbarrier per stage.
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lay::kBarOff) + warp * kNS;
+    if (lane == 0) {
+#pragma unroll
+        for (int s2 = 0; s2 < kNS; ++s2) ptx::mbar_init(&bars[s2], 1);
+        ptx::fence_mbar_init();
+        ptx::prefetch_tensormap(&tmK);
+        ptx::prefetch_tensormap(&tmV);
+    }
+    __syncwarp();
+
+    // Starts the two box loads (K, V; 8 keys x D each) of this warp's chunk i
+    // into stage i % kNS on the stage's mbarrier (chunks are issued in
+    // increasing order); returns true (and copies nothing, the barrier
+    // completing at once) when the chunk's page id is out of range.  Rows past
+    // the visible end are in-page (zero-filled past a dense cache's end) and
+    // masked.
     auto issue = [&](int i) -> bool {
+        if ((i & 31) == 0 && i > 0) {
+            pg_cur = pg_next;
+            pg_next = page_of(i + 32 + lane);
+        }
         const int key0 = (cb + warp + i * kW) * 8;
         const int pi = key0 / p.page_size, tok = key0 - pi * p.page_size;
-        const int page = p.block_table ? __ldg(bt + pi) : pi;
+        const int page = __shfl_sync(kFull, pg_cur, i & 31);
+        uint64_t* bar = &bars[i % kNS];
         if (page < 0 || page >= p.num_pages) {
-            if (lane == 0) record_status(p.status, KESSIE_DEV_BAD_PAGE_ID);
+            if (lane == 0) {
+                record_status(p.status, KESSIE_DEV_BAD_PAGE_ID);
+                ptx::mbar_arrive(bar);
+            }
             return true;
         }
-        float* dK = sw + (i % kNS) * Lay::kStage;
-        float* dV = dK + Lay::kChunk;
-        const int64_t base = (int64_t)page * p.page_stride + (int64_t)tok * p.token_stride + (int64_t)hk * p.head_stride;
-        const float* gK = p.k_cache + base;
-        const float* gV = p.v_cache + base;
-        // rows at or past the visible end are never read (they are masked
-        // anyway): a dense cache may end inside the chunk
-        const int rows = min(8, si.k_hi - key0);
-#pragma unroll
-        for (int t = 0; t < 8 * RC / 32; ++t) {
-            const int idx = t * 32 + lane;
-            const int r = idx / RC, x = idx - r * RC;
-            if (r >= rows) continue;
-            const int64_t src = (int64_t)r * p.token_stride + x * 4;
-            cp_async16(dK + r * D + ((x ^ (r & 7)) << 2), gK + src);
-            cp_async16(dV + r * D + (x << 2), gV + src);
+        if (lane == 0) {
+            float* dK = sw + (i % kNS) * Lay::kStage;
+            float* dV = dK + Lay::kChunk;
+            ptx::mbar_arrive_expect_tx(bar, (uint32_t)(2 * Lay::kChunk * 4));
+            if (dense) {
+                ptx::tma_load_4d(dK, &tmK, bar, 0, key0, 0, hk);
+                ptx::tma_load_4d(dV, &tmV, bar, 0, key0, 0, hk);
+            } else {
+                ptx::tma_load_5d(dK, &tmK, bar, 0, tok, 0, hk, page);
+                ptx::tma_load_5d(dV, &tmV, bar, 0, tok, 0, hk, page);
+            }
         }
         return false;
     };
@@ -212,11 +263,11 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
     float m[H4], l[H4];
 #pragma unroll
     for (int h = 0; h < H4; ++h) { m[h] = -INFINITY; l[h] = 0.f; }
-    float acc[GP][E];
+    uint64_t acc2[GP / 2][E];       // (acc[2gp][e], acc[2gp+1][e]) as packed fp32 pairs
 #pragma unroll
-    for (int g = 0; g < GP; ++g)
+    for (int gp = 0; gp < GP / 2; ++gp)
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[g][e] = 0.f;
+        for (int e = 0; e < E; ++e) acc2[gp][e] = 0ull;
 
     uint32_t badm = 0;   // bit s: the chunk in stage s had a bad page id (warp-uniform)
 #pragma unroll
@@ -227,9 +278,15 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
         cp_async_commit();
     }
     const int kk = lane >> 2, dq = lane & 3;
+    int stuck = -1;      // chunk whose wait gave up (warp-uniform); the rest is not read
     for (int i = 0; i < nw; ++i) {
-        cp_async_wait_group<kNS - 2>();
-        __syncwarp();
+        const bool ok = __all_sync(kFull, ptx::mbar_wait(&bars[i % kNS], (uint32_t)(i / kNS) & 1u));
+        __syncwarp();                      // every lane is done with the stage refilled next
+        if (!ok) {
+            if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+            stuck = i;
+            break;
+        }
         {
             const int nx = i + kNS - 1;
             if (nx < nw) {
@@ -244,24 +301,31 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
         const bool bad = (badm >> sl) & 1u;
         const int key0 = (cb + warp + i * kW) * 8;
 
-        // ---- scores: lane (kk, dq) dots its quarter of key kk with every head
-        float s[GP];
+        // ---- scores: lane (kk, dq) dots its quarter of key kk with every head,
+        // two heads per packed fma (fma.rn.f32x2)
+        uint64_t s2[GP / 2];
 #pragma unroll
-        for (int g = 0; g < GP; ++g) s[g] = 0.f;
+        for (int gp = 0; gp < GP / 2; ++gp) s2[gp] = 0ull;
 #pragma unroll
         for (int cc = 0; cc < CPL; ++cc) {
             const int x = dq * CPL + cc;
-            const float4 kf = *reinterpret_cast<const float4*>(sK + kk * D + ((x ^ (kk & 7)) << 2));
-            const int qx = (dq * CPL + (cc ^ dq)) << 2;
+            const float4 kf = *reinterpret_cast<const float4*>(sK + tile_off(kk, x));
+            const uint64_t kx = ptx::f2_pack(kf.x, kf.x), ky = ptx::f2_pack(kf.y, kf.y);
+            const uint64_t kz = ptx::f2_pack(kf.z, kf.z), kw = ptx::f2_pack(kf.w, kf.w);
+            const int c0 = dq * QC + 2 * cc;           // chunks of dims 4cc.. 4cc+3 of the quarter
 #pragma unroll
-            for (int g = 0; g < GP; ++g) {
-                const float4 qf = *reinterpret_cast<const float4*>(sq + g * D + qx);
-                s[g] = fmaf(qf.x, kf.x, s[g]);
-                s[g] = fmaf(qf.y, kf.y, s[g]);
-                s[g] = fmaf(qf.z, kf.z, s[g]);
-                s[g] = fmaf(qf.w, kf.w, s[g]);
+            for (int gp = 0; gp < GP / 2; ++gp) {
+                const float4 qa = *reinterpret_cast<const float4*>(sq + (gp * (D / 2) + (c0 ^ dq)) * 4);
+                const float4 qb = *reinterpret_cast<const float4*>(sq + (gp * (D / 2) + ((c0 + 1) ^ dq)) * 4);
+                s2[gp] = ptx::ffma2(ptx::f2_pack(qa.x, qa.y), kx, s2[gp]);
+                s2[gp] = ptx::ffma2(ptx::f2_pack(qa.z, qa.w), ky, s2[gp]);
+                s2[gp] = ptx::ffma2(ptx::f2_pack(qb.x, qb.y), kz, s2[gp]);
+                s2[gp] = ptx::ffma2(ptx::f2_pack(qb.z, qb.w), kw, s2[gp]);
             }
         }
+        float s[GP];
+#pragma unroll
+        for (int gp = 0; gp < GP / 2; ++gp) ptx::f2_unpack(s2[gp], s[2 * gp], s[2 * gp + 1]);
         // transposing reduction over the quarters: lane keeps heads dq*H4 .. dq*H4+H4-1
         float t[GP / 2];
         {
@@ -317,12 +381,11 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
 #pragma unroll
             for (int g4 = 0; g4 < GP / 4; ++g4) {
                 const float4 a = *reinterpret_cast<const float4*>(sA + g4 * 4);
+                const uint64_t a01 = ptx::f2_pack(a.x, a.y), a23 = ptx::f2_pack(a.z, a.w);
 #pragma unroll
                 for (int e = 0; e < E; ++e) {
-                    acc[g4 * 4 + 0][e] *= a.x;
-                    acc[g4 * 4 + 1][e] *= a.y;
-                    acc[g4 * 4 + 2][e] *= a.z;
-                    acc[g4 * 4 + 3][e] *= a.w;
+                    acc2[g4 * 2][e] = ptx::fmul2(acc2[g4 * 2][e], a01);
+                    acc2[g4 * 2 + 1][e] = ptx::fmul2(acc2[g4 * 2 + 1][e], a23);
                 }
             }
         }
@@ -330,28 +393,32 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
         for (int r = 0; r < 8; ++r) {
             const int j = key0 + r;
             if (bad || j < si.k_lo || j >= si.k_hi) continue;     // warp-uniform
-            float v[E];
+            uint64_t v2[E];                                        // (v[e], v[e]): one V value for a head pair
             if (E == 4) {
-                const float4 vf = *reinterpret_cast<const float4*>(sV + r * D + lane * 4);
-                v[0] = vf.x; v[1] = vf.y; v[2] = vf.z; v[3] = vf.w;
+                const float4 vf = *reinterpret_cast<const float4*>(sV + tile_off(r, lane));
+                v2[0] = ptx::f2_pack(vf.x, vf.x); v2[1] = ptx::f2_pack(vf.y, vf.y);
+                v2[2] = ptx::f2_pack(vf.z, vf.z); v2[3] = ptx::f2_pack(vf.w, vf.w);
             } else {
-                const float2 vf = *reinterpret_cast<const float2*>(sV + r * D + lane * 2);
-                v[0] = vf.x; v[1] = vf.y;
+                const float2 vf = *reinterpret_cast<const float2*>(sV + tile_off(r, lane >> 1) + (lane & 1) * 2);
+                v2[0] = ptx::f2_pack(vf.x, vf.x); v2[1] = ptx::f2_pack(vf.y, vf.y);
             }
 #pragma unroll
             for (int g4 = 0; g4 < GP / 4; ++g4) {
                 const float4 pq = *reinterpret_cast<const float4*>(sP + r * GP + g4 * 4);
+                const uint64_t p01 = ptx::f2_pack(pq.x, pq.y), p23 = ptx::f2_pack(pq.z, pq.w);
 #pragma unroll
                 for (int e = 0; e < E; ++e) {
-                    acc[g4 * 4 + 0][e] = fmaf(pq.x, v[e], acc[g4 * 4 + 0][e]);
-                    acc[g4 * 4 + 1][e] = fmaf(pq.y, v[e], acc[g4 * 4 + 1][e]);
-                    acc[g4 * 4 + 2][e] = fmaf(pq.z, v[e], acc[g4 * 4 + 2][e]);
-                    acc[g4 * 4 + 3][e] = fmaf(pq.w, v[e], acc[g4 * 4 + 3][e]);
+                    acc2[g4 * 2][e] = ptx::ffma2(p01, v2[e], acc2[g4 * 2][e]);
+                    acc2[g4 * 2 + 1][e] = ptx::ffma2(p23, v2[e], acc2[g4 * 2 + 1][e]);
                 }
             }
         }
     }
-    cp_async_wait_group<0>();
+    if (stuck >= 0) {
+        // box loads still in flight land before the stages are reused
+        for (int j = stuck; j < min(nw, stuck + kNS - 1); ++j)
+            (void)__all_sync(kFull, ptx::mbar_wait(&bars[j % kNS], (uint32_t)(j / kNS) & 1u));
+    }
     __syncthreads();
 
     // ---- merge the 8 warps (each writes into its own stage area)
@@ -365,14 +432,20 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
         }
     }
 #pragma unroll
-    for (int g = 0; g < GP; ++g) {
-        if (E == 4)
-            *reinterpret_cast<float4*>(ow + g * D + lane * 4) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-        else
-            *reinterpret_cast<float2*>(ow + g * D + lane * 2) = make_float2(acc[g][0], acc[g][1]);
+    for (int gp = 0; gp < GP / 2; ++gp) {
+        float lo[E], hi[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) ptx::f2_unpack(acc2[gp][e], lo[e], hi[e]);
+        if (E == 4) {
+            *reinterpret_cast<float4*>(ow + (2 * gp) * D + lane * 4) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<float4*>(ow + (2 * gp + 1) * D + lane * 4) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        } else {
+            *reinterpret_cast<float2*>(ow + (2 * gp) * D + lane * 2) = make_float2(lo[0], lo[1]);
+            *reinterpret_cast<float2*>(ow + (2 * gp + 1) * D + lane * 2) = make_float2(hi[0], hi[1]);
+        }
     }
     __syncthreads();
-    auto warp_area = [&](int w) { return sm + Lay::kWarpOff + w * Lay::kWarpF; };
+    auto warp_area = [&](int w) { return sm + w * Lay::kRing; };
     if (threadIdx.x < G) {
         const int g = threadIdx.x;
         float M = -INFINITY;
@@ -427,7 +500,7 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
 
     // ---- last CTA of the group: merge the S slots.  Per (slot, head) scale
     // L_s * 2^(m_s - M) / L into the (now idle) stage area.
-    float* ssc = sm + Lay::kWarpOff;      // [S][GP]
+    float* ssc = sm;                      // [S][GP]
     for (int g = warp; g < G; g += kW) {
         float M = -INFINITY;
         for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(p.part_ml + ((size_t)(grp * S + s2) * G + g) * 2));
@@ -465,15 +538,16 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
 }
 
 template <int D, int GP>
-int launch_f32_t(const DecodeF32Args& a, int S, cudaStream_t st) {
+int launch_f32_t(const DecodeF32Args& a, int S, const CUtensorMap& mk, const CUtensorMap& mv, int dense,
+                 cudaStream_t st) {
     using Lay = F32Layout<D, GP>;
     auto kern = fog_decode_f32_kernel<D, GP>;
     // the last CTA's per-slot scales [S][GP] live in the warps' stage areas
-    if (S * GP > kW * Lay::kWarpF) S = kW * Lay::kWarpF / GP;
+    if (S * GP > kW * Lay::kRing) S = kW * Lay::kRing / GP;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kBytes) != cudaSuccess)
         return check_launch("paged_fog_decode (fp32): set smem attribute");
     dim3 grid(S, a.B * a.Hkv);
-    kern<<<grid, kT, Lay::kBytes, st>>>(a, S);
+    kern<<<grid, kT, Lay::kBytes, st>>>(a, S, mk, mv, dense);
     return check_launch("paged_fog_decode (fp32)");
 }
 
@@ -499,14 +573,28 @@ int launch_decode_f32(const DecodeF32Args& a, cudaStream_t st) {
     double best = fill(S);
     for (int s = S + 1; s <= min(s_max, 8 * S) && best < 0.97; ++s)
         if (fill(s) > best + 1e-9) { best = fill(s); S = s; }
+    // K/V tiles by TMA boxes: pages (a multiple of 8 tokens) through a 5-D
+    // map, a dense cache through a 4-D map that zero-fills past its end
+    if (a.square_n <= 0 && a.page_size % 8)
+        return set_error(KESSIE_ERR_UNSUPPORTED, "paged_fog_decode (fp32): page_size %d not a multiple of 8",
+                         a.page_size);
+    const int dense = a.square_n > 0 ? 1 : 0;
+    const int tokens = dense ? a.square_n : a.page_size, pages = dense ? 0 : a.num_pages;
+    CUtensorMap mk, mv;
+    const CUresult r1 = encode_f32_kv_map(&mk, a.k_cache, a.D, tokens, a.Hkv, pages, a.token_stride, a.head_stride,
+                                          a.page_stride);
+    const CUresult r2 = encode_f32_kv_map(&mv, a.v_cache, a.D, tokens, a.Hkv, pages, a.token_stride, a.head_stride,
+                                          a.page_stride);
+    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
+        return set_error(KESSIE_ERR_ARG, "paged_fog_decode (fp32): TMA descriptor rejected (%d/%d)", (int)r1, (int)r2);
     if (a.D == 128) {
-        if (G <= 4) return launch_f32_t<128, 4>(a, S, st);
-        if (G <= 8) return launch_f32_t<128, 8>(a, S, st);
-        return launch_f32_t<128, 16>(a, S, st);
+        if (G <= 4) return launch_f32_t<128, 4>(a, S, mk, mv, dense, st);
+        if (G <= 8) return launch_f32_t<128, 8>(a, S, mk, mv, dense, st);
+        return launch_f32_t<128, 16>(a, S, mk, mv, dense, st);
     }
-    if (G <= 4) return launch_f32_t<64, 4>(a, S, st);
-    if (G <= 8) return launch_f32_t<64, 8>(a, S, st);
-    return launch_f32_t<64, 16>(a, S, st);
+    if (G <= 4) return launch_f32_t<64, 4>(a, S, mk, mv, dense, st);
+    if (G <= 8) return launch_f32_t<64, 8>(a, S, mk, mv, dense, st);
+    return launch_f32_t<64, 16>(a, S, mk, mv, dense, st);
 }
 
 }  // namespace kessie

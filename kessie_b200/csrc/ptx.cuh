@@ -66,6 +66,15 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
            "r"(c4), "r"(smem_u32(bar))
         : "memory");
 }
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+           "r"(smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ void tma_load_5d_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
                                                  int c0, int c1, int c2, int c3, int c4, uint64_t policy) {
     asm volatile(

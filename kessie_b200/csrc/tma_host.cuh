@@ -58,4 +58,27 @@ inline CUresult encode_tiled_5d_sw128(CUtensorMap* map, const void* base, bool b
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+// Tensor map over an fp32 K (or V) cache for the fp32 decode: one box = 8
+// tokens of one head, all of head_dim, as rows of 32 floats (128 bytes,
+// 128-byte swizzled); row d_hi * 8 + token holds dims [32 d_hi, 32 d_hi + 32).
+// Paged (num_pages > 0): the 5-D tensor [32][page_size][D/32][heads][pages],
+// coordinates (0, token in page, 0, head, page).  Dense (num_pages == 0): the
+// 4-D tensor [32][tokens][D/32][heads], coordinates (0, token, 0, head); rows
+// past `tokens` read as zeros.  Strides in elements.
+inline CUresult encode_f32_kv_map(CUtensorMap* map, const void* base, int head_dim, int tokens, int num_heads,
+                                  int num_pages, int64_t token_stride, int64_t head_stride, int64_t page_stride) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return CUDA_ERROR_NOT_SUPPORTED;
+    const int rank = num_pages > 0 ? 5 : 4;
+    cuuint64_t dims[5] = {32, (cuuint64_t)tokens, (cuuint64_t)(head_dim / 32), (cuuint64_t)num_heads,
+                          (cuuint64_t)(num_pages > 0 ? num_pages : 1)};
+    cuuint64_t strides[4] = {(cuuint64_t)token_stride * 4, 128, (cuuint64_t)head_stride * 4,
+                             (cuuint64_t)page_stride * 4};
+    cuuint32_t box[5] = {32, 8, (cuuint32_t)(head_dim / 32), 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
 }  // namespace kessie
