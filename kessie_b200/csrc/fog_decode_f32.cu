@@ -32,13 +32,20 @@
 //           by sm_scale*log2e, swizzled so the four quarters read distinct
 //           banks); a two-step transposing shuffle reduction over the
 //           quarters leaves each lane the full scores of GP/4 heads of its key.
-//   soft  = online softmax per head across the chunk's 8 keys (xor shuffles
-//           over the key lanes), running (m, l) per lane; p*w and the rescale
-//           factors go to a per-warp shared tile.
-//   PV    = lane owns D/32 consecutive dims of O for every head; per visible
-//           key: one V load and GP*D/64 packed FMAs (two heads each).
-//   The pipeline is bound by bytes in flight: 128 KB of K+V per SM (two of a
-//   warp's three 8 KB stages) against a loaded DRAM latency of a few us.
+//   soft  = online softmax per head across the chunk's 8 keys with a lazy
+//           max: the running max m moves (xor-shuffle max over the key lanes,
+//           rescale of l and O) only when a score passes it by more than
+//           kSlack = 8 (log2 units), so p <= 2^8 and most chunks need no
+//           reduction; each key lane keeps its share of l and its true max,
+//           summed / reduced once at the end, where (m, l, O) move to the
+//           true max so the merges and the partials carry it.  p*w and the
+//           rescale factors go to a per-warp shared tile.
+//   PV    = lane owns D/32 consecutive dims of O for every head; per key one
+//           V load and GP*D/64 packed FMAs (two heads each), with no per-key
+//           branch: masked keys of a partial chunk have their V rows zeroed.
+//   What bounds it is the per-warp dependency chain per chunk (8 warps per
+//   SM; fewer warps with deeper rings measured slower), so the loop keeps
+//   shuffles, votes and branches off the common path.
 //   merge = the 8 warps merge through shared memory; with S > 1 each CTA
 //           writes (O/l, m, l) per head into its workspace slot and bumps the
 //           group's tagged arrival counter; the last CTA merges the S slots
@@ -55,6 +62,7 @@ namespace {
 constexpr int kW = 8;            // warps per CTA
 constexpr int kT = kW * 32;
 constexpr int kNS = 3;           // shared-memory stages per warp
+constexpr float kSlack = 8.f;    // log2 units a score may pass the running max by before it moves
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr unsigned kFull = 0xffffffffu;
@@ -260,9 +268,9 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
         return false;
     };
 
-    float m[H4], l[H4];
+    float m[H4], l[H4], mx[H4];     // running (m, l) of the heads; mx: this key lane's true max
 #pragma unroll
-    for (int h = 0; h < H4; ++h) { m[h] = -INFINITY; l[h] = 0.f; }
+    for (int h = 0; h < H4; ++h) { m[h] = -INFINITY; l[h] = 0.f; mx[h] = -INFINITY; }
     uint64_t acc2[GP / 2][E];       // (acc[2gp][e], acc[2gp+1][e]) as packed fp32 pairs
 #pragma unroll
     for (int gp = 0; gp < GP / 2; ++gp)
@@ -352,28 +360,38 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
         const int jl = key0 + kk;
         const bool valid = !bad && jl >= si.k_lo && jl < si.k_hi;
         const float w = valid ? fog_weight_f32(p, si.cs, si.off + jl) : 0.f;
-        bool moved = false;
+        // The running max m moves only when a score passes it by more than
+        // kSlack (log2 units): p = 2^(x - m) stays <= 2^kSlack, and a chunk
+        // that passes no lane's bound needs no max reduction and no rescale.
+        float x[H4];
+        bool over = false;
 #pragma unroll
         for (int h = 0; h < H4; ++h) {
-            const float x = valid ? u[h] : -INFINITY;
-            float cm = x;
-            cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 4));
-            cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 8));
-            cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 16));
-            const float mn = fmaxf(m[h], cm);
-            const float al = mn == -INFINITY ? 1.f : exp2f(m[h] - mn);
-            const float pr = valid ? exp2f(x - mn) : 0.f;
-            float ps = pr;
-            ps += __shfl_xor_sync(kFull, ps, 4);
-            ps += __shfl_xor_sync(kFull, ps, 8);
-            ps += __shfl_xor_sync(kFull, ps, 16);
-            l[h] = l[h] * al + ps;
-            m[h] = mn;
-            moved |= al != 1.f;
-            sP[kk * GP + dq * H4 + h] = pr * w;
-            if (kk == 0) sA[dq * H4 + h] = al;
+            x[h] = valid ? u[h] : -INFINITY;
+            over |= x[h] > m[h] + kSlack;
+            mx[h] = fmaxf(mx[h], x[h]);
         }
-        const bool rescale = __any_sync(kFull, moved);
+        const bool rescale = __any_sync(kFull, over);          // warp-uniform
+        if (rescale) {
+#pragma unroll
+            for (int h = 0; h < H4; ++h) {
+                float cm = x[h];
+                cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 4));
+                cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 8));
+                cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, 16));
+                const float mn = fmaxf(m[h], cm);
+                const float al = mn == -INFINITY ? 1.f : exp2f(m[h] - mn);
+                l[h] *= al;
+                m[h] = mn;
+                if (kk == 0) sA[dq * H4 + h] = al;
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < H4; ++h) {
+            const float pr = valid ? exp2f(x[h] - m[h]) : 0.f;
+            l[h] += pr;                        // this key lane's share; summed over the key lanes at the end
+            sP[kk * GP + dq * H4 + h] = pr * w;
+        }
         __syncwarp();
 
         // ---- O += P * V (fog already in P); lane owns dims lane*E .. lane*E+E-1
@@ -389,10 +407,22 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
                 }
             }
         }
+        // masked keys of a partial chunk (first / last of a range, or a bad
+        // page) get zero V rows, so the PV loop needs no per-key branch and
+        // 0 * (stale NaN) cannot reach O; each lane zeroes the dims it reads
+        const bool partial = bad || key0 < si.k_lo || key0 + 8 > si.k_hi;    // warp-uniform
+        if (partial) {
+            float* zV = sw + sl * Lay::kStage + Lay::kChunk;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const int j = key0 + r;
+                if (!(bad || j < si.k_lo || j >= si.k_hi)) continue;
+                if (E == 4) *reinterpret_cast<float4*>(zV + tile_off(r, lane)) = make_float4(0.f, 0.f, 0.f, 0.f);
+                else *reinterpret_cast<float2*>(zV + tile_off(r, lane >> 1) + (lane & 1) * 2) = make_float2(0.f, 0.f);
+            }
+        }
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
-            const int j = key0 + r;
-            if (bad || j < si.k_lo || j >= si.k_hi) continue;     // warp-uniform
             uint64_t v2[E];                                        // (v[e], v[e]): one V value for a head pair
             if (E == 4) {
                 const float4 vf = *reinterpret_cast<const float4*>(sV + tile_off(r, lane));
@@ -413,6 +443,9 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
                 }
             }
         }
+        // the zero rows (generic proxy) are ordered before the TMA refill of
+        // this stage (async proxy), which follows the next iteration's warp barrier
+        if (partial) ptx::fence_proxy_async_smem();
     }
     if (stuck >= 0) {
         // box loads still in flight land before the stages are reused
@@ -424,6 +457,34 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
     // ---- merge the 8 warps (each writes into its own stage area)
     float* mw = sw;              // [GP][2] (m, l)
     float* ow = sw + 2 * GP;     // [GP][D]
+    // The running max trails the true max by at most kSlack: move the warp's
+    // (m, l, O) to the true max, so the merges and the reported partials
+    // carry the exact maximum.
+#pragma unroll
+    for (int h = 0; h < H4; ++h) {
+        l[h] += __shfl_xor_sync(kFull, l[h], 4);
+        l[h] += __shfl_xor_sync(kFull, l[h], 8);
+        l[h] += __shfl_xor_sync(kFull, l[h], 16);
+        float mt = mx[h];
+        mt = fmaxf(mt, __shfl_xor_sync(kFull, mt, 4));
+        mt = fmaxf(mt, __shfl_xor_sync(kFull, mt, 8));
+        mt = fmaxf(mt, __shfl_xor_sync(kFull, mt, 16));
+        const float al = mt == -INFINITY ? 1.f : exp2f(m[h] - mt);
+        l[h] *= al;
+        m[h] = mt;
+        if (kk == 0) sA[dq * H4 + h] = al;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int g4 = 0; g4 < GP / 4; ++g4) {
+        const float4 a = *reinterpret_cast<const float4*>(sA + g4 * 4);
+        const uint64_t a01 = ptx::f2_pack(a.x, a.y), a23 = ptx::f2_pack(a.z, a.w);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            acc2[g4 * 2][e] = ptx::fmul2(acc2[g4 * 2][e], a01);
+            acc2[g4 * 2 + 1][e] = ptx::fmul2(acc2[g4 * 2 + 1][e], a23);
+        }
+    }
     if (kk == 0) {
 #pragma unroll
         for (int h = 0; h < H4; ++h) {
