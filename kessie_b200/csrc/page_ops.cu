@@ -525,13 +525,16 @@ __global__ void __launch_bounds__(256, INSERT ? 5 : 6) rope_tokens_kernel(
     // go through shared memory first: a kernel parameter read at a per-thread
     // index is serialised by the constant cache.
     for (int i = threadIdx.x; i < half; i += blockDim.x) fqs[i] = ft.f[i];
-    __syncthreads();
+    // tokens whose position moves by the same amount share one table row: a
+    // recalled page moves its consecutive positions by one delta, so the
+    // usual CTA (its tokens in one page) builds a single row
+    auto delta = [&](int t) -> int { return (tgt ? tgt[t] : conv_pos + t) - orig[t]; };
+    const int d0 = delta(t0);
+    const bool uni = __syncthreads_and((int)threadIdx.x >= nt || delta(t0 + (int)threadIdx.x) == d0) != 0;
     const int hp = half / 2;
-    for (int i = threadIdx.x; i < nt * hp; i += blockDim.x) {
+    for (int i = threadIdx.x; i < (uni ? 1 : nt) * hp; i += blockDim.x) {
         const int tl = i / hp, dp = i - tl * hp;
-        const int t = t0 + tl;
-        const int target = tgt ? tgt[t] : conv_pos + t;
-        const float dlt = (float)(target - orig[t]);
+        const float dlt = (float)(uni ? d0 : delta(t0 + tl));
         float4 cs;
         rope_sincos(dlt * fqs[2 * dp], &cs.y, &cs.x);
         rope_sincos(dlt * fqs[2 * dp + 1], &cs.w, &cs.z);
@@ -565,7 +568,7 @@ __global__ void __launch_bounds__(256, INSERT ? 5 : 6) rope_tokens_kernel(
     };
     if (kact) {
         float4 cs[N / 2];
-        const float4* tp = tab + ktl * hp + kc * (N / 2);
+        const float4* tp = tab + (uni ? 0 : ktl * hp) + kc * (N / 2);
 #pragma unroll
         for (int q = 0; q < N / 2; ++q) cs[q] = tp[q];
 #pragma unroll
