@@ -177,7 +177,13 @@ int kessie_page_insert_v2(void* kv_cache, int dtype, int64_t page_stride, int64_
  * (kessie_hip_kernels.py:558-564) and the connector's block copies
  * (kessie_kv_connector.py:419-428, 467-479).  Ids outside [0,max_pages)
  * produce zero rows and set KESSIE_DEV_BAD_PAGE_ID.  Either output may be
- * NULL (gather only K or only V). */
+ * NULL (gather only K or only V).  With rows of H*D contiguous elements the
+ * gather is a programmatic dependent launch, like kessie_tiered_update_v2:
+ * its first page loads may start before the previous kernel on the stream
+ * completes when the last such launch of this library on that stream wrote
+ * none of the cache or page-id bytes it reads; it writes only after that
+ * kernel completes.  A kernel that writes the cache or the ids must not be
+ * launched with a programmatic dependency that triggers before its writes. */
 int kessie_page_gather_v2(const void* kv_cache, int dtype, int64_t page_stride,
                           int64_t token_stride, int64_t kv_stride, int64_t head_stride,
                           int max_pages, int page_size, const int32_t* page_ids, int num_gather,

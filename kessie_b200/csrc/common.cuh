@@ -26,6 +26,22 @@ int* device_status_ptr();
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// ------------------------------------------- programmatic dependent launches
+// Kernels of this library launched as programmatic dependents wait for the
+// preceding grid (griddepcontrol.wait) before they let the next launch start
+// (launch_dependents), so while one runs, at most its immediate predecessor
+// still runs.  Such a kernel may issue loads before its wait ("early reads")
+// when that predecessor writes none of the bytes the loads read.  The
+// library records, per (device, stream), the byte ranges written by the last
+// programmatic launch it made there; a launch that is not programmatic
+// (library or not) serialises fully and needs no record.
+struct ByteRange { uintptr_t lo, hi; };
+// Records `writes` as the last programmatic launch on (current device,
+// `stream`) and returns true when none of the previous record's ranges
+// overlaps any of `reads` (an empty range overlaps nothing).
+bool claim_early_reads(cudaStream_t stream, const ByteRange* reads, int nreads, const ByteRange* writes,
+                       int nwrites);
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // Scoped NVTX range around a C-ABI entry point, so host-side timelines

@@ -141,6 +141,7 @@ struct BulkArgs {
     int units;
     int ns, stage_b;                // ring stages, bytes per stage
     int* status;
+    int early;                      // first ring fill before griddepcontrol.wait
 };
 
 __global__ void __launch_bounds__(64, 1) page_gather_bulk_kernel(const BulkArgs a) {
@@ -165,6 +166,17 @@ __global__ void __launch_bounds__(64, 1) page_gather_bulk_kernel(const BulkArgs 
         ptx::fence_mbar_init();
     }
     __syncthreads();
+    // Programmatic dependent launch: a thread touches global memory only after
+    // the preceding grid has completed (griddepcontrol.wait), then lets the
+    // next launch start.  With a.early the producer issues its first ring
+    // fill (reads of the page ids and of the cache only) before its wait; the
+    // host allows that only when the preceding programmatic launch of this
+    // library wrote none of those bytes.  Every store follows the wait.
+    const bool early_producer = a.early && threadIdx.x == 0;
+    if (!early_producer) {
+        ptx::grid_dependency_wait();
+        ptx::launch_dependents();
+    }
     const uint32_t R = (uint32_t)a.R;
     const uint32_t blk = (uint32_t)a.ps * R;          // one K (or V) block of a page
     auto fail = [&]() {
@@ -175,7 +187,12 @@ __global__ void __launch_bounds__(64, 1) page_gather_bulk_kernel(const BulkArgs 
         // ------------------------------------------------------------ producer
         int issued = 0;
         if (lane == 0) {
+            bool waited = !early_producer;
             for (int k = 0; k < my_units && !*abort_flag; ++k) {
+                if (!waited && k == a.ns) {
+                    ptx::grid_dependency_wait();
+                    waited = true;
+                }
                 const int s = k % a.ns;
                 if (k >= a.ns && !ptx::mbar_wait(&empty[s], (uint32_t)(k / a.ns - 1) & 1u)) { fail(); break; }
                 const int pg = page_of(unit_of(k));
@@ -192,6 +209,7 @@ __global__ void __launch_bounds__(64, 1) page_gather_bulk_kernel(const BulkArgs 
                 }
                 issued = k + 1;
             }
+            if (!waited) ptx::grid_dependency_wait();
         }
         __syncwarp();
         // the CTA exits only after every issued load has landed (bounded)
@@ -254,7 +272,34 @@ int launch_gather_bulk(BulkArgs a, cudaStream_t st) {
         return 0;
     }
     const int grid = std::min(a.units, sm_count());
-    page_gather_bulk_kernel<<<grid, 64, smem, st>>>(a);
+    // early reads: the cache rows and page ids this gather reads against the
+    // bytes the preceding programmatic launch on the stream wrote
+    {
+        const uintptr_t cb = reinterpret_cast<uintptr_t>(a.cache), ib = reinterpret_cast<uintptr_t>(a.ids);
+        const int64_t span = (int64_t)(a.max_pages - 1) * a.page_b + (int64_t)(a.ps - 1) * a.token_b +
+                             (a.rv ? a.kv_b : 0) + a.R;
+        const bool fwd = a.page_b >= 0 && a.token_b >= 0 && a.kv_b >= 0;
+        const ByteRange reads[2] = {{cb, cb + (uintptr_t)span}, {ib, ib + (uintptr_t)a.units * 4}};
+        const uintptr_t kb = reinterpret_cast<uintptr_t>(a.rk), vb = reinterpret_cast<uintptr_t>(a.rv);
+        const uintptr_t out_b = (uintptr_t)a.units * a.ps * (uintptr_t)a.R;
+        const ByteRange writes[2] = {a.rk ? ByteRange{kb, kb + out_b} : ByteRange{0, 0},
+                                     a.rv ? ByteRange{vb, vb + out_b} : ByteRange{0, 0}};
+        a.early = claim_early_reads(st, reads, 2, writes, 2) && fwd ? 1 : 0;
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(64);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, page_gather_bulk_kernel, a) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
     return 1;
 }
 

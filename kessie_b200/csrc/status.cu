@@ -5,7 +5,9 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 namespace {
 
@@ -76,6 +78,40 @@ int sm_count() {
         g_sm_count[dev] = n;
     }
     return g_sm_count[dev];
+}
+
+namespace {
+constexpr int kMaxWrites = 4;
+struct LaunchWrites { int n; ByteRange r[kMaxWrites]; };
+std::mutex g_pdl_mu;
+std::map<std::pair<int, uintptr_t>, LaunchWrites> g_last_pdl;
+bool overlaps(const ByteRange& a, const ByteRange& b) { return a.lo < a.hi && b.lo < b.hi && a.lo < b.hi && b.lo < a.hi; }
+}  // namespace
+
+bool claim_early_reads(cudaStream_t stream, const ByteRange* reads, int nreads, const ByteRange* writes,
+                       int nwrites) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        dev = -1;
+    }
+    LaunchWrites w;
+    w.n = nwrites < kMaxWrites ? nwrites : kMaxWrites;
+    for (int i = 0; i < w.n; ++i) w.r[i] = writes[i];
+    bool early = nwrites <= kMaxWrites;
+    std::lock_guard<std::mutex> lk(g_pdl_mu);
+    const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
+    auto it = g_last_pdl.find(key);
+    if (it != g_last_pdl.end())
+        for (int i = 0; i < it->second.n; ++i)
+            for (int j = 0; j < nreads; ++j)
+                if (overlaps(it->second.r[i], reads[j])) early = false;
+    if (nwrites > kMaxWrites) {
+        w.n = 1;                                    // unknown writes: everything overlaps the next reads
+        w.r[0] = ByteRange{0, ~uintptr_t(0)};
+    }
+    g_last_pdl[key] = w;
+    return early;
 }
 
 }  // namespace kessie

@@ -26,9 +26,6 @@
 
 #include <math.h>
 
-#include <map>
-#include <mutex>
-#include <utility>
 
 namespace kessie {
 namespace {
@@ -83,9 +80,10 @@ constexpr int kItems = 4;                                  // 16-byte items in f
 // launch start (launch_dependents), so while a grid runs, every grid launched
 // before its predecessor has completed.  With a.early the loads of the live V
 // rows already in the store are issued BEFORE the wait, overlapping the
-// preceding grid's drain: the host sets it only when the last tiered update
-// launched on this stream wrote none of this V store, so the one grid that
-// can still be running writes no byte these loads read.  Loads of the new
+// preceding grid's drain: the host sets it only when the last programmatic
+// launch of this library on this stream (claim_early_reads) wrote none of
+// this V store, so the one grid that can still be running writes no byte
+// these loads read.  Loads of the new
 // tokens (written by the caller's producer) and every store follow the wait.
 template <typename T, int CH>
 __global__ void __launch_bounds__(256) tiered_update_kernel(TieredUpdateArgs a) {
@@ -200,30 +198,6 @@ int grid_x(long long items, long long rows_y) {
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Byte ranges written by the last tiered update launched on each (device,
-// stream) of this process: K store, V store, fogged V.  An update may read its
-// V store early exactly when none of these ranges overlaps it.
-struct ByteRange { uintptr_t lo, hi; };
-struct UpdateWrites { ByteRange r[3]; };
-std::mutex g_last_mu;
-std::map<std::pair<int, uintptr_t>, UpdateWrites> g_last_update;
-
-bool overlaps(const ByteRange& a, const ByteRange& b) { return a.lo < b.hi && b.lo < a.hi; }
-
-// Decides the early flag of an update that reads `v_reads` and writes `w` on
-// (dev, stream), and records `w` as that stream's last update.
-bool claim_early_read(int dev, cudaStream_t stream, const ByteRange& v_reads, const UpdateWrites& w) {
-    std::lock_guard<std::mutex> lock(g_last_mu);
-    const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
-    bool early = true;
-    auto it = g_last_update.find(key);
-    if (it != g_last_update.end())
-        for (const ByteRange& r : it->second.r)
-            if (overlaps(r, v_reads)) early = false;
-    g_last_update[key] = w;
-    return early;
-}
-
 }  // namespace
 }  // namespace kessie
 
@@ -274,13 +248,10 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
         const uintptr_t store_bytes = (uintptr_t)((long long)B * H * cap * a.chunks * 16);
         const uintptr_t kb = reinterpret_cast<uintptr_t>(k_store), vb = reinterpret_cast<uintptr_t>(v_store);
         const uintptr_t fb = reinterpret_cast<uintptr_t>(v_fog);
-        UpdateWrites w;
-        w.r[0] = {kb, kb + store_bytes};
-        w.r[1] = {vb, vb + store_bytes};
-        w.r[2] = v_fog ? ByteRange{fb, fb + (uintptr_t)((long long)B * H * S * a.chunks * 16)} : ByteRange{0, 0};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        a.early = claim_early_read(dev, st, w.r[1], w) && v_fog != nullptr ? 1 : 0;
+        const ByteRange w[3] = {{kb, kb + store_bytes}, {vb, vb + store_bytes},
+                                v_fog ? ByteRange{fb, fb + (uintptr_t)((long long)B * H * S * a.chunks * 16)}
+                                      : ByteRange{0, 0}};
+        a.early = claim_early_reads(st, &w[1], 1, w, 3) && v_fog != nullptr ? 1 : 0;
     }
     const dim3 grid(grid_x(rows * a.chunks, (long long)B * H), B * H);
     cudaLaunchAttribute attr[1];

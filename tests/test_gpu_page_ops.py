@@ -230,6 +230,41 @@ def test_page_gather_matches_oracle(layout, dt):
     assert np.array_equal(to_np(K), wk) and np.array_equal(to_np(V), wv)
 
 
+def test_page_gather_back_to_back():
+    """Gathers enqueued with nothing in between and no synchronisation, as a
+    multi-layer recall runs them: each may start loading its pages before the
+    previous gather has finished, which is allowed only when that gather
+    wrote none of the bytes it reads.  Four caches in turn, three rounds, then
+    a gather whose output overwrites part of the next gather's cache (that
+    one must wait); all bit-exact."""
+    from kessie_b200 import ops
+    P, ps, H, D, n = 64, 16, 8, 128, 24
+    caches = [make_paged(40 + i, P, ps, H, D, "bf16") for i in range(4)]
+    rng = np.random.default_rng(5)
+    ids = [rng.permutation(P)[:n].astype(np.int32) for _ in range(4)]
+    ids_d = [torch.from_numpy(x).cuda() for x in ids]
+    outs = [(torch.empty(n * ps, H, D, dtype=torch.bfloat16, device="cuda"),
+             torch.empty(n * ps, H, D, dtype=torch.bfloat16, device="cuda")) for _ in range(4)]
+    torch.cuda.synchronize()
+    for _ in range(3):
+        for i in range(4):
+            ops.page_gather(caches[i][1], ids_d[i], out_keys=outs[i][0], out_values=outs[i][1])
+    # cache 1's K pages land in the first bytes of cache 0, which the next gather reads
+    c0 = caches[0][1]
+    k_into_c0 = c0.view(-1)[:n * ps * H * D].view(n * ps, H, D)
+    ops.page_gather(caches[1][1], ids_d[1], out_keys=k_into_c0, want_values=False)
+    K0, V0 = ops.page_gather(c0, ids_d[0])
+    torch.cuda.synchronize()
+    for i in range(4):
+        wk, wv = O.page_gather(caches[i][0], ids[i])
+        assert np.array_equal(to_np(outs[i][0]), wk) and np.array_equal(to_np(outs[i][1]), wv)
+    c0n = caches[0][0].copy().reshape(-1)
+    c0n[:n * ps * H * D] = O.page_gather(caches[1][0], ids[1])[0].reshape(-1)
+    wk, wv = O.page_gather(c0n.reshape(P, ps, 2, H, D), ids[0])
+    assert np.array_equal(to_np(K0), wk) and np.array_equal(to_np(V0), wv)
+    assert np.array_equal(to_np(c0).reshape(-1), c0n)
+
+
 def test_page_gather_bad_id_zero_and_flag():
     from kessie_b200 import ops
     _status()
