@@ -286,6 +286,22 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
         cp_async_commit();
     }
     const int kk = lane >> 2, dq = lane & 3;
+    // At GP 4 the lane's q slice (its quarter of 4 heads: 128 floats) stays in
+    // registers for the whole range, halving the shared loads per chunk; at
+    // GP 8 / 16 it does not fit, and the loop reads it from shared memory.
+    constexpr bool kQReg = GP == 4;
+    constexpr int kQG = kQReg ? GP / 2 : 1, kQC = kQReg ? CPL : 1;
+    float4 qreg[kQG][kQC][2];
+    if (kQReg) {
+#pragma unroll
+        for (int gp = 0; gp < kQG; ++gp)
+#pragma unroll
+            for (int cc = 0; cc < kQC; ++cc) {
+                const int c0 = dq * QC + 2 * cc;
+                qreg[gp][cc][0] = *reinterpret_cast<const float4*>(sq + (gp * (D / 2) + (c0 ^ dq)) * 4);
+                qreg[gp][cc][1] = *reinterpret_cast<const float4*>(sq + (gp * (D / 2) + ((c0 + 1) ^ dq)) * 4);
+            }
+    }
     int stuck = -1;      // chunk whose wait gave up (warp-uniform); the rest is not read
     for (int i = 0; i < nw; ++i) {
         const bool ok = __all_sync(kFull, ptx::mbar_wait(&bars[i % kNS], (uint32_t)(i / kNS) & 1u));
@@ -323,8 +339,10 @@ __global__ void __launch_bounds__(kT, 1) fog_decode_f32_kernel(const DecodeF32Ar
             const int c0 = dq * QC + 2 * cc;           // chunks of dims 4cc.. 4cc+3 of the quarter
 #pragma unroll
             for (int gp = 0; gp < GP / 2; ++gp) {
-                const float4 qa = *reinterpret_cast<const float4*>(sq + (gp * (D / 2) + (c0 ^ dq)) * 4);
-                const float4 qb = *reinterpret_cast<const float4*>(sq + (gp * (D / 2) + ((c0 + 1) ^ dq)) * 4);
+                const float4 qa = kQReg ? qreg[kQReg ? gp : 0][kQReg ? cc : 0][0]
+                                        : *reinterpret_cast<const float4*>(sq + (gp * (D / 2) + (c0 ^ dq)) * 4);
+                const float4 qb = kQReg ? qreg[kQReg ? gp : 0][kQReg ? cc : 0][1]
+                                        : *reinterpret_cast<const float4*>(sq + (gp * (D / 2) + ((c0 + 1) ^ dq)) * 4);
                 s2[gp] = ptx::ffma2(ptx::f2_pack(qa.x, qa.y), kx, s2[gp]);
                 s2[gp] = ptx::ffma2(ptx::f2_pack(qa.z, qa.w), ky, s2[gp]);
                 s2[gp] = ptx::ffma2(ptx::f2_pack(qb.x, qb.y), kz, s2[gp]);
