@@ -126,7 +126,13 @@ void launch_kessie_rope_remap(void* k_data, const void* orig_positions,
  * head_dim contiguous).  Same math as kessie_hip_kernels.py:596-606 /
  * kessie_kernels_v2.hip:670-707; the frequency table 1/theta^(d/half) is
  * computed once on the host in float64 and rounded to fp32 (bit-identical to
- * the reference's torch table at theta 1e4 and 5e5). */
+ * the reference's torch table at theta 1e4 and 5e5).  With 16-byte aligned
+ * rows it is a programmatic dependent launch, like kessie_page_gather_v2: its
+ * rows and positions may be copied in before the previous kernel on the
+ * stream completes when the last such launch of this library there wrote none
+ * of them; it writes only after that kernel completes.  The same holds for
+ * kessie_page_insert_v2 with orig_positions (rows, positions and page ids
+ * read early; cache rows and page metadata written after). */
 int kessie_rope_remap_v2(void* k_data, int dtype, int num_tokens, int num_heads, int head_dim,
                          int64_t token_stride, int64_t head_stride,
                          const int32_t* orig_positions, const int32_t* target_positions,

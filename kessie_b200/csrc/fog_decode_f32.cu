@@ -30,7 +30,8 @@
 //           K with every query head of the group, two heads per packed fp32
 //           FMA (fma.rn.f32x2; q staged once per CTA by head pairs, pre-scaled
 //           by sm_scale*log2e, swizzled so the four quarters read distinct
-//           banks); a two-step transposing shuffle reduction over the
+//           banks, and at GP 4 held in registers for the whole range); a
+//           two-step transposing shuffle reduction over the
 //           quarters leaves each lane the full scores of GP/4 heads of its key.
 //   soft  = online softmax per head across the chunk's 8 keys with a lazy
 //           max: the running max m moves (xor-shuffle max over the key lanes,

@@ -305,6 +305,28 @@ int launch_gather_bulk(BulkArgs a, cudaStream_t st) {
 
 bool bulk_ok(int64_t bytes) { return bytes % 16 == 0; }
 
+// [p, p + bytes) as a byte range (empty for a null pointer or no bytes).
+ByteRange span_bytes(const void* p, int64_t bytes) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+    return (p && bytes > 0) ? ByteRange{b, b + (uintptr_t)bytes} : ByteRange{0, 0};
+}
+
+// Launch as a programmatic dependent of the preceding kernel on the stream.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // ------------------------------------------------------------------ RoPE remap
 // CTA = `tpb` tokens.  Stage 1: cos/sin of (tgt-orig)*f_d for the CTA's tokens
 // into smem.  Stage 2: every (token, head, 16B chunk of the low half) item
@@ -520,8 +542,18 @@ __global__ void __launch_bounds__(256, INSERT ? 5 : 6) rope_tokens_kernel(
     int half, int64_t sts, int64_t shs, int64_t dts, int64_t dhs, int64_t dkv, int64_t page_stride, int ps,
     const int32_t* __restrict__ page_ids, int max_pages, int8_t* __restrict__ valid, int32_t* __restrict__ positions,
     int conv_pos, const int32_t* __restrict__ orig, const int32_t* __restrict__ tgt, FreqTable ft, int tpb,
-    int* status, int bulk_st) {
+    int* status, int bulk_st, int early) {
     extern __shared__ float4 tab[];                 // [tpb][half/2] of (cos d, sin d, cos d+1, sin d+1)
+    // Programmatic dependent launch: every global access follows the wait for
+    // the preceding grid, then the next launch may start -- except that with
+    // `early` (the host found that the preceding programmatic launch of this
+    // library wrote none of the rows, positions and page ids read here) the
+    // copies in and the angle table run before the wait, overlapping the
+    // preceding grid's last CTAs; every store still follows it.
+    if (!early) {
+        ptx::grid_dependency_wait();
+        ptx::launch_dependents();
+    }
     constexpr int N = VecOps<T>::N;
     const int hc = half / N;                        // 16-byte chunks per half row
     const int hg = num_heads / HPT;                 // head groups
@@ -593,17 +625,27 @@ __global__ void __launch_bounds__(256, INSERT ? 5 : 6) rope_tokens_kernel(
             const int phys = page_ids[t / ps];
             const bool ok = phys >= 0 && phys < max_pages;
             rowoff[tl] = ok ? (long long)phys * page_stride + (long long)(t % ps) * dts : -1ll;
-            if (t % ps == 0) {
-                if (!ok) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
-                else {
-                    if (valid) valid[phys] = 1;
-                    if (positions) positions[phys] = conv_pos + t;
-                }
-            }
         }
     }
     cp_async_wait_all();
     __syncthreads();
+    if (early) {
+        ptx::grid_dependency_wait();
+        ptx::launch_dependents();
+    }
+    if (INSERT) {
+        for (int tl = threadIdx.x; tl < nt; tl += blockDim.x) {
+            const int t = t0 + tl;
+            if (t % ps) continue;
+            const long long off = rowoff[tl];
+            if (off < 0) record_status(status, KESSIE_DEV_BAD_PAGE_ID);
+            else {
+                const int phys = page_ids[t / ps];
+                if (valid) valid[phys] = 1;
+                if (positions) positions[phys] = conv_pos + t;
+            }
+        }
+    }
     // ---- 3. rotate the K pairs with one table read for all HPT heads; copy V
     auto dst_row = [&](int tl, int h, bool& ok) -> T* {
         if (!INSERT) { ok = true; return dst + (int64_t)(t0 + tl) * dts + (int64_t)h * dhs; }
@@ -713,9 +755,15 @@ int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int
     if (tpb_t > 0) {
         size_t smem = rope_tokens_smem(tpb_t, H, half, (int)sizeof(T), false);
         auto kern = hpt == 2 ? rope_tokens_kernel<T, false, 2> : rope_tokens_kernel<T, false, 1>;
-        kern<<<(T_ + tpb_t - 1) / tpb_t, 256, smem, st>>>(
-            (T*)k, (const T*)k, nullptr, T_, H, half, ts, hs, ts, hs, 0, 0, 1, nullptr, 0, nullptr, nullptr, 0, orig, tgt,
-            ft, tpb_t, nullptr, 0);
+        const int64_t es = sizeof(T);
+        const ByteRange krows = span_bytes(k, ((int64_t)(T_ - 1) * ts + (int64_t)(H - 1) * hs + D) * es);
+        const ByteRange reads[3] = {krows, span_bytes(orig, (int64_t)T_ * 4), span_bytes(tgt, tgt ? (int64_t)T_ * 4 : 0)};
+        const int early = claim_early_reads(st, reads, 3, &krows, 1) && ts >= 0 && hs >= 0 ? 1 : 0;
+        if (launch_pdl(kern, dim3((T_ + tpb_t - 1) / tpb_t), dim3(256), smem, st, (T*)k, (const T*)k,
+                       (const T*)nullptr, T_, H, half, ts, hs, ts, hs, (int64_t)0, (int64_t)0, 1,
+                       (const int32_t*)nullptr, 0, (int8_t*)nullptr, (int32_t*)nullptr, 0, orig, tgt, ft, tpb_t,
+                       (int*)nullptr, 0, early) != cudaSuccess)
+            return check_launch("rope_remap");
     } else if (vec && rows_shape<T>(H, D, tt, threads, cpr, kt)) {
         size_t smem = (size_t)2 * tt * half * sizeof(float);
         launch_rows<T, 0>(kt, dim3((T_ + tt - 1) / tt), threads, smem, st, (T*)k, (const T*)k, nullptr, T_, H, half,
@@ -1096,10 +1144,22 @@ int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv
         auto kern = hpt == 2 ? rope_tokens_kernel<T, true, 2> : rope_tokens_kernel<T, true, 1>;
         // destination rows of all heads contiguous: K and V rows leave as bulk copies
         const int bulk_st = (g.head_stride == g.head_dim && ((int64_t)g.num_heads * g.head_dim * es) % 16 == 0) ? 1 : 0;
-        kern<<<(T_ + tpb_i - 1) / tpb_i, 256, smem, st>>>(
-            (T*)cache, (const T*)nk, (const T*)nv, T_, g.num_heads, g.head_dim / 2, sts, shs, g.token_stride,
-            g.head_stride, g.kv_stride, g.page_stride, g.page_size, ids, g.max_pages, valid, positions, conv_pos, orig,
-            tgt, ft, tpb_i, status, bulk_st);
+        const int64_t rows_e = (int64_t)(T_ - 1) * sts + (int64_t)(g.num_heads - 1) * shs + g.head_dim;
+        const ByteRange reads[5] = {span_bytes(nk, rows_e * es), span_bytes(nv, rows_e * es),
+                                    span_bytes(ids, (int64_t)pages * 4), span_bytes(orig, (int64_t)T_ * 4),
+                                    span_bytes(tgt, tgt ? (int64_t)T_ * 4 : 0)};
+        const int64_t cache_e = (int64_t)(g.max_pages - 1) * g.page_stride + (int64_t)(g.page_size - 1) * g.token_stride +
+                                g.kv_stride + (int64_t)(g.num_heads - 1) * g.head_stride + g.head_dim;
+        const ByteRange writes[3] = {span_bytes(cache, cache_e * es), span_bytes(valid, valid ? g.max_pages : 0),
+                                     span_bytes(positions, positions ? (int64_t)g.max_pages * 4 : 0)};
+        const bool fwd = sts >= 0 && shs >= 0 && g.page_stride >= 0 && g.token_stride >= 0 && g.kv_stride >= 0 &&
+                         g.head_stride >= 0;
+        const int early = claim_early_reads(st, reads, 5, writes, 3) && fwd ? 1 : 0;
+        if (launch_pdl(kern, dim3((T_ + tpb_i - 1) / tpb_i), dim3(256), smem, st, (T*)cache, (const T*)nk,
+                       (const T*)nv, T_, g.num_heads, g.head_dim / 2, sts, shs, g.token_stride, g.head_stride,
+                       g.kv_stride, g.page_stride, g.page_size, ids, g.max_pages, valid, positions, conv_pos, orig,
+                       tgt, ft, tpb_i, status, bulk_st, early) != cudaSuccess)
+            return check_launch("page_insert");
     } else if (orig && vec && g.page_size <= 256 && rows_shape<T>(g.num_heads, g.head_dim, g.page_size, threads, cpr, kt)) {
         FreqTable ft = make_freqs(theta, g.head_dim / 2);
         size_t smem = (size_t)2 * g.page_size * (g.head_dim / 2) * sizeof(float);

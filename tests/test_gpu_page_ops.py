@@ -265,6 +265,58 @@ def test_page_gather_back_to_back():
     assert np.array_equal(to_np(c0).reshape(-1), c0n)
 
 
+def test_remap_and_insert_back_to_back():
+    """RoPE remaps and fused inserts enqueued with nothing in between and no
+    synchronisation, as a multi-layer recall runs them: a launch may copy its
+    rows in before the previous one has finished when that one wrote none of
+    them.  Four K buffers remapped in turn twice, a gather followed at once by
+    a remap of its output (which must wait for it), and fused inserts into
+    three caches in turn."""
+    from kessie_b200 import ops
+    T, H, D, P, ps, theta = 256, 8, 128, 64, 16, 500000.0
+    rng = np.random.default_rng(8)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    xs = [ROUND["bf16"](rnd(60 + i, (T, H, D))) for i in range(4)]
+    ks = [to_dev(x, "bf16") for x in xs]
+    # per-token positions (no shared delta) for two buffers, page-aligned shifts for the others
+    origs = [rng.integers(0, 100000, T).astype(np.int32) if i < 2 else
+             (16 * np.repeat(rng.permutation(1000)[:T // 16], 16) + np.tile(np.arange(16), T // 16)).astype(np.int32)
+             for i in range(4)]
+    tgts = [(131072 + np.arange(T)).astype(np.int32) for _ in range(4)]
+    od, td = [dev(o) for o in origs], [dev(t) for t in tgts]
+    kvn, kv = make_paged(70, P, ps, H, D, "bf16")
+    gids = rng.permutation(P)[:T // ps].astype(np.int32)
+    gids_d = dev(gids)
+    caches = [torch.zeros(P, ps, 2, H, D, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    vals = [ROUND["bf16"](rnd(80 + i, (T, H, D))) for i in range(3)]
+    vals_d = [to_dev(v, "bf16") for v in vals]
+    ins_ids = [rng.permutation(P)[:T // ps].astype(np.int32) for _ in range(3)]
+    ins_d = [dev(x) for x in ins_ids]
+    torch.cuda.synchronize()
+    for _ in range(2):
+        for i in range(4):
+            ops.rope_remap(ks[i], od[i], td[i], theta)
+    K, _ = ops.page_gather(kv, gids_d)
+    ops.rope_remap(K, od[3], td[3], theta)
+    for i in range(3):
+        ops.page_insert(caches[i], ks[i], vals_d[i], ins_d[i], conv_pos=131072, orig_positions=od[i], rope_theta=theta)
+    torch.cuda.synchronize()
+    want = []
+    for i in range(4):
+        w = ROUND["bf16"](O.rope_remap(xs[i], origs[i], tgts[i], theta))
+        w = ROUND["bf16"](O.rope_remap(w, origs[i], tgts[i], theta))
+        want.append(w)
+        np.testing.assert_allclose(to_np(ks[i]), w, **TOL["bf16"])
+    wk = O.page_gather(kvn, gids)[0]
+    np.testing.assert_allclose(to_np(K), ROUND["bf16"](O.rope_remap(wk, origs[3], tgts[3], theta)), **TOL["bf16"])
+    for i in range(3):
+        got = to_np(caches[i])
+        rot = ROUND["bf16"](O.rope_remap(to_np(ks[i]), origs[i], 131072 + np.arange(T), theta))
+        for p_, pid in enumerate(ins_ids[i]):
+            np.testing.assert_allclose(got[pid, :, 0], rot[p_ * ps:(p_ + 1) * ps], **TOL["bf16"])
+            assert np.array_equal(got[pid, :, 1], vals[i][p_ * ps:(p_ + 1) * ps])
+
+
 def test_page_gather_bad_id_zero_and_flag():
     from kessie_b200 import ops
     _status()
