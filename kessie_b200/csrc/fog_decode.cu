@@ -19,7 +19,7 @@
 //           from seq_lens, so the launch needs no host synchronisation.
 //           A CTA's range splits into "segments", one per group it touches;
 //           each KV byte is read once for all Hq/Hkv query heads (GQA).
-//   CTA   = 1 producer warp + 4 consumer warps.  The producer prefetches page
+//   CTA   = 1 producer warp + 4 consumer warps + 1 helper warp.  The producer prefetches page
 //           ids 128 units ahead (registers -> smem window) and issues one TMA
 //           tensor load per 16-token K (and V) slice into a 3-stage ring
 //           (mbarrier full/empty pairs, bounded waits).  Tiles are 128-byte
@@ -42,7 +42,13 @@
 //           self-validating (value, epoch) words -- no fence, no flag, so the
 //           storing CTA never waits on the remote stores (cp_layout.cuh).
 //           The merging CTA also zeroes the counter, so graph replays (same
-//           tag) start clean.
+//           tag) start clean.  A segment that ends inside the CTA's range
+//           (its group continues in the next CTA) is handed to the helper
+//           warp through a shared-memory staging area: the helper stores the
+//           partial, fences, arrives and merges if it was last, while the
+//           consumers go on streaming.  Under a saturated memory system that
+//           fence took ~5 us, and the CTAs that switch groups were the last to
+//           finish.
 //   cp    = cp_combine_kernel polls its own exchange buffer (bounded) until
 //           every rank's words of a row carry the step's epoch, then merges
 //           the world shard results.  One decode kernel and one small combine
@@ -66,7 +72,8 @@ namespace {
 constexpr int kNCW = 4;          // consumer warps
 constexpr int kNST = 3;          // pipeline stages
 constexpr int kIdWin = 128;      // page ids per prefetch window (units)
-constexpr int kThreads = (kNCW + 1) * 32;
+constexpr int kHelperWarp = kNCW + 1;  // finishes mid-range segment ends for the consumers
+constexpr int kThreads = (kNCW + 2) * 32;
 constexpr int kCtasPerSm = 2;    // upper bound used to size the workspace
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -146,9 +153,10 @@ struct Smem {
     static constexpr int kMrgOff = kNST * kStage;
     static constexpr int kIdsOff = kMrgOff + 2 * kMrgFloats * 4;
     static constexpr int kMetaOff = kIdsOff + kIdWin * 4;
-    static constexpr int kBarOff = (kMetaOff + kNST * kNCW * 4 + 7) & ~7;
-    static constexpr int kCtlOff = kBarOff + 2 * kNST * 8;
-    static constexpr int kBytes = kCtlOff + 16 * 4;
+    static constexpr int kBarOff = (kMetaOff + kNST * kNCW * 4 + 7) & ~7;   // full[kNST], empty[kNST], job_full, job_empty
+    static constexpr int kCtlOff = kBarOff + (2 * kNST + 2) * 8;
+    static constexpr int kStgOff = (kCtlOff + 16 * 4 + 15) & ~15;           // handed-off partial: [QP][D] O/l, [QP][2] (m, l)
+    static constexpr int kBytes = kStgOff + QP * (D + 2) * 4;
     static constexpr int kAlloc = kBytes + 1024;          // 1 KB slack for 1024-byte alignment
 };
 
@@ -252,13 +260,14 @@ __device__ __forceinline__ void emit_row(const DecodeParams& p, int row, int lan
 }
 
 // Merge the K segment partials of group g (slots first+g .. first+K-1+g) and
-// emit its G rows; K == 0 emits empty rows.  Run by the 4 consumer warps.
+// emit its G rows; K == 0 emits empty rows.  Run by `nw` warps (warp index
+// `warp` among them): the 4 consumer warps, or the helper warp alone.
 template <int D, bool BF16>
-__device__ void merge_and_emit(const DecodeParams& p, int g, int first, int K, int warp, int lane) {
+__device__ void merge_and_emit(const DecodeParams& p, int g, int first, int K, int warp, int lane, int nw = kNCW) {
     constexpr int E = D / 32;
     const int b = g / p.Hkv, hk = g - b * p.Hkv;
     const size_t sstride = (size_t)p.G * D;
-    for (int q = warp; q < p.G; q += kNCW) {
+    for (int q = warp; q < p.G; q += nw) {
         float M = -INFINITY;
         for (int k = lane; k < K; k += 32) M = fmaxf(M, __ldcg(p.part_ml + ((size_t)(first + k + g) * p.G + q) * 2));
         M = warp_max(M);
@@ -323,12 +332,17 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
     int32_t* meta = reinterpret_cast<int32_t*>(smem + S::kMetaOff);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
     uint64_t* empty = full + kNST;
+    uint64_t* job_full = empty + kNST;     // a mid-range segment's partial is staged for the helper
+    uint64_t* job_empty = job_full + 1;    // the helper is done with the staging
+    float* stg = reinterpret_cast<float*>(smem + S::kStgOff);
     int* ctl = reinterpret_cast<int*>(smem + S::kCtlOff);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // ---------------------------------------------------------------- range of this CTA
     if (threadIdx.x == 0) {
         for (int s = 0; s < kNST; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], kNCW); }
+        ptx::mbar_init(job_full, 1);
+        ptx::mbar_init(job_empty, 1);
         ptx::fence_mbar_init();
     }
     if (warp == kNCW) {
@@ -460,6 +474,47 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
         return;
     }
 
+    // ---------------------------------------------------------------- helper
+    // A segment that ends inside the CTA's range (its group continues in the
+    // next CTA) is finished here, off the consumers' path: the consumers
+    // stage the normalised partial in shared memory and go on with the next
+    // segment, while this warp stores the partial, fences, counts the
+    // arrival and, if it was the group's last, merges the group alone.
+    // Under a saturated memory system the fence alone took several us.
+    if (warp == kHelperWarp) {
+        for (int job = 0;; ++job) {
+            // lane 0 waits (the warp may idle for most of the launch); the
+            // warp barrier orders the other lanes' reads after it
+            bool ok = true;
+            if (lane == 0) ok = ptx::mbar_wait(job_full, (uint32_t)job & 1u);
+            __syncwarp();
+            if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+                break;
+            }
+            const int slot = ctl[8], g = ctl[9], first = ctl[10], K = ctl[11];
+            if (slot < 0) break;                                    // no more segments
+            const int G = p.G;
+            float4* po = reinterpret_cast<float4*>(p.part_o + (size_t)slot * G * D);
+            const float4* so = reinterpret_cast<const float4*>(stg);
+            for (int i = lane; i < G * D / 4; i += 32) po[i] = so[i];
+            for (int i = lane; i < 2 * G; i += 32) p.part_ml[(size_t)slot * G * 2 + i] = stg[S::QP * D + i];
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = arrive(p.counters + g, p.tag) == (unsigned)(K - 1);
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                if (lane == 0) p.counters[g] = 0ull;
+                merge_and_emit<D, BF16>(p, g, first, K, 0, lane, 1);
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(job_empty);
+        }
+        return;
+    }
+
     // ---------------------------------------------------------------- consumers
     // Groups with no visible key anywhere in this shard still produce rows
     // (zeros; m = -inf, l = 0); CTA g % grid emits them.
@@ -475,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
     const int v_key = rr + 8 * (mi >> 1), v_cadd = mi & 1;     // ldmatrix rows for V (trans)
     float* mrg = reinterpret_cast<float*>(smem + S::kMrgOff);  // [2][D*QP + 2*QP]
     int itg = 0;
+    int njobs = 0;                         // segments handed to the helper
     bool broken = false;
     Segment sg;
     while (walk.next(p, sg)) {
@@ -673,37 +729,66 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
         if (warp == 1) put(mrg);
         consumers_sync();
         const int slot = (int)blockIdx.x + sg.g;
+        const int first = sg.gstart / W;
+        const int K = (sg.gstart + sg.gn - 1) / W - first + 1;
+        const bool final_seg = walk.pos >= walk.end;
         if (warp == 0) {
             take(mrg);
+            // a mid-range segment goes to the helper: wait until it has
+            // released the staging (bounded), stage, hand over
+            if (!final_seg && njobs > 0 &&
+                !__all_sync(0xffffffffu, ptx::mbar_wait(job_empty, (uint32_t)(njobs - 1) & 1u))) {
+                if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
                     const int q = nt * 8 + 2 * t + j;
                     if (q < p.G) {
-                        float* po = p.part_o + ((size_t)slot * p.G + q) * D;
+                        float* po = final_seg ? p.part_o + ((size_t)slot * p.G + q) * D : stg + q * D;
+                        float* pm = final_seg ? p.part_ml + ((size_t)slot * p.G + q) * 2 : stg + S::QP * D + q * 2;
                         const float L = l[nt][j];
 #pragma unroll
                         for (int mt = 0; mt < D / 16; ++mt) {
                             po[mt * 16 + g8] = L > 0.f ? acc[nt][mt][j] / L : 0.f;
                             po[mt * 16 + g8 + 8] = L > 0.f ? acc[nt][mt][2 + j] / L : 0.f;
                         }
-                        if (g8 == 0)
-                            *reinterpret_cast<float2*>(p.part_ml + ((size_t)slot * p.G + q) * 2) = make_float2(m[nt][j], L);
+                        if (g8 == 0) *reinterpret_cast<float2*>(pm) = make_float2(m[nt][j], L);
                     }
                 }
-            __threadfence();
+            if (final_seg) {
+                __threadfence();
+            } else {
+                __syncwarp();
+                if (lane == 0) {
+                    ctl[8] = slot; ctl[9] = sg.g; ctl[10] = first; ctl[11] = K;
+                    ptx::mbar_arrive(job_full);
+                }
+            }
+        }
+        if (!final_seg) {
+            ++njobs;
+            continue;
         }
         consumers_sync();
-        if (walk.pos >= walk.end) ptx::launch_dependents();   // last segment: the cp combine may start
-        const int first = sg.gstart / W;
-        const int K = (sg.gstart + sg.gn - 1) / W - first + 1;
+        ptx::launch_dependents();                            // last segment: the cp combine may start
         if (threadIdx.x == 0) ctl[5] = arrive(p.counters + sg.g, p.tag) == (unsigned)(K - 1);
         consumers_sync();
         if (ctl[5]) {
             __threadfence();
             if (threadIdx.x == 0) p.counters[sg.g] = 0ull;
             merge_and_emit<D, BF16>(p, sg.g, first, K, warp, lane);
+        }
+    }
+    // the helper stops once it has finished the last segment handed to it
+    if (warp == 0) {
+        if (njobs > 0 && !__all_sync(0xffffffffu, ptx::mbar_wait(job_empty, (uint32_t)(njobs - 1) & 1u))) {
+            if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
+        }
+        if (lane == 0) {
+            ctl[8] = -1;
+            ptx::mbar_arrive(job_full);
         }
     }
 }
