@@ -932,10 +932,15 @@ int launch_decode_t(const CUtensorMap& mk, const CUtensorMap& mv, const DecodePa
     auto kern = fog_decode_kernel<D, BF16, NT>;
     const int smem = Smem<D, NT>::kAlloc;
     static int occ_cache[64] = {0};
+    static std::atomic<uint64_t> attr_set{0};            // bit d: the smem attribute is set on device d
     int dev = 0;
     cudaGetDevice(&dev);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-        return check_launch("decode: set smem attribute");
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (!(attr_set.load(std::memory_order_acquire) & bit)) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return check_launch("decode: set smem attribute");
+        attr_set.fetch_or(bit, std::memory_order_acq_rel);
+    }
     int occ = dev < 64 ? occ_cache[dev] : 0;
     if (occ <= 0) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess || occ <= 0)
@@ -1028,9 +1033,9 @@ int prepare_decode(DecodeParams& p, Plan& pl, const void* q, int64_t q_stride_b,
 int run_decode(const DecodeParams& p, const void* k_cache, const void* v_cache, int64_t page_stride,
                int64_t token_stride, int64_t head_stride, int page_size, int head_dim, bool bf16, cudaStream_t st) {
     CUtensorMap mk, mv;
-    CUresult r1 = encode_kv_tile_map(&mk, k_cache, bf16, head_dim, page_size, p.Hkv, p.num_pages, token_stride,
+    CUresult r1 = encode_kv_tile_map_cached(&mk, k_cache, bf16, head_dim, page_size, p.Hkv, p.num_pages, token_stride,
                                      head_stride, page_stride);
-    CUresult r2 = encode_kv_tile_map(&mv, v_cache, bf16, head_dim, page_size, p.Hkv, p.num_pages, token_stride,
+    CUresult r2 = encode_kv_tile_map_cached(&mv, v_cache, bf16, head_dim, page_size, p.Hkv, p.num_pages, token_stride,
                                      head_stride, page_stride);
     if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: TMA descriptor rejected (%d/%d)", (int)r1, (int)r2);

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <string.h>
 
 namespace kessie {
 
@@ -44,6 +45,39 @@ inline CUresult encode_kv_tile_map(CUtensorMap* map, const void* base, bool bf16
     return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
                const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+// encode_kv_tile_map through a small cache of the last 8 distinct argument
+// sets: the encode is pure host work, but a per-call cost of a decode step.
+inline CUresult encode_kv_tile_map_cached(CUtensorMap* map, const void* base, bool bf16, int head_dim, int page_size,
+                                          int num_heads, int num_pages, int64_t token_stride, int64_t head_stride,
+                                          int64_t page_stride) {
+    struct Entry { bool used; const void* base; int64_t key[8]; CUtensorMap map; };
+    static Entry cache[8];
+    static int next = 0;
+    static std::mutex mu;
+    const int64_t key[8] = {bf16 ? 1 : 0, head_dim, page_size, num_heads, num_pages, token_stride, head_stride,
+                            page_stride};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const Entry& e : cache)
+            if (e.used && e.base == base && memcmp(e.key, key, sizeof(key)) == 0) {
+                *map = e.map;
+                return CUDA_SUCCESS;
+            }
+    }
+    const CUresult r = encode_kv_tile_map(map, base, bf16, head_dim, page_size, num_heads, num_pages, token_stride,
+                                          head_stride, page_stride);
+    if (r == CUDA_SUCCESS) {
+        std::lock_guard<std::mutex> lock(mu);
+        Entry& e = cache[next];
+        next = (next + 1) % 8;
+        e.used = true;
+        e.base = base;
+        memcpy(e.key, key, sizeof(key));
+        e.map = *map;
+    }
+    return r;
 }
 
 // Generic 5-D tiled tensor map with 128-byte swizzle (16-bit elements).

@@ -37,9 +37,17 @@ def _p(t: Optional[torch.Tensor]):
     return None if t is None else t.data_ptr()
 
 
-def _stream(stream) -> int:
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream(stream, device_index: Optional[int] = None) -> int:
+    """The cudaStream_t to launch on: `stream`, or torch's current stream of
+    `device_index` (the current device when None).  The current stream is
+    read as a raw handle, without building a torch.cuda.Stream per call."""
     if stream is None:
-        return torch.cuda.current_stream().cuda_stream
+        if _raw_stream is not None:
+            return _raw_stream(torch.cuda.current_device() if device_index is None else device_index)
+        return torch.cuda.current_stream(device_index).cuda_stream
     if isinstance(stream, torch.cuda.Stream):
         return stream.cuda_stream
     return int(stream)
@@ -255,11 +263,12 @@ def _decode_args(q, k_cache, v_cache, block_table, seq_lens, clear_start, fog_al
     _need_cuda(q, k_cache, v_cache, block_table, seq_lens)
     B, Hq, D = q.shape
     P, ps, Hkv, Dk = k_cache.shape
-    if Dk != D or v_cache.shape != k_cache.shape or v_cache.stride() != k_cache.stride():
+    ks, qs = k_cache.stride(), q.stride()
+    if Dk != D or v_cache.shape != k_cache.shape or v_cache.stride() != ks:
         raise ValueError("k_cache/v_cache must be matching [P, ps, Hkv, D] views")
     if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
         raise TypeError("q and the cache must share a dtype")
-    if q.stride(2) != 1 or k_cache.stride(3) != 1:
+    if qs[2] != 1 or ks[3] != 1:
         raise ValueError("head_dim must be contiguous")
     bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
     if bt.stride(1) != 1:
@@ -284,8 +293,8 @@ def _decode_args(q, k_cache, v_cache, block_table, seq_lens, clear_start, fog_al
         ws = workspace(need, q.device, tag)
     # keep the converted tensors alive until the launch
     keep = (bt, sl, cs, off, qp, fw)
-    args = (q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
-            k_cache.stride(1), k_cache.stride(2), P, ps, bt.data_ptr(), bt.stride(0), sl.data_ptr(), _p(off), _p(qp),
+    args = (q.data_ptr(), qs[0], qs[1], k_cache.data_ptr(), v_cache.data_ptr(), ks[0],
+            ks[1], ks[2], P, ps, bt.data_ptr(), bt.stride(0), sl.data_ptr(), _p(off), _p(qp),
             _p(cs), float(fog_alpha), _p(fw), int(window_size), float(sm_scale), B, Hq, Hkv, D, int(max_seq_len),
             dtype_code(q))
     return lib, args, ws, keep
@@ -314,7 +323,8 @@ def paged_fog_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                    "paged_fog_decode")
         return out
     _lib.check(lib.kessie_paged_fog_decode_ex_v2(*args, _p(out if want_out else None), _p(out_partial), ws.data_ptr(),
-                                                 ws.numel(), int(phases), _stream(stream)), "paged_fog_decode")
+                                                 ws.numel(), int(phases), _stream(stream, q.device.index)),
+               "paged_fog_decode")
     return out
 
 
@@ -397,7 +407,7 @@ def paged_fog_decode_cp(exchange: "CpExchange", epoch: int, q: torch.Tensor, k_c
                                        fog_weights, window_size, sm_scale, kv_pos_offset, q_positions, max_seq_len, ws)
     _lib.check(lib.kessie_paged_fog_decode_cp_v2(
         *args, exchange.ptrs, exchange.rank, exchange.world, int(epoch), int(wait_timeout_s * 1e9), _p(out),
-        _p(out_partial), ws.data_ptr(), ws.numel(), int(phases), _stream(stream)), "paged_fog_decode_cp")
+        _p(out_partial), ws.data_ptr(), ws.numel(), int(phases), _stream(stream, q.device.index)), "paged_fog_decode_cp")
     return out
 
 
