@@ -28,8 +28,9 @@
  *     reads and clears it.
  *   - Strides are in ELEMENTS; head_dim is always the contiguous dimension.
  *   - The library caches, per device, the addresses of its own device
- *     variables (the status word, the allocation-free decode's scratch): do
- *     not use it on a device after cudaDeviceReset of that device.
+ *     variables (the status word, the allocation-free decode's scratch) and
+ *     launch settings (kernels' shared-memory limits, occupancy): do not use
+ *     it on a device after cudaDeviceReset of that device.
  *   - Positions are int32; page tables are int32; page_valid is int8.
  */
 #ifndef KESSIE_CAPI_H
