@@ -878,6 +878,11 @@ __global__ void __launch_bounds__(128) cp_combine_kernel(const CpCombineParams a
         for (int e = 0; e < E; e += 2) *reinterpret_cast<float2*>(dst + lane * E + e) = make_float2(o[e], o[e + 1]);
         if (lane == 0) *reinterpret_cast<float2*>(dst + D) = make_float2(M == -INFINITY ? -INFINITY : M * kLn2, L);
     }
+    // The combine never signals its own dependents, so whatever follows on
+    // the stream starts after it completes; one thread waiting here for the
+    // decode grid makes that completion imply the decode's too (the library's
+    // programmatic launches rely on it when they read ahead of their wait).
+    if (blockIdx.x == 0 && threadIdx.x == 0) ptx::grid_dependency_wait();
 }
 
 // Merge S partial triples (natural-log m) per row; blockDim = D.
