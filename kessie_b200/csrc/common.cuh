@@ -36,9 +36,20 @@ int sm_count();
 // programmatic launch it made there; a launch that is not programmatic
 // (library or not) serialises fully and needs no record.
 struct ByteRange { uintptr_t lo, hi; };
+// Holds the registry locked from a claim until the launch it decided has
+// been issued, so the record follows the stream's real launch order when
+// several host threads launch on one stream.
+class LaunchOrderGuard {
+  public:
+    LaunchOrderGuard();
+    ~LaunchOrderGuard();
+    LaunchOrderGuard(const LaunchOrderGuard&) = delete;
+    LaunchOrderGuard& operator=(const LaunchOrderGuard&) = delete;
+};
 // Records `writes` as the last programmatic launch on (current device,
 // `stream`) and returns true when none of the previous record's ranges
-// overlaps any of `reads` (an empty range overlaps nothing).
+// overlaps any of `reads` (an empty range overlaps nothing).  The caller
+// holds a LaunchOrderGuard from before this call until its launch is issued.
 bool claim_early_reads(cudaStream_t stream, const ByteRange* reads, int nreads, const ByteRange* writes,
                        int nwrites);
 

@@ -272,6 +272,7 @@ int launch_gather_bulk(BulkArgs a, cudaStream_t st) {
         return 0;
     }
     const int grid = std::min(a.units, sm_count());
+    LaunchOrderGuard order;                  // held until the launch below is issued
     // early reads: the cache rows and page ids this gather reads against the
     // bytes the preceding programmatic launch on the stream wrote
     {
@@ -756,6 +757,7 @@ int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int
         size_t smem = rope_tokens_smem(tpb_t, H, half, (int)sizeof(T), false);
         auto kern = hpt == 2 ? rope_tokens_kernel<T, false, 2> : rope_tokens_kernel<T, false, 1>;
         const int64_t es = sizeof(T);
+        LaunchOrderGuard order;              // held until the launch below is issued
         const ByteRange krows = span_bytes(k, ((int64_t)(T_ - 1) * ts + (int64_t)(H - 1) * hs + D) * es);
         const ByteRange reads[3] = {krows, span_bytes(orig, (int64_t)T_ * 4), span_bytes(tgt, tgt ? (int64_t)T_ * 4 : 0)};
         const int early = claim_early_reads(st, reads, 3, &krows, 1) && ts >= 0 && hs >= 0 ? 1 : 0;
@@ -1144,6 +1146,7 @@ int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv
         auto kern = hpt == 2 ? rope_tokens_kernel<T, true, 2> : rope_tokens_kernel<T, true, 1>;
         // destination rows of all heads contiguous: K and V rows leave as bulk copies
         const int bulk_st = (g.head_stride == g.head_dim && ((int64_t)g.num_heads * g.head_dim * es) % 16 == 0) ? 1 : 0;
+        LaunchOrderGuard order;              // held until the launch below is issued
         const int64_t rows_e = (int64_t)(T_ - 1) * sts + (int64_t)(g.num_heads - 1) * shs + g.head_dim;
         const ByteRange reads[5] = {span_bytes(nk, rows_e * es), span_bytes(nv, rows_e * es),
                                     span_bytes(ids, (int64_t)pages * 4), span_bytes(orig, (int64_t)T_ * 4),

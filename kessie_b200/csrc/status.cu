@@ -88,6 +88,9 @@ std::map<std::pair<int, uintptr_t>, LaunchWrites> g_last_pdl;
 bool overlaps(const ByteRange& a, const ByteRange& b) { return a.lo < a.hi && b.lo < b.hi && a.lo < b.hi && b.lo < a.hi; }
 }  // namespace
 
+LaunchOrderGuard::LaunchOrderGuard() { g_pdl_mu.lock(); }
+LaunchOrderGuard::~LaunchOrderGuard() { g_pdl_mu.unlock(); }
+
 bool claim_early_reads(cudaStream_t stream, const ByteRange* reads, int nreads, const ByteRange* writes,
                        int nwrites) {
     int dev = 0;
@@ -99,7 +102,6 @@ bool claim_early_reads(cudaStream_t stream, const ByteRange* reads, int nreads, 
     w.n = nwrites < kMaxWrites ? nwrites : kMaxWrites;
     for (int i = 0; i < w.n; ++i) w.r[i] = writes[i];
     bool early = nwrites <= kMaxWrites;
-    std::lock_guard<std::mutex> lk(g_pdl_mu);
     const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
     auto it = g_last_pdl.find(key);
     if (it != g_last_pdl.end())

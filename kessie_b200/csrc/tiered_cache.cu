@@ -244,6 +244,7 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
     const long long rows = (v_fog ? S : T) + T;
     if (rows == 0) { clear_error(); return 0; }
     cudaStream_t st = as_stream(stream);
+    LaunchOrderGuard order;                  // held until the launch below is issued
     {
         const uintptr_t store_bytes = (uintptr_t)((long long)B * H * cap * a.chunks * 16);
         const uintptr_t kb = reinterpret_cast<uintptr_t>(k_store), vb = reinterpret_cast<uintptr_t>(v_store);
