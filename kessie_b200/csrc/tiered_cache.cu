@@ -70,7 +70,13 @@ struct TieredUpdateArgs {
     int early;                    // issue the live-V loads before griddepcontrol.wait
 };
 
-constexpr int kItems = 4;                                  // 16-byte items in flight per thread
+constexpr int kItems = 4;                                  // 16-byte items in flight per thread (pack)
+// The update keeps 8 in flight per thread: a layer's grid (392 CTAs at the
+// decode-step shape, 3 per SM at 79 registers) then leaves SM slots for the
+// next layer's CTAs to start their early reads while this one drains
+// (4 items: 776 CTAs filled the 740 slots, 0.73 of HBM; 8: 0.78; 12 / 16
+// drop to 2 CTAs per SM, 0.62 / 0.57).
+constexpr int kUpdItems = 8;
 
 // grid (x over the rows of one (b, h), y = b * H + h): rows [0, S) are the
 // fogged V (or [0, T) the V append when the fog is off), then T K-append rows.
@@ -103,11 +109,11 @@ __global__ void __launch_bounds__(256) tiered_update_kernel(TieredUpdateArgs a) 
         ptx::grid_dependency_wait();
         ptx::launch_dependents();
     }
-    for (int base = blockIdx.x * 256 * kItems + threadIdx.x; base < items; base += gridDim.x * 256 * kItems) {
-        uint4 raw[kItems];
-        const char* src[kItems];
+    for (int base = blockIdx.x * 256 * kUpdItems + threadIdx.x; base < items; base += gridDim.x * 256 * kUpdItems) {
+        uint4 raw[kUpdItems];
+        const char* src[kUpdItems];
 #pragma unroll
-        for (int u = 0; u < kItems; ++u) {
+        for (int u = 0; u < kUpdItems; ++u) {
             const int i = base + u * 256;
             src[u] = nullptr;
             if (i >= items) break;
@@ -127,7 +133,7 @@ __global__ void __launch_bounds__(256) tiered_update_kernel(TieredUpdateArgs a) 
             ptx::launch_dependents();
             waited = true;
 #pragma unroll
-            for (int u = 0; u < kItems; ++u) {
+            for (int u = 0; u < kUpdItems; ++u) {
                 const int i = base + u * 256;
                 if (i >= items) break;
                 const int r = i / chunks;
@@ -135,7 +141,7 @@ __global__ void __launch_bounds__(256) tiered_update_kernel(TieredUpdateArgs a) 
             }
         }
 #pragma unroll
-        for (int u = 0; u < kItems; ++u) {
+        for (int u = 0; u < kUpdItems; ++u) {
             const int i = base + u * 256;
             if (i >= items) break;
             const int r = i / chunks, c = i - r * chunks;
@@ -186,10 +192,11 @@ __global__ void __launch_bounds__(256) strided_pack_kernel(const unsigned long l
     }
 }
 
-// x blocks for `items` per y row: enough CTAs in total for the SMs, at most
-// one item batch per thread when that fits.
-int grid_x(long long items, long long rows_y) {
-    const long long per = 256LL * kItems;
+// x blocks for `items` per y row (`per_thread` 16-byte items per thread and
+// batch): enough CTAs in total for the SMs, at most one item batch per thread
+// when that fits.
+int grid_x(long long items, long long rows_y, int per_thread) {
+    const long long per = 256LL * per_thread;
     long long gx = (items + per - 1) / per;
     const long long cap = ((long long)sm_count() * 16 + rows_y - 1) / rows_y;
     if (gx > cap) gx = cap;
@@ -254,7 +261,7 @@ extern "C" int kessie_tiered_update_v2(void* k_store, void* v_store, long long c
                                       : ByteRange{0, 0}};
         a.early = claim_early_reads(st, &w[1], 1, w, 3) && v_fog != nullptr ? 1 : 0;
     }
-    const dim3 grid(grid_x(rows * a.chunks, (long long)B * H), B * H);
+    const dim3 grid(grid_x(rows * a.chunks, (long long)B * H, kUpdItems), B * H);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -298,7 +305,7 @@ extern "C" int kessie_strided_pack_v2(const unsigned long long* store_bases, con
         return set_error(KESSIE_ERR_ARG, "strided_pack_v2: stores * rows <= 65535, tokens * row chunks < 2^30");
     if (tokens == 0) { clear_error(); return 0; }
     const int ch = row_bytes / 16, ys = num_stores * rows_per_store;
-    const dim3 grid(grid_x(tokens * ch, ys), ys);
+    const dim3 grid(grid_x(tokens * ch, ys, kItems), ys);
     cudaStream_t st = as_stream(stream);
     if (ch == 16)
         strided_pack_kernel<16><<<grid, 256, 0, st>>>(store_bases, store_pitch_bytes, rows_per_store, (int)tokens, ch,
