@@ -373,35 +373,28 @@ def run_cp_decode(args):
     time.sleep(0.15)
     if world > 1:
         dist.barrier()
-    # At N = 1 a step is one decode launch, so an event at every step boundary
-    # inside the timed loop gives the kernel's own duration at no cost.  At
-    # N > 1 an event between the decode and its programmatic-dependent combine
-    # would stop their overlap, so the timed loop has none and the decode is
+    # An event between two launches would stop the next one from starting
+    # while the previous one finishes (each decode may read its pages ahead of
+    # the previous step's tail; at N > 1 the combine is a programmatic
+    # dependent of the decode), so the timed loop has none, and the decode is
     # timed alone in a loop of the same step right after it.
-    step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)] if world == 1 else None
     torch.cuda.synchronize()
     t_start.record()
     for i in range(K):
-        if step_ev is not None:
-            step_ev[i].record()
         step()
-    if step_ev is not None:
-        step_ev[K].record()
     t_end.record()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    if step_ev is None:
-        Kk = max(10, K // 2)
-        ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
-        ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
-        for i in range(Kk):
-            step_split(ev_a, ev_b, i)
-        torch.cuda.synchronize()
+    Kk = max(10, K // 2)
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
+    for i in range(Kk):
+        step_split(ev_a, ev_b, i)
+    torch.cuda.synchronize()
+    if world > 1:
         dist.barrier()
-        kern_ms = sum(ev_a[i].elapsed_time(ev_b[i]) for i in range(Kk)) / Kk
-    else:
-        kern_ms = sum(step_ev[i].elapsed_time(step_ev[i + 1]) for i in range(K)) / K
+    kern_ms = sum(ev_a[i].elapsed_time(ev_b[i]) for i in range(Kk)) / Kk
     clocks.stop()
     el_ms = t_start.elapsed_time(t_end)
     t = torch.tensor([el_ms, kern_ms], dtype=torch.float64, device=dev)

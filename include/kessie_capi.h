@@ -226,7 +226,14 @@ int kessie_build_fog_weights_v2(float* out, int seq_len, int clear_start, float 
  *   f32 (q, caches and out all fp32) runs every product in fp32 on the CUDA
  *   cores, for the reference's fp32 path at its 1e-4 bar; the additive-bias
  *   and context-parallel forms below take f16 / bf16 only.
- * workspace: kessie_paged_fog_decode_workspace_size(...) bytes. */
+ * workspace: kessie_paged_fog_decode_workspace_size(...) bytes.
+ * f16 / bf16 decodes are programmatic dependent launches: when the last such
+ * launch of this library on the same (device, stream) wrote none of q, the
+ * caches, the block table or the length arrays (and no fog weights or bias
+ * are passed), the q and page loads may start before the previous kernel on
+ * the stream completes; everything is written only after it completes.  A
+ * kernel that writes those inputs must not be launched with a programmatic
+ * dependency that triggers before its writes. */
 size_t kessie_paged_fog_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
                                               int head_dim, int max_seq_len, int page_size);
 int kessie_paged_fog_decode_v2(const void* q, int64_t q_stride_b, int64_t q_stride_h,
@@ -487,7 +494,10 @@ int kessie_strided_pack_v2(const unsigned long long* store_bases, const long lon
  *     then KESSIE_DEV_WAIT_TIMEOUT in the device status word and zero rows)
  *     and writes out [B, Hq, D] and/or out_partial [B, Hq, D+2] (same triple
  *     as kessie_paged_fog_decode_v2).  With both bits the combine is a
- *     programmatic dependent launch of the decode.
+ *     programmatic dependent launch of the decode.  The combine lets the
+ *     next launch on the stream start at once (the next step's decode then
+ *     reads ahead while this step finishes; the library keeps the decode's
+ *     and the combine's written ranges for that decision).
  * All ranks call it with the same shapes and the same epoch; epoch starts at
  * 1 and goes up by one per step (consecutive steps alternate between two
  * slots of the buffer, so keep the parity alternating across any wrap).

@@ -50,8 +50,25 @@ class LaunchOrderGuard {
 // `stream`) and returns true when none of the previous record's ranges
 // overlaps any of `reads` (an empty range overlaps nothing).  The caller
 // holds a LaunchOrderGuard from before this call until its launch is issued.
+//
+// Every launch of this library signals its dependents only after its own
+// griddepcontrol.wait, except the context-parallel combine, which signals at
+// its start (so the next step's decode overlaps this step's tail) and waits
+// for the decode at its end.  Such a launch passes `merge` (its record keeps
+// the previous record's writes: that launch may still run when the next one
+// starts) and `delay_ns`, a bound on how long its dependents can sit in
+// griddepcontrol.wait after it signalled (its cross-rank wait).  A caller
+// that gives no `prev_delay_ns` gets false after such a launch, since its
+// bounded waits do not cover that delay; one that does gets the delay, to add
+// to every bounded wait that may sit behind another thread's
+// griddepcontrol.wait.
 bool claim_early_reads(cudaStream_t stream, const ByteRange* reads, int nreads, const ByteRange* writes,
-                       int nwrites);
+                       int nwrites, uint64_t* prev_delay_ns = nullptr, uint64_t delay_ns = 0, bool merge = false);
+// [p, p + bytes) as a byte range (empty for a null pointer or no bytes).
+inline ByteRange byte_span(const void* p, int64_t bytes) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+    return (p && bytes > 0) ? ByteRange{b, b + (uintptr_t)bytes} : ByteRange{0, 0};
+}
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -70,6 +70,7 @@ namespace kessie {
 namespace {
 
 constexpr int kNCW = 4;          // consumer warps
+constexpr uint64_t kSpinNs = 2000000000ull;   // bound of an mbarrier wait with nothing ahead of it
 constexpr int kNST = 3;          // pipeline stages
 constexpr int kIdWin = 128;      // page ids per prefetch window (units)
 constexpr int kHelperWarp = kNCW + 1;  // finishes mid-range segment ends for the consumers
@@ -102,6 +103,10 @@ struct DecodeParams {
     CpLink cp;            // cp.world > 0: push merged rows into every rank's exchange buffer
     FogBias bias;         // additive fog bias on the scores (vLLM path), bias.on == 0: none
     int* status;
+    int early;            // read ahead of griddepcontrol.wait (every global store still follows it)
+    uint64_t spin_ns;     // bound of each mbarrier wait (longer when early: see run_decode)
+    const void* ws_base;  // host side: the workspace's byte range, for the launch registry
+    size_t ws_bytes;
 };
 
 // Visible local key range of one sequence.
@@ -337,6 +342,17 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
     float* stg = reinterpret_cast<float*>(smem + S::kStgOff);
     int* ctl = reinterpret_cast<int*>(smem + S::kCtlOff);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Programmatic dependent launch.  Without p.early every thread waits here
+    // for the preceding grid.  With it (the host found that the preceding
+    // programmatic launches wrote none of q, the cache, the tables or the
+    // lengths) the range search, page ids, TMA loads and the math run ahead,
+    // and each thread waits before its first global store: the consumers at
+    // their final segment (mid-range ends only stage into shared memory) or
+    // before emitting an empty group, the helper before its first partial.
+    // While one warp sits in that wait another may wait on it through an
+    // mbarrier, so those waits are bounded by p.spin_ns, which covers how long
+    // the preceding grid can still run.
+    if (!p.early) ptx::grid_dependency_wait();
 
     // ---------------------------------------------------------------- range of this CTA
     if (threadIdx.x == 0) {
@@ -439,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
                 }
                 const int s = itg % kNST;
                 bool ok = true;
-                if (lane == 0 && itg >= kNST) ok = ptx::mbar_wait(&empty[s], ((uint32_t)(itg / kNST) & 1u) ^ 1u);
+                if (lane == 0 && itg >= kNST) ok = ptx::mbar_wait(&empty[s], ((uint32_t)(itg / kNST) & 1u) ^ 1u, p.spin_ns);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) {
                     if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
@@ -465,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
         // drain: every issued load has landed before this warp exits
         if (lane == 0) {
             for (int it = max(0, itg - kNST); it < itg; ++it) {
-                if (!ptx::mbar_wait(&full[it % kNST], (uint32_t)(it / kNST) & 1u)) {
+                if (!ptx::mbar_wait(&full[it % kNST], (uint32_t)(it / kNST) & 1u, p.spin_ns)) {
                     record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
                     break;
                 }
@@ -482,11 +498,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
     // arrival and, if it was the group's last, merges the group alone.
     // Under a saturated memory system the fence alone took several us.
     if (warp == kHelperWarp) {
+        bool waited = !p.early;
         for (int job = 0;; ++job) {
             // lane 0 waits (the warp may idle for most of the launch); the
             // warp barrier orders the other lanes' reads after it
             bool ok = true;
-            if (lane == 0) ok = ptx::mbar_wait(job_full, (uint32_t)job & 1u);
+            if (lane == 0) ok = ptx::mbar_wait(job_full, (uint32_t)job & 1u, p.spin_ns);
             __syncwarp();
             if (!__shfl_sync(0xffffffffu, ok, 0)) {
                 if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
@@ -494,6 +511,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
             }
             const int slot = ctl[8], g = ctl[9], first = ctl[10], K = ctl[11];
             if (slot < 0) break;                                    // no more segments
+            if (!waited) {
+                ptx::grid_dependency_wait();
+                waited = true;
+            }
             const int G = p.G;
             float4* po = reinterpret_cast<float4*>(p.part_o + (size_t)slot * G * D);
             const float4* so = reinterpret_cast<const float4*>(stg);
@@ -518,8 +539,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
     // ---------------------------------------------------------------- consumers
     // Groups with no visible key anywhere in this shard still produce rows
     // (zeros; m = -inf, l = 0); CTA g % grid emits them.
+    bool waited = !p.early;
     for (int g = blockIdx.x; g < p.B * p.Hkv; g += gridDim.x) {
         if (seq_info(p, g / p.Hkv).n == 0) {
+            if (!waited) {
+                ptx::grid_dependency_wait();
+                waited = true;
+            }
             merge_and_emit<D, BF16>(p, g, 0, 0, warp, lane);
         }
     }
@@ -568,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
         for (int it = 0; it < n_iter; ++it, ++itg) {
             const int s = itg % kNST;
             if (!broken) {
-                const bool ok = ptx::mbar_wait(&full[s], (uint32_t)(itg / kNST) & 1u);
+                const bool ok = ptx::mbar_wait(&full[s], (uint32_t)(itg / kNST) & 1u, p.spin_ns);
                 if (!__all_sync(0xffffffffu, ok)) {
                     if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
                     broken = true;
@@ -721,6 +747,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
                 }
             }
         };
+        if (!waited && walk.pos >= walk.end) {              // the final segment's stores follow the wait
+            ptx::grid_dependency_wait();
+            waited = true;
+        }
         consumers_sync();                                   // region free from the previous segment
         if (warp >= 2) put(mrg + (warp - 2) * S::kMrgFloats);
         consumers_sync();
@@ -737,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
             // a mid-range segment goes to the helper: wait until it has
             // released the staging (bounded), stage, hand over
             if (!final_seg && njobs > 0 &&
-                !__all_sync(0xffffffffu, ptx::mbar_wait(job_empty, (uint32_t)(njobs - 1) & 1u))) {
+                !__all_sync(0xffffffffu, ptx::mbar_wait(job_empty, (uint32_t)(njobs - 1) & 1u, p.spin_ns))) {
                 if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
             }
 #pragma unroll
@@ -783,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
     }
     // the helper stops once it has finished the last segment handed to it
     if (warp == 0) {
-        if (njobs > 0 && !__all_sync(0xffffffffu, ptx::mbar_wait(job_empty, (uint32_t)(njobs - 1) & 1u))) {
+        if (njobs > 0 && !__all_sync(0xffffffffu, ptx::mbar_wait(job_empty, (uint32_t)(njobs - 1) & 1u, p.spin_ns))) {
             if (lane == 0) record_status(p.status, KESSIE_DEV_WAIT_TIMEOUT);
         }
         if (lane == 0) {
@@ -791,6 +821,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1) fog_decode_kernel(c
             ptx::mbar_arrive(job_full);
         }
     }
+    // a CTA with nothing to store still ends after the preceding grid, so
+    // that this grid's completion (or signal) implies that grid's completion
+    if (!waited) ptx::grid_dependency_wait();
 }
 
 // Context-parallel combine: one warp per output row (4 rows per CTA), reading
@@ -814,6 +847,10 @@ __global__ void __launch_bounds__(128) cp_combine_kernel(const CpCombineParams a
     constexpr int E = D / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 4 + warp;
+    // The next step's decode may start now, while this step's decode CTAs
+    // finish: its stores follow its own wait for this grid, whose block 0
+    // waits for the decode at the end.
+    ptx::launch_dependents();
     if (row >= a.lay.rows) return;
     const int par = par_of(a.epoch);
     const int world = a.lay.world;
@@ -878,10 +915,9 @@ __global__ void __launch_bounds__(128) cp_combine_kernel(const CpCombineParams a
         for (int e = 0; e < E; e += 2) *reinterpret_cast<float2*>(dst + lane * E + e) = make_float2(o[e], o[e + 1]);
         if (lane == 0) *reinterpret_cast<float2*>(dst + D) = make_float2(M == -INFINITY ? -INFINITY : M * kLn2, L);
     }
-    // The combine never signals its own dependents, so whatever follows on
-    // the stream starts after it completes; one thread waiting here for the
-    // decode grid makes that completion imply the decode's too (the library's
-    // programmatic launches rely on it when they read ahead of their wait).
+    // One thread waiting here for the decode grid makes this grid's completion
+    // imply the decode's: a dependent's griddepcontrol.wait (before any of
+    // its stores) then orders it after both.
     if (blockIdx.x == 0 && threadIdx.x == 0) ptx::grid_dependency_wait();
 }
 
@@ -953,8 +989,21 @@ int launch_decode_t(const CUtensorMap& mk, const CUtensorMap& mv, const DecodePa
         if (occ > kCtasPerSm) occ = kCtasPerSm;
         if (dev < 64) occ_cache[dev] = occ;
     }
-    dim3 grid(occ * sm_count());
-    kern<<<grid, kThreads, smem, st>>>(mk, mv, p);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(occ * sm_count());
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mk, mv, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(KESSIE_ERR_CUDA, "paged_fog_decode: %s", cudaGetErrorString(e));
+    }
     return check_launch("paged_fog_decode");
 }
 
@@ -1031,6 +1080,9 @@ int prepare_decode(DecodeParams& p, Plan& pl, const void* q, int64_t q_stride_b,
     p.part_ml = reinterpret_cast<float*>(ws + pl.ml_off);
     p.part_o = reinterpret_cast<float*>(ws + pl.o_off);
     p.status = device_status_ptr();
+    p.spin_ns = kSpinNs;
+    p.ws_base = workspace;
+    p.ws_bytes = pl.ws;
     (void)k_cache; (void)v_cache; (void)page_stride; (void)token_stride; (void)head_stride;
     return 0;
 }
@@ -1044,13 +1096,42 @@ int run_decode(const DecodeParams& p, const void* k_cache, const void* v_cache, 
                                      head_stride, page_stride);
     if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: TMA descriptor rejected (%d/%d)", (int)r1, (int)r2);
+    // Early reads when the preceding programmatic launches on the stream wrote
+    // none of the inputs (fog weights or a bias: extents unknown here, no).
+    // After a launch that signals before its own wait (the context-parallel
+    // combine) the preceding grid can run for up to its delay bound while
+    // this one's warps wait in griddepcontrol.wait: the mbarrier waits get
+    // that much longer.
+    LaunchOrderGuard order;                  // held until the launch below is issued
+    DecodeParams pe = p;
+    {
+        const int ps = p.units_per_page * 16;
+        const int64_t kv_e = (int64_t)(p.num_pages - 1) * page_stride + (int64_t)(ps - 1) * token_stride +
+                             (int64_t)(p.Hkv - 1) * head_stride + head_dim;
+        const int64_t q_e = (int64_t)(p.B - 1) * p.q_sb + (int64_t)(p.Hq - 1) * p.q_sh + head_dim;
+        const int64_t nb = (int64_t)p.B * 4;
+        const ByteRange reads[8] = {byte_span(p.q, q_e * 2), byte_span(k_cache, kv_e * 2), byte_span(v_cache, kv_e * 2),
+                                    byte_span(p.block_table, (int64_t)p.B * p.bt_stride * 4),
+                                    byte_span(p.seq_lens, nb), byte_span(p.kv_off, nb), byte_span(p.q_pos, nb),
+                                    byte_span(p.clear_start, nb)};
+        const CpLayout lay{p.cp.world, p.B * p.Hq, head_dim};
+        const ByteRange writes[4] = {byte_span(p.out, (int64_t)p.B * p.Hq * head_dim * 2),
+                                     byte_span(p.out_part, (int64_t)p.B * p.Hq * (head_dim + 2) * 4),
+                                     byte_span(p.ws_base, (int64_t)p.ws_bytes),
+                                     byte_span(p.cp.world > 0 ? p.cp.peer[p.cp.rank] : nullptr, (int64_t)lay.bytes())};
+        const bool fwd = page_stride >= 0 && token_stride >= 0 && head_stride >= 0 && p.q_sb >= 0 && p.q_sh >= 0;
+        uint64_t prev_delay = 0;
+        const bool ok = claim_early_reads(st, reads, 8, writes, 4, &prev_delay);
+        pe.early = ok && fwd && !p.fog_w && !p.bias.on ? 1 : 0;
+        if (pe.early) pe.spin_ns = kSpinNs + prev_delay < kSpinNs ? ~uint64_t(0) : kSpinNs + prev_delay;
+    }
     const bool nt2 = p.G > 8;
     if (head_dim == 128) {
-        if (bf16) return nt2 ? launch_decode_t<128, true, 2>(mk, mv, p, st) : launch_decode_t<128, true, 1>(mk, mv, p, st);
-        return nt2 ? launch_decode_t<128, false, 2>(mk, mv, p, st) : launch_decode_t<128, false, 1>(mk, mv, p, st);
+        if (bf16) return nt2 ? launch_decode_t<128, true, 2>(mk, mv, pe, st) : launch_decode_t<128, true, 1>(mk, mv, pe, st);
+        return nt2 ? launch_decode_t<128, false, 2>(mk, mv, pe, st) : launch_decode_t<128, false, 1>(mk, mv, pe, st);
     }
-    if (bf16) return nt2 ? launch_decode_t<64, true, 2>(mk, mv, p, st) : launch_decode_t<64, true, 1>(mk, mv, p, st);
-    return nt2 ? launch_decode_t<64, false, 2>(mk, mv, p, st) : launch_decode_t<64, false, 1>(mk, mv, p, st);
+    if (bf16) return nt2 ? launch_decode_t<64, true, 2>(mk, mv, pe, st) : launch_decode_t<64, true, 1>(mk, mv, pe, st);
+    return nt2 ? launch_decode_t<64, false, 2>(mk, mv, pe, st) : launch_decode_t<64, false, 1>(mk, mv, pe, st);
 }
 
 }  // namespace
@@ -1190,6 +1271,15 @@ int cp_combine(void* const* exchange_buffers, int rank, int world, uint32_t epoc
     const bool bf16 = dtype == KESSIE_DTYPE_BF16;
     cudaStream_t st = as_stream(stream);
     const bool pdl = follows_decode;
+    // The combine signals its dependents at its start, before its wait for
+    // the decode: its record keeps the decode's writes, and its dependents may
+    // sit in griddepcontrol.wait for its cross-rank wait (plus the decode's
+    // tail, bounded by the decode's own waits).
+    LaunchOrderGuard order;
+    const int64_t rows = (int64_t)batch * num_q_heads;
+    const ByteRange writes[2] = {byte_span(out, rows * head_dim * 2), byte_span(out_partial, rows * (head_dim + 2) * 4)};
+    uint64_t prev_delay = 0;
+    claim_early_reads(st, nullptr, 0, writes, 2, &prev_delay, (uint64_t)wait_timeout_ns + kSpinNs, true);
     if (head_dim == 128) return bf16 ? launch_cp_combine_t<128, true>(a, st, pdl) : launch_cp_combine_t<128, false>(a, st, pdl);
     return bf16 ? launch_cp_combine_t<64, true>(a, st, pdl) : launch_cp_combine_t<64, false>(a, st, pdl);
 }

@@ -306,11 +306,6 @@ int launch_gather_bulk(BulkArgs a, cudaStream_t st) {
 
 bool bulk_ok(int64_t bytes) { return bytes % 16 == 0; }
 
-// [p, p + bytes) as a byte range (empty for a null pointer or no bytes).
-ByteRange span_bytes(const void* p, int64_t bytes) {
-    const uintptr_t b = reinterpret_cast<uintptr_t>(p);
-    return (p && bytes > 0) ? ByteRange{b, b + (uintptr_t)bytes} : ByteRange{0, 0};
-}
 
 // Launch as a programmatic dependent of the preceding kernel on the stream.
 template <typename... Params, typename... Args>
@@ -758,8 +753,8 @@ int launch_rope(void* k, int T_, int H, int D, int64_t ts, int64_t hs, const int
         auto kern = hpt == 2 ? rope_tokens_kernel<T, false, 2> : rope_tokens_kernel<T, false, 1>;
         const int64_t es = sizeof(T);
         LaunchOrderGuard order;              // held until the launch below is issued
-        const ByteRange krows = span_bytes(k, ((int64_t)(T_ - 1) * ts + (int64_t)(H - 1) * hs + D) * es);
-        const ByteRange reads[3] = {krows, span_bytes(orig, (int64_t)T_ * 4), span_bytes(tgt, tgt ? (int64_t)T_ * 4 : 0)};
+        const ByteRange krows = byte_span(k, ((int64_t)(T_ - 1) * ts + (int64_t)(H - 1) * hs + D) * es);
+        const ByteRange reads[3] = {krows, byte_span(orig, (int64_t)T_ * 4), byte_span(tgt, tgt ? (int64_t)T_ * 4 : 0)};
         const int early = claim_early_reads(st, reads, 3, &krows, 1) && ts >= 0 && hs >= 0 ? 1 : 0;
         if (launch_pdl(kern, dim3((T_ + tpb_t - 1) / tpb_t), dim3(256), smem, st, (T*)k, (const T*)k,
                        (const T*)nullptr, T_, H, half, ts, hs, ts, hs, (int64_t)0, (int64_t)0, 1,
@@ -1148,13 +1143,13 @@ int launch_insert(void* cache, const PageGeom& g, const void* nk, const void* nv
         const int bulk_st = (g.head_stride == g.head_dim && ((int64_t)g.num_heads * g.head_dim * es) % 16 == 0) ? 1 : 0;
         LaunchOrderGuard order;              // held until the launch below is issued
         const int64_t rows_e = (int64_t)(T_ - 1) * sts + (int64_t)(g.num_heads - 1) * shs + g.head_dim;
-        const ByteRange reads[5] = {span_bytes(nk, rows_e * es), span_bytes(nv, rows_e * es),
-                                    span_bytes(ids, (int64_t)pages * 4), span_bytes(orig, (int64_t)T_ * 4),
-                                    span_bytes(tgt, tgt ? (int64_t)T_ * 4 : 0)};
+        const ByteRange reads[5] = {byte_span(nk, rows_e * es), byte_span(nv, rows_e * es),
+                                    byte_span(ids, (int64_t)pages * 4), byte_span(orig, (int64_t)T_ * 4),
+                                    byte_span(tgt, tgt ? (int64_t)T_ * 4 : 0)};
         const int64_t cache_e = (int64_t)(g.max_pages - 1) * g.page_stride + (int64_t)(g.page_size - 1) * g.token_stride +
                                 g.kv_stride + (int64_t)(g.num_heads - 1) * g.head_stride + g.head_dim;
-        const ByteRange writes[3] = {span_bytes(cache, cache_e * es), span_bytes(valid, valid ? g.max_pages : 0),
-                                     span_bytes(positions, positions ? (int64_t)g.max_pages * 4 : 0)};
+        const ByteRange writes[3] = {byte_span(cache, cache_e * es), byte_span(valid, valid ? g.max_pages : 0),
+                                     byte_span(positions, positions ? (int64_t)g.max_pages * 4 : 0)};
         const bool fwd = sts >= 0 && shs >= 0 && g.page_stride >= 0 && g.token_stride >= 0 && g.kv_stride >= 0 &&
                          g.head_stride >= 0;
         const int early = claim_early_reads(st, reads, 5, writes, 3) && fwd ? 1 : 0;

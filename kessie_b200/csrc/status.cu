@@ -81,8 +81,8 @@ int sm_count() {
 }
 
 namespace {
-constexpr int kMaxWrites = 4;
-struct LaunchWrites { int n; ByteRange r[kMaxWrites]; };
+constexpr int kMaxWrites = 8;
+struct LaunchWrites { int n; ByteRange r[kMaxWrites]; uint64_t delay_ns; };
 std::mutex g_pdl_mu;
 std::map<std::pair<int, uintptr_t>, LaunchWrites> g_last_pdl;
 bool overlaps(const ByteRange& a, const ByteRange& b) { return a.lo < a.hi && b.lo < b.hi && a.lo < b.hi && b.lo < a.hi; }
@@ -92,23 +92,38 @@ LaunchOrderGuard::LaunchOrderGuard() { g_pdl_mu.lock(); }
 LaunchOrderGuard::~LaunchOrderGuard() { g_pdl_mu.unlock(); }
 
 bool claim_early_reads(cudaStream_t stream, const ByteRange* reads, int nreads, const ByteRange* writes,
-                       int nwrites) {
+                       int nwrites, uint64_t* prev_delay_ns, uint64_t delay_ns, bool merge) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
         cudaGetLastError();
         dev = -1;
     }
-    LaunchWrites w;
-    w.n = nwrites < kMaxWrites ? nwrites : kMaxWrites;
-    for (int i = 0; i < w.n; ++i) w.r[i] = writes[i];
-    bool early = nwrites <= kMaxWrites;
     const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
     auto it = g_last_pdl.find(key);
-    if (it != g_last_pdl.end())
-        for (int i = 0; i < it->second.n; ++i)
+    const LaunchWrites* prev = it != g_last_pdl.end() ? &it->second : nullptr;
+    bool early = true;
+    if (prev)
+        for (int i = 0; i < prev->n; ++i)
             for (int j = 0; j < nreads; ++j)
-                if (overlaps(it->second.r[i], reads[j])) early = false;
-    if (nwrites > kMaxWrites) {
+                if (overlaps(prev->r[i], reads[j])) early = false;
+    const uint64_t pd = prev ? prev->delay_ns : 0;
+    if (prev_delay_ns) *prev_delay_ns = pd;
+    else if (pd) early = false;
+    LaunchWrites w{};
+    bool known = true;
+    auto add = [&](const ByteRange& r) {
+        if (r.lo >= r.hi) return;
+        if (w.n == kMaxWrites) known = false;
+        else w.r[w.n++] = r;
+    };
+    for (int i = 0; i < nwrites; ++i) add(writes[i]);
+    w.delay_ns = delay_ns;
+    if (merge && prev) {
+        for (int i = 0; i < prev->n; ++i) add(prev->r[i]);
+        w.delay_ns = delay_ns + pd < delay_ns ? ~uint64_t(0) : delay_ns + pd;
+    }
+    if (!known) {
+        early = false;
         w.n = 1;                                    // unknown writes: everything overlaps the next reads
         w.r[0] = ByteRange{0, ~uintptr_t(0)};
     }

@@ -119,3 +119,55 @@ def test_cp_combine_wait_runs_out_and_reports():
     finally:
         torch.cuda.synchronize()
         bufs.free()
+
+
+def test_cp_steps_back_to_back():
+    """Single-rank context-parallel steps (decode + combine) with nothing in
+    between and no synchronisation.  The combine lets the next step's decode
+    start at once, so that decode may read ahead while this step's decode
+    and combine finish: steps with their own q and outputs, then a chain whose
+    combined output is the next step's q (those must wait), then a page
+    gather right after a combine.  Every result equals the same steps run one
+    at a time."""
+    from kessie_b200 import ops
+    B, Hq, Hkv, D, ps = 2, 16, 4, 128, 16
+    N = 5000
+    pages = (N + ps - 1) // ps
+    _, kv = make_paged(81, B * pages, ps, Hkv, D, "bf16")
+    bt = torch.from_numpy(np.random.default_rng(82).permutation(B * pages).astype(np.int32).reshape(B, pages)).cuda()
+    sl = torch.full((B,), N, dtype=torch.int32, device="cuda")
+    cs = torch.full((B,), N - 256, dtype=torch.int32, device="cuda")
+    qs = [to_dev(ROUND["bf16"](rnd(83 + i, (B, Hq, D))), "bf16") for i in range(2)]
+    ws = torch.empty(ops.decode_workspace_bytes(B, Hq, Hkv, D, pages * ps, ps), dtype=torch.uint8, device="cuda")
+    gid = torch.arange(8, dtype=torch.int32, device="cuda")
+    epoch = [0]
+
+    def run(sync):
+        bufs = _Buffers(1, B, Hq, Hkv, D)
+        try:
+            view = _View(bufs, 0, 1)
+            outs = [torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda") for _ in range(4)]
+            chain = [qs[0].clone()] + [torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+            gk = torch.empty(8 * ps, Hkv, D, dtype=torch.bfloat16, device="cuda")
+            gv = torch.empty_like(gk)
+            torch.cuda.synchronize()
+            steps = [(qs[j % 2], outs[j]) for j in range(4)] + [(chain[j], chain[j + 1]) for j in range(3)]
+            for i, (q, o) in enumerate(steps):
+                epoch[0] += 1
+                ops.paged_fog_decode_cp(view, epoch[0], q, kv[:, :, 0], kv[:, :, 1], bt, sl, clear_start=cs,
+                                        out=o, ws=ws, phases=3)
+                if i == 3:
+                    ops.page_gather(kv, gid, out_keys=gk, out_values=gv)
+                if sync:
+                    torch.cuda.synchronize()
+            torch.cuda.synchronize()
+            assert ops.read_device_status() == 0
+            return outs + chain[1:] + [gk, gv]
+        finally:
+            torch.cuda.synchronize()
+            bufs.free()
+
+    got, want = run(False), run(True)
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
+    assert torch.equal(got[0], got[2]) and not torch.equal(got[4], got[5])

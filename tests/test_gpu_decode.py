@@ -270,3 +270,46 @@ def test_decode_workspace_garbage_is_ignored():
     torch.cuda.synchronize()
     want = O.paged_fog_decode(q, kvn[:, :, 0], kvn[:, :, 1], bt_np, lens, cs, 0.5)
     np.testing.assert_allclose(to_np(out), want, **TOL["bf16"])
+
+
+def test_decode_back_to_back():
+    """Decodes enqueued with nothing in between and no synchronisation, as
+    the steps of a serving loop run them: each may load its pages and q
+    before the previous decode has finished when that decode wrote none of
+    those bytes.  Independent decodes over three caches in turn (twice), then
+    a chain whose output is the next step's q (those must wait); every result
+    equals the same launches run one at a time."""
+    from kessie_b200 import ops
+    B, Hq, Hkv, D, ps = 4, 16, 4, 128, 16
+    lens = np.array([3000, 1777, 4096, 2500])
+    P = int(sum((n + ps - 1) // ps for n in lens)) + 2
+    caches = [make_paged(90 + i, P, ps, Hkv, D, "bf16")[1] for i in range(3)]
+    bt = torch.from_numpy(random_block_table(93, lens, ps, P)).cuda()
+    sl = torch.from_numpy(lens.astype(np.int32)).cuda()
+    cs = torch.from_numpy((lens - 64).astype(np.int32)).cuda()
+    qs = [to_dev(ROUND["bf16"](rnd(94 + i, (B, Hq, D))), "bf16") for i in range(3)]
+    ws = torch.empty(ops.decode_workspace_bytes(B, Hq, Hkv, D, bt.shape[1] * ps, ps), dtype=torch.uint8,
+                     device="cuda")
+
+    def run(sync):
+        outs = [torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda") for _ in range(6)]
+        chain = [qs[0].clone()] + [torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda") for _ in range(4)]
+        torch.cuda.synchronize()
+        for j in range(6):
+            c = caches[j % 3]
+            ops.paged_fog_decode(qs[j % 3], c[:, :, 0], c[:, :, 1], bt, sl, clear_start=cs, ws=ws, out=outs[j])
+            if sync:
+                torch.cuda.synchronize()
+        for j in range(4):
+            c = caches[j % 3]
+            ops.paged_fog_decode(chain[j], c[:, :, 0], c[:, :, 1], bt, sl, clear_start=cs, ws=ws, out=chain[j + 1])
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return outs + chain[1:]
+
+    got, want = run(False), run(True)
+    assert ops.read_device_status() == 0
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
+    assert torch.equal(got[0], got[3]) and not torch.equal(got[6], got[7])
