@@ -376,8 +376,11 @@ def run_cp_decode(args):
     # An event between two launches would stop the next one from starting
     # while the previous one finishes (each decode may read its pages ahead of
     # the previous step's tail; at N > 1 the combine is a programmatic
-    # dependent of the decode), so the timed loop has none, and the decode is
-    # timed alone in a loop of the same step right after it.
+    # dependent of the decode), so the timed loop has none.  At N = 1 a step
+    # is one decode launch, so the decode's duration per launch is the timed
+    # loop's own (events around the region, launches overlapping as they do
+    # in service).  At N > 1 the decode is timed alone in a loop of the same
+    # step right after the timed region.
     torch.cuda.synchronize()
     t_start.record()
     for i in range(K):
@@ -386,17 +389,19 @@ def run_cp_decode(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    Kk = max(10, K // 2)
-    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
-    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
-    for i in range(Kk):
-        step_split(ev_a, ev_b, i)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    kern_ms = sum(ev_a[i].elapsed_time(ev_b[i]) for i in range(Kk)) / Kk
-    clocks.stop()
     el_ms = t_start.elapsed_time(t_end)
+    if world == 1:
+        kern_ms = el_ms / K
+    else:
+        Kk = max(10, K // 2)
+        ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
+        ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(Kk)]
+        for i in range(Kk):
+            step_split(ev_a, ev_b, i)
+        torch.cuda.synchronize()
+        dist.barrier()
+        kern_ms = sum(ev_a[i].elapsed_time(ev_b[i]) for i in range(Kk)) / Kk
+    clocks.stop()
     t = torch.tensor([el_ms, kern_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -456,8 +461,8 @@ def run_cp_decode(args):
                 "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "peak_source": f"{peak_src} hbm_gbs (copy, burst)",
                 "algorithmic_bytes_per_launch": local_bytes, "kernel_ms": round(kern_ms, 4),
-                "kernel_timing": ("CUDA events at every step boundary of the timed loop (N=1: a step is one "
-                                  "decode launch)" if world == 1 else
+                "kernel_timing": ("CUDA events around the timed loop / K (N=1: a step is one decode launch; "
+                                  "consecutive launches overlap as programmatic dependents)" if world == 1 else
                                   "CUDA events around each decode launch (max over ranks), in a loop of the same "
                                   "step right after the timed region"),
                 "traffic": (int(tr * local_bytes) if tr else None)}
