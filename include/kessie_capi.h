@@ -77,6 +77,33 @@ const char* kessie_version(void);
  * OR of KESSIE_DEV_* bits) and clears it.  Returns <0 on a CUDA error. */
 int kessie_read_device_status(void* stream);
 
+/* The library's registry of programmatic launches, open to callers that
+ * launch their own programmatic dependents (griddepcontrol) on a stream that
+ * this library also launches on.  The library's f16/bf16 decodes, page
+ * gathers, RoPE remaps, fused inserts and tiered updates are programmatic
+ * dependent launches that may read their inputs before their
+ * griddepcontrol.wait when the previous programmatic launch on the same
+ * (device, stream) wrote none of them; the registry keeps that launch's
+ * written byte ranges.  A caller that launches such a kernel of its own
+ * records it here just before the launch:
+ *   writes: nwrites [lo, hi) byte-address pairs (2 * nwrites values); more
+ *     than 8 non-empty ranges record "everything" (and that claim gets 0);
+ *   *may_read_early = 1 when none of the previous record's ranges overlaps
+ *     the nreads pairs in `reads` (the new launch may read them before its
+ *     wait), else 0;
+ *   merge = 1 and delay_ns: for a launch that signals its dependents before
+ *     its own griddepcontrol.wait -- its record keeps the previous record's
+ *     ranges (that launch may still run when the next one starts), and
+ *     delay_ns bounds how long its dependents can then sit in
+ *     griddepcontrol.wait;
+ *   prev_delay_ns (nullable) receives the previous record's bound; when it
+ *     is NULL a non-zero bound gives *may_read_early = 0.
+ * Issue the launch before any other claim on the same stream.  Returns
+ * KESSIE_OK or KESSIE_ERR_ARG. */
+int kessie_launch_registry_claim(void* stream, const uint64_t* reads, int nreads, const uint64_t* writes,
+                                 int nwrites, uint64_t delay_ns, int merge, uint64_t* prev_delay_ns,
+                                 int* may_read_early);
+
 /* ------------------------------------------------------------------------- */
 /* Legacy launchers -- identical argument lists to the reference             */
 /* ------------------------------------------------------------------------- */

@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
-from ctypes import c_double, c_float, c_int, c_int64, c_size_t, c_void_p, c_char_p, POINTER, c_uint32
+from ctypes import c_double, c_float, c_int, c_int64, c_size_t, c_void_p, c_char_p, POINTER, c_uint32, c_uint64
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 DEFAULT_PATHS = [
@@ -46,6 +46,7 @@ SIGNATURES = {
     "kessie_get_last_error": (c_int, [c_char_p, c_int]),
     "kessie_version": (c_char_p, []),
     "kessie_read_device_status": (c_int, [P]),
+    "kessie_launch_registry_claim": (c_int, [P, P, c_int, P, c_int, c_uint64, c_int, P, P]),
     # legacy (kessie_kernels_v2.hip:714-844)
     "launch_kessie_windowed_attn": (None, [P, P, P, P, c_float, c_int, c_int, c_int, c_int, c_int, c_int, P]),
     "launch_kessie_fused_fog_attn": (None, [P, P, P, P, P, c_float, c_int, c_int, c_int, c_int, c_int, c_int, P]),

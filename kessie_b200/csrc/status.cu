@@ -8,6 +8,7 @@
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 namespace {
 
@@ -142,6 +143,23 @@ extern "C" int kessie_get_last_error(char* buf, int len) {
 }
 
 extern "C" const char* kessie_version(void) { return "kessie_b200 0.1 sm_100a"; }
+
+extern "C" int kessie_launch_registry_claim(void* stream, const uint64_t* reads, int nreads, const uint64_t* writes,
+                                            int nwrites, uint64_t delay_ns, int merge, uint64_t* prev_delay_ns,
+                                            int* may_read_early) {
+    using namespace kessie;
+    if (!may_read_early || nreads < 0 || nwrites < 0 || nreads > 4096 || nwrites > 4096 || (nreads && !reads) ||
+        (nwrites && !writes))
+        return set_error(KESSIE_ERR_ARG, "launch_registry_claim: bad range arrays");
+    std::vector<ByteRange> r((size_t)nreads), w((size_t)nwrites);
+    for (int i = 0; i < nreads; ++i) r[i] = ByteRange{(uintptr_t)reads[2 * i], (uintptr_t)reads[2 * i + 1]};
+    for (int i = 0; i < nwrites; ++i) w[i] = ByteRange{(uintptr_t)writes[2 * i], (uintptr_t)writes[2 * i + 1]};
+    LaunchOrderGuard order;
+    *may_read_early = claim_early_reads(as_stream(stream), r.data(), nreads, w.data(), nwrites, prev_delay_ns,
+                                        delay_ns, merge != 0) ? 1 : 0;
+    clear_error();
+    return KESSIE_OK;
+}
 
 extern "C" int kessie_read_device_status(void* stream) {
     int* p = kessie::device_status_ptr();
