@@ -235,6 +235,20 @@ def cpu_decode_sample(seconds=10.0, tokens=131072, max_seconds=30.0, seed=0):
                       f"(oracle.fog_decode_group_fp32), {reps} reps in {el:.1f} s; GB/s of bf16-equivalent KV")
 
 
+def _host_cpu():
+    """The host's CPU model and thread count, for the CPU baselines."""
+    model = "unknown CPU"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return f"{model}, {os.cpu_count() or 1} threads"
+
+
 def _cpu_rate(fn, seconds=1.0):
     """Mean wall time of fn on the host over about `seconds`, and the BLAS
     thread count it ran with."""
@@ -286,7 +300,8 @@ def reference_arm(args):
             "dtype": "f32", "data": "synthetic (seeded N(0,1) q/k/v)",
             "config": {"workload": "cp_decode_1m (BASELINE config 5)", **c, "parallelism": "host cores",
                        "sample_tokens_per_step": tokens, "sample_kv_heads_per_step": 1},
-            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
+                             "host": _host_cpu()},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -470,7 +485,7 @@ def run_cp_decode(args):
         if world == 1 and not args.no_cpu_baseline:
             gbs, per, sample = cpu_decode_sample()
             cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
-                   "sample": sample}
+                   "sample": sample, "host": _host_cpu()}
         line = {"metric": METRIC,
                 "value": round(total_bytes / (ms_step / 1e3) / 1e9, 3), "unit": "GB/s", "n_gpus": world,
                 "steps": K, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4),
