@@ -256,8 +256,8 @@ int kessie_build_fog_weights_v2(float* out, int seq_len, int clear_start, float 
  * workspace: kessie_paged_fog_decode_workspace_size(...) bytes.
  * f16 / bf16 decodes are programmatic dependent launches: when the last such
  * launch of this library on the same (device, stream) wrote none of q, the
- * caches, the block table or the length arrays (and no fog weights or bias
- * are passed), the q and page loads may start before the previous kernel on
+ * caches, the block table, the length arrays or a bias's recall bitmap (and
+ * no fog_weights array is passed), the q and page loads may start before the previous kernel on
  * the stream completes; everything is written only after it completes.  A
  * kernel that writes those inputs must not be launched with a programmatic
  * dependency that triggers before its writes. */

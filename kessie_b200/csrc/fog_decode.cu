@@ -1097,7 +1097,8 @@ int run_decode(const DecodeParams& p, const void* k_cache, const void* v_cache, 
     if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
         return set_error(KESSIE_ERR_ARG, "paged_fog_decode_v2: TMA descriptor rejected (%d/%d)", (int)r1, (int)r2);
     // Early reads when the preceding programmatic launches on the stream wrote
-    // none of the inputs (fog weights or a bias: extents unknown here, no).
+    // none of the inputs (with fog weights, whose extent the host does not
+    // know, no).
     // After a launch that signals before its own wait (the context-parallel
     // combine) the preceding grid can run for up to its delay bound while
     // this one's warps wait in griddepcontrol.wait: the mbarrier waits get
@@ -1110,10 +1111,11 @@ int run_decode(const DecodeParams& p, const void* k_cache, const void* v_cache, 
                              (int64_t)(p.Hkv - 1) * head_stride + head_dim;
         const int64_t q_e = (int64_t)(p.B - 1) * p.q_sb + (int64_t)(p.Hq - 1) * p.q_sh + head_dim;
         const int64_t nb = (int64_t)p.B * 4;
-        const ByteRange reads[8] = {byte_span(p.q, q_e * 2), byte_span(k_cache, kv_e * 2), byte_span(v_cache, kv_e * 2),
+        const int64_t recall_bytes = p.bias.on && p.bias.recall ? ((int64_t)p.bias.recall_nbits + 31) / 32 * 4 : 0;
+        const ByteRange reads[9] = {byte_span(p.q, q_e * 2), byte_span(k_cache, kv_e * 2), byte_span(v_cache, kv_e * 2),
                                     byte_span(p.block_table, (int64_t)p.B * p.bt_stride * 4),
                                     byte_span(p.seq_lens, nb), byte_span(p.kv_off, nb), byte_span(p.q_pos, nb),
-                                    byte_span(p.clear_start, nb)};
+                                    byte_span(p.clear_start, nb), byte_span(p.bias.recall, recall_bytes)};
         const CpLayout lay{p.cp.world, p.B * p.Hq, head_dim};
         const ByteRange writes[4] = {byte_span(p.out, (int64_t)p.B * p.Hq * head_dim * 2),
                                      byte_span(p.out_part, (int64_t)p.B * p.Hq * (head_dim + 2) * 4),
@@ -1121,8 +1123,8 @@ int run_decode(const DecodeParams& p, const void* k_cache, const void* v_cache, 
                                      byte_span(p.cp.world > 0 ? p.cp.peer[p.cp.rank] : nullptr, (int64_t)lay.bytes())};
         const bool fwd = page_stride >= 0 && token_stride >= 0 && head_stride >= 0 && p.q_sb >= 0 && p.q_sh >= 0;
         uint64_t prev_delay = 0;
-        const bool ok = claim_early_reads(st, reads, 8, writes, 4, &prev_delay);
-        pe.early = ok && fwd && !p.fog_w && !p.bias.on ? 1 : 0;
+        const bool ok = claim_early_reads(st, reads, 9, writes, 4, &prev_delay);
+        pe.early = ok && fwd && !p.fog_w ? 1 : 0;
         if (pe.early) pe.spin_ns = kSpinNs + prev_delay < kSpinNs ? ~uint64_t(0) : kSpinNs + prev_delay;
     }
     const bool nt2 = p.G > 8;

@@ -98,3 +98,46 @@ def test_prefill_with_bias_matches_oracle(dt, D, staged):
         want = O.paged_fog_prefill(np.transpose(q[b], (1, 0, 2)), kvn[:, :, 0], kvn[:, :, 1], bt[b], lens[b],
                                    lens[b] - T, 0, 0.0, bias_spec=spec)
         np.testing.assert_allclose(got[b], np.transpose(want, (1, 0, 2)), **TOL[dt])
+
+
+def test_biased_decode_back_to_back():
+    """Biased decodes (the vLLM path) enqueued with nothing in between and no
+    synchronisation: each may read q, its pages and the recall bitmap before
+    the previous decode finishes, when that decode wrote none of them.
+    Independent steps, then a chain whose output is the next step's q (those
+    must wait); every result equals the same launches run one at a time, and
+    the first matches the oracle."""
+    from kessie_b200 import ops
+    B, Hq, Hkv, D, ps = 3, 16, 4, 128, 16
+    lens = np.array([2000, 3333, 1500])
+    P = int(sum((n + ps - 1) // ps for n in lens)) + 2
+    kvn, kv = make_paged(61, P, ps, Hkv, D, "bf16")
+    btn = random_block_table(62, lens, ps, P)
+    bt = torch.from_numpy(btn).cuda()
+    sl = torch.from_numpy(lens.astype(np.int32)).cuda()
+    qn = [ROUND["bf16"](rnd(63 + i, (B, Hq, D))) for i in range(2)]
+    qs = [to_dev(x, "bf16") for x in qn]
+    spec = (0.5, 0.5, [7, 900, 2500], 0.25)
+    bias = ops.FogBias(*spec, dtype=torch.bfloat16)
+    ws = torch.empty(ops.decode_workspace_bytes(B, Hq, Hkv, D, bt.shape[1] * ps, ps), dtype=torch.uint8,
+                     device="cuda")
+
+    def run(sync):
+        outs = [torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda") for _ in range(4)]
+        chain = [qs[0].clone()] + [torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+        torch.cuda.synchronize()
+        steps = [(qs[j % 2], outs[j]) for j in range(4)] + [(chain[j], chain[j + 1]) for j in range(3)]
+        for q, o in steps:
+            ops.paged_fog_decode(q, kv[:, :, 0], kv[:, :, 1], bt, sl, fog_alpha=0.0, bias=bias, ws=ws, out=o)
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return outs + chain[1:]
+
+    got, want = run(False), run(True)
+    assert ops.read_device_status() == 0
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
+    ref = O.paged_fog_decode(qn[0], kvn[:, :, 0], kvn[:, :, 1], btn, lens, np.zeros(B, np.int32), 0.0, 0,
+                             bias_spec=spec + ("bfloat16",))
+    np.testing.assert_allclose(to_np(got[0]), ref, **TOL["bf16"])
