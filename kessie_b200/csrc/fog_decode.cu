@@ -1010,8 +1010,8 @@ int launch_decode_t(const CUtensorMap& mk, const CUtensorMap& mv, const DecodePa
 // The combine follows the decode kernel with programmatic stream
 // serialization: it may start while the decode's last CTAs still merge and
 // push (every decode CTA signals launch_dependents at its last segment).  It
-// reads nothing of the decode's except through the release/acquire flags, so
-// it does not wait for the decode grid to complete.
+// reads the decode's results only as epoch-tagged words of this rank's
+// exchange buffer, so one thread of it waits for the decode grid, at its end.
 template <int D, bool BF16>
 int launch_cp_combine_t(const CpCombineParams& a, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
