@@ -16,7 +16,8 @@
 //   grid  = (S splits, B*Hkv groups); the visible keys of a group are cut into
 //           8-key chunks (a chunk never crosses a page: page_size % 16 == 0)
 //           and split S ways; S is chosen from the SM count so the grid's
-//           last wave is nearly full, with at least two chunks per warp.
+//           last wave is nearly full (one wave when one fills nearly as
+//           well), with at least two chunks per warp.
 //   CTA   = 8 warps.  Each warp streams every 8th chunk of the CTA's range
 //           through its own 3-stage ring: per chunk two TMA box loads (K, V;
 //           8 keys x D of one head, 4 KB each at D 128) on the stage's
@@ -653,6 +654,12 @@ int launch_decode_f32(const DecodeF32Args& a, cudaStream_t st) {
     double best = fill(S);
     for (int s = S + 1; s <= min(s_max, 8 * S) && best < 0.97; ++s)
         if (fill(s) > best + 1e-9) { best = fill(s); S = s; }
+    // a single wave that fills nearly as well wins: each CTA pays its ramp
+    // (q, page ids, the first ring fill) and its merge once per SM instead of
+    // once per wave (2 sequences at the config-3 shape: 16 groups x 9 splits
+    // in one wave 344.7 us against 16 x 18 in two 355.1 us)
+    const int s1 = min(s_max, sms / groups);
+    if (s1 >= 1 && s1 < S && fill(s1) >= best - 0.03) S = s1;
     // K/V tiles by TMA boxes: pages (a multiple of 8 tokens) through a 5-D
     // map, a dense cache through a 4-D map that zero-fills past its end
     if (a.square_n <= 0 && a.page_size % 8)
