@@ -71,6 +71,7 @@ namespace {
 
 constexpr int kNCW = 4;          // consumer warps
 constexpr uint64_t kSpinNs = 2000000000ull;   // bound of an mbarrier wait with nothing ahead of it
+constexpr uint64_t kSpinMaxNs = 32000000000ull; // cap when a preceding combine's delay is added
 constexpr int kNST = 3;          // pipeline stages
 constexpr int kIdWin = 128;      // page ids per prefetch window (units)
 constexpr int kHelperWarp = kNCW + 1;  // finishes mid-range segment ends for the consumers
@@ -1125,7 +1126,7 @@ int run_decode(const DecodeParams& p, const void* k_cache, const void* v_cache, 
         uint64_t prev_delay = 0;
         const bool ok = claim_early_reads(st, reads, 9, writes, 4, &prev_delay);
         pe.early = ok && fwd && !p.fog_w ? 1 : 0;
-        if (pe.early) pe.spin_ns = kSpinNs + prev_delay < kSpinNs ? ~uint64_t(0) : kSpinNs + prev_delay;
+        if (pe.early) pe.spin_ns = prev_delay < kSpinMaxNs - kSpinNs ? kSpinNs + prev_delay : kSpinMaxNs;
     }
     const bool nt2 = p.G > 8;
     if (head_dim == 128) {
