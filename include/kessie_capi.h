@@ -77,7 +77,8 @@ const char* kessie_version(void);
  * OR of KESSIE_DEV_* bits) and clears it.  Returns <0 on a CUDA error. */
 int kessie_read_device_status(void* stream);
 
-/* The library's registry of programmatic launches, open to callers that
+/* No reference counterpart (the reference launches nothing programmatically).
+ * The library's registry of programmatic launches, open to callers that
  * launch their own programmatic dependents (griddepcontrol) on a stream that
  * this library also launches on.  The library's f16/bf16 decodes, page
  * gathers, RoPE remaps, fused inserts and tiered updates are programmatic
