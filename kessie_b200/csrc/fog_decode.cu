@@ -53,6 +53,12 @@
 //           every rank's words of a row carry the step's epoch, then merges
 //           the world shard results.  One decode kernel and one small combine
 //           per step, no collective library call.
+//   launch = programmatic dependent launches (cudaLaunchKernelEx).  When the
+//           launch registry shows that the preceding programmatic launch on
+//           the stream wrote none of q, the cache, the tables, the lengths or
+//           the bias bitmap, everything up to a CTA's first global store runs
+//           before griddepcontrol.wait, so a step's ramp overlaps the previous
+//           step's tail; the combine lets the next step start at its own start.
 #include "common.cuh"
 #include "cp_layout.cuh"
 #include "decode_f32.cuh"
